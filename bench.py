@@ -1,0 +1,325 @@
+"""Benchmark: batch-1 Qwen3-0.6B bf16 greedy decode on B200 (BASELINE.json `metric`).
+
+Workload (the configuration the reference's headline tok/s is quoted on,
+metal_infrence_engine/README.md:15-24): the Qwen3-0.6B geometry with seeded random-init bf16
+weights, a 130-id seeded prompt fed token by token, then 128 greedy decode steps at positions
+130..257, batch 1, f32 KV cache. One bench STEP = one 128-token greedy decode from the prefilled
+cache (one launch of the persistent decode kernel). `--config long` selects configs[1] instead
+(2048-id prompt, 512 decode steps at positions 2048..2559).
+
+Printed JSON (one line, rank 0):
+  value        decode tok/s over all ranks: 128 x steps x N / (max over ranks of the device time of
+               the timed steps), tokens and logits resident in HBM (qw_decode_device)
+  e2e          the same metric through the public host API qw_decode (host first token in, every
+               token streamed back to the host callback), timed with CUDA events on the model's
+               stream around each call
+  roofline     the decode kernel against the measured HBM copy bandwidth (MEASURED_PEAKS.json):
+               achieved = the reference's bytes-per-token rule (tests/mbu.rs:151-167: all weights
+               but the embedding table + one embedding row + f32 K/V of positions 0..pos) summed
+               over the 128 positions of a launch / average launch time (CUDA events)
+  cpu_baseline the CPU oracle (C++ restatement of cpu_inference.rs, all host threads) on a bounded
+               sample of the same decode positions
+Multi-GPU (torchrun): every rank holds a weight replica and decodes its own independent sequence
+(prompt seed 1 + rank); no collective touches the decode path (weak scaling).
+`--impl reference` times the reference's CPU engine (its C++ restatement; the Rust original cannot
+be built here) on the same config, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "mac-gpu-compiler_b200"))
+
+import randmodel  # noqa: E402
+
+CONFIGS = {
+    "ai130": dict(prompt=130, decode=128, label="configs[0]: 130-id prompt token-by-token, then 128 greedy decode steps (pos 130..257)"),
+    "long": dict(prompt=2048, decode=512, label="configs[1]: 2048-id prompt token-by-token, then 512 greedy decode steps (pos 2048..2559)"),
+}
+# reference's published decode tok/s for this metric and config: Metal engine, f32 KV cache, Apple M1
+# (metal_infrence_engine/README.md:22)
+PUBLISHED_TPS = 46.37
+# DRAM bytes per decode token of the decode kernel, from an ncu capture (see profiles/); None until measured
+NCU_DRAM_BYTES_PER_TOKEN = None
+
+
+def kv_bytes_at(cfg, pos: int) -> int:
+    """tests/mbu.rs:162-167 — f32 K and V for every cached position (0..=pos) in every layer."""
+    return 2 * cfg.num_hidden_layers * (pos + 1) * cfg.num_key_value_heads * cfg.head_dim * 4
+
+
+def load_peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except (ValueError, KeyError):
+            pass
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+        return False
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def cpu_sample(path, cfg_name: str, budget_s: float = 12.0) -> dict:
+    """Times the CPU oracle on decode positions of the workload: the cache is pre-filled with
+    synthetic K/V for the prompt positions (untimed), then decode tokens are timed."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import cpu_oracle as co
+    c = CONFIGS[cfg_name]
+    m = co.Model.load_model(path)
+    cache = co.KVCache(m)
+    cache.fill_synthetic(c["prompt"], seed=0)
+    tok, pos = 1, c["prompt"]
+    t0 = time.perf_counter()
+    m.forward(tok, pos, cache)   # warm-up token (pages in the mmap)
+    first = time.perf_counter() - t0
+    n = max(2, min(c["decode"], int(budget_s / max(first, 1e-3))))
+    t0 = time.perf_counter()
+    for i in range(n):
+        lg = m.forward(tok, pos + 1 + i, cache)
+        tok = co.argmax(lg)
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": "tok/s", "cores": co.threads(), "kind": "port",
+            "sample": f"{n} greedy decode tokens at positions {pos + 1}..{pos + n} after a synthetic "
+                      f"{c['prompt'] + 1}-position K/V cache, {co.threads()} host threads"}
+
+
+def run_reference(args, cfg_name: str) -> None:
+    world, rank, _ = dist_setup()
+    if rank != 0:
+        return
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import cpu_oracle as co
+    c = CONFIGS[cfg_name]
+    path = randmodel.make_model("qwen3-0.6b", 0)
+    m = co.Model.load_model(path)
+    cache = co.KVCache(m)
+    cache.fill_synthetic(c["prompt"], seed=0)
+    per_step = 2   # decode tokens per bench step: keeps the whole run within a few minutes
+    pos, tok = c["prompt"], 1
+    for _ in range(args.warmup):
+        for _ in range(per_step):
+            tok = co.argmax(m.forward(tok, pos, cache))
+            pos += 1
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        for _ in range(per_step):
+            tok = co.argmax(m.forward(tok, pos, cache))
+            pos += 1
+    dt = time.perf_counter() - t0
+    v = per_step * args.steps / dt
+    sample = (f"{per_step} greedy decode tokens per step at positions {c['prompt']}..{pos - 1} after a "
+              f"synthetic {c['prompt']}-position K/V cache, {co.threads()} host threads")
+    print(json.dumps({
+        "impl": "reference", "metric": "Qwen3-0.6B bf16 decode tok/s @bs1", "value": v, "unit": "tok/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": c["label"], "model": "Qwen3-0.6B geometry, random-init bf16 (seed 0)",
+                   "engine": "CPU oracle: C++ restatement of metal_infrence_engine/src/cpu_inference.rs "
+                             "(the Rust original needs cargo, absent on these machines)"},
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": co.threads(), "kind": "port", "sample": sample},
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="ai130", choices=sorted(CONFIGS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args, args.config)
+        return
+
+    import numpy as np
+    import torch
+    import cuda_inference as ci
+
+    world, rank, local = dist_setup()
+    if world != args.gpus and world > 1:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+
+    c = CONFIGS[args.config]
+    n_prompt, n_dec = c["prompt"], c["decode"]
+    path = randmodel.make_model("qwen3-0.6b", 0)
+    model = ci.CudaModel.load_model(path, device=local)
+    cfg = model.config
+    cache = ci.CudaKVCache(model, n_prompt + n_dec + 1)
+    ids = randmodel.prompt_ids(n_prompt, cfg.vocab_size, seed=1 + rank)
+    logits = None
+    for pos, tok in enumerate(ids):              # token-by-token prefill (untimed)
+        logits = model.forward(tok, pos, cache)
+    first = int(np.argmax(logits))
+    stream = torch.cuda.ExternalStream(model.stream)
+    toks = torch.zeros(n_dec + 1, dtype=torch.int32, device=f"cuda:{local}")
+    toks[0] = first
+    torch.cuda.synchronize()
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+
+    def step():
+        model.decode_device(cache, toks.data_ptr(), n_prompt, n_dec, stream=model.stream)
+
+    for _ in range(args.warmup):
+        step()
+    model.sync()
+    barrier()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        t_start.record(stream)
+        for i in range(args.steps):
+            evs[i][0].record(stream)
+            step()
+            evs[i][1].record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    model.sync()
+    elapsed = t_start.elapsed_time(t_end) / 1e3
+    launch_ms = [a.elapsed_time(b) for a, b in evs]
+    barrier()
+    # max over ranks
+    el = torch.tensor([elapsed], dtype=torch.float64, device=f"cuda:{local}")
+    if pg is not None:
+        pg.all_reduce(el, op=pg.ReduceOp.MAX)
+    elapsed_max = float(el.item())
+
+    # decode tokens must match the prefix invariant: the first decoded token is deterministic
+    out_tokens = toks.cpu().tolist()
+
+    # e2e through the public host API (qw_decode: host first token in, tokens streamed to host)
+    e2e_times = []
+    for i in range(max(2, min(args.steps, 5)) + 1):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        got = model.decode(first, n_prompt, n_dec, cache)
+        b.record(stream)
+        torch.cuda.synchronize()
+        if i > 0:
+            e2e_times.append(a.elapsed_time(b) / 1e3)
+        assert got == out_tokens[1:], "host-API decode disagrees with the device-resident decode"
+    e2e_t = torch.tensor([statistics.mean(e2e_times)], dtype=torch.float64, device=f"cuda:{local}")
+    if pg is not None:
+        pg.all_reduce(e2e_t, op=pg.ReduceOp.MAX)
+
+    if rank == 0:
+        W = model.weight_bytes_per_token()
+        bytes_launch = sum(W + kv_bytes_at(cfg, pos) for pos in range(n_prompt, n_prompt + n_dec))
+        avg_launch = statistics.mean(launch_ms) / 1e3
+        achieved = bytes_launch / avg_launch / 1e9
+        peak, peak_kind = load_peaks()
+        value = n_dec * args.steps * world / elapsed_max
+        traffic = None if NCU_DRAM_BYTES_PER_TOKEN is None else NCU_DRAM_BYTES_PER_TOKEN * n_dec
+        line = {
+            "metric": "Qwen3-0.6B bf16 decode tok/s @bs1 & % of HBM roofline; box tok/s at 1-8 GPUs",
+            "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": elapsed_max / args.steps * 1e3, "ms_per_token": elapsed_max / args.steps / n_dec * 1e3,
+            "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": value / PUBLISHED_TPS if args.config == "ai130" else None,
+            "vs_baseline_ref": "reference Metal engine, f32 KV, Apple M1: 46.37 tok/s (README.md:22)",
+            "dtype": "bf16", "accumulate": "f32", "data": "synthetic",
+            "config": {"workload": c["label"], "model": "Qwen3-0.6B geometry, random-init bf16 (seed 0)",
+                       "global_batch": world, "seq_len": n_prompt + n_dec,
+                       "parallelism": f"replicas x{world}, one independent sequence per GPU, no collective",
+                       "l2": "inputs larger than L2: 1.19 GB of weights streamed per token",
+                       "step": f"one {n_dec}-token greedy decode = one decode-kernel launch"},
+            "e2e": {"value": n_dec * world / float(e2e_t.item()), "unit": "tok/s", "h2d_bytes_per_step": 4,
+                    "d2h_bytes_per_step": 4 * n_dec, "api": "qw_decode (host callback per token)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": f"{peak_kind} (hbm_gbs, copy)", "traffic": traffic,
+                         "algorithmic_bytes_per_launch": bytes_launch,
+                         "kernel": "qw::decode_kernel", "avg_launch_ms": avg_launch * 1e3},
+            "gpu_launches": args.steps,
+            "clocks": clocks.summary(),
+            "first_tokens": out_tokens[1:9],
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_sample(path, args.config)
+        print(json.dumps(line), flush=True)
+    model.close()
+    if pg is not None:
+        pg.barrier()
+        pg.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,138 @@
+/*
+ * cuda_inference.h — C ABI of the B200 (sm_100a) batch-1 Qwen3 decode engine.
+ *
+ * It is the surface of the reference's GPU engine, metal_infrence_engine/src/metal_inference.rs,
+ * re-expressed as plain C so that a thin `cuda_inference.rs` (or ctypes/cffi) can bind it and drop
+ * it in beside the reference CPU engine, metal_infrence_engine/src/cpu_inference.rs. Each
+ * declaration names the reference item it replaces (path:line inside metal_infrence_engine/).
+ *
+ * Conventions (where the reference panics, these return a status code):
+ *   - every int-returning call returns QW_OK (0) or a QW_ERR_* code; qw_last_error() gives the
+ *     message of the calling thread's most recent failure;
+ *   - the caller owns handles and frees them with the matching *_free;
+ *   - a model is bound to one CUDA device and owns one stream; calls on one handle are not
+ *     thread-safe; different handles (one per device) may be driven from different threads;
+ *   - host pointers are plain host memory; `d_` pointers are device memory on the model's device;
+ *     `stream` is a cudaStream_t (NULL = the model's own stream).
+ */
+#ifndef CUDA_INFERENCE_H
+#define CUDA_INFERENCE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    QW_OK = 0,
+    QW_ERR_IO = 1,             /* file missing / unreadable (reference: io::Error from load_model) */
+    QW_ERR_FORMAT = 2,         /* malformed safetensors/config, missing tensor, wrong shape */
+    QW_ERR_UNSUPPORTED = 3,    /* non-BF16 tensor, geometry the kernels do not support */
+    QW_ERR_ARG = 4,            /* bad argument: token >= vocab, pos >= max_seq, NULL handle */
+    QW_ERR_CUDA = 5,           /* CUDA runtime error (no device, launch failure, ...) */
+    QW_ERR_DEVICE_TIMEOUT = 6, /* a bounded device-side wait expired; the kernel stopped cleanly */
+    QW_ERR_NOMEM = 7           /* device or pinned host allocation failed */
+};
+
+typedef struct qw_model qw_model;
+typedef struct qw_cache qw_cache;
+
+/* cpu_inference.rs:21-33 Config (the ten config.json fields the reference reads) */
+typedef struct qw_config {
+    uint64_t hidden_size;
+    uint64_t intermediate_size;
+    uint64_t num_hidden_layers;
+    uint64_t num_attention_heads;
+    uint64_t num_key_value_heads;
+    uint64_t head_dim;
+    uint64_t vocab_size;
+    float rms_norm_eps;
+    float rope_theta;
+    uint32_t eos_token_id;
+} qw_config;
+
+/* message of this thread's most recent failure ("" if none) */
+const char* qw_last_error(void);
+
+/* Parse and validate `safetensors_path` and the config.json beside it without touching a GPU.
+ * Replaces the parsing half of Model::load_model (cpu_inference.rs:58-84). */
+int qw_inspect(const char* safetensors_path, qw_config* out);
+
+/* MetalModel::load_model (metal_inference.rs:157-168): parse, validate, upload (repacked) to
+ * `device`. */
+int qw_load(const char* safetensors_path, int device, qw_model** out);
+void qw_free(qw_model* model);
+
+/* MetalModel::config (metal_inference.rs:170) */
+int qw_config_get(const qw_model* model, qw_config* out);
+
+/* bytes one decode token reads by the reference's rule (tests/mbu.rs:151-160, bench.rs:107-116):
+ * every tensor except the embedding table, plus one bf16 embedding row */
+uint64_t qw_weight_bytes_per_token(const qw_model* model);
+
+/* MetalKVCache::new (metal_inference.rs:129-137): f32 K/V for `max_seq` positions and the RoPE
+ * table. Unlike the reference (max_seq <= 4064, metal_inference.rs:130) the only cap is memory. */
+int qw_cache_new(qw_model* model, size_t max_seq, qw_cache** out);
+void qw_cache_free(qw_cache* cache);
+size_t qw_cache_max_seq(const qw_cache* cache); /* MetalKVCache::max_seq (metal_inference.rs:121) */
+
+/* MetalModel::forward (metal_inference.rs:286-291): run `token` at `pos`, write its K/V into the
+ * cache, copy vocab_size f32 logits to `logits_out` (host). Synchronous. */
+int qw_forward(qw_model* model, qw_cache* cache, uint32_t token, size_t pos, float* logits_out);
+
+/* MetalModel::decode (metal_inference.rs:297-316): greedy decode; `first` goes in at `start_pos`,
+ * each step's argmax feeds the next, and on_token(user, t) is called with each step's output
+ * token as soon as the GPU produces it (steps calls). The whole run is one kernel launch. */
+typedef void (*qw_token_fn)(void* user, uint32_t token);
+int qw_decode(qw_model* model, qw_cache* cache, uint32_t first, size_t start_pos, size_t steps,
+              qw_token_fn on_token, void* user);
+
+/* Device-resident variants of forward/decode (no host copies, no synchronisation): stream-ordered
+ * launches for callers that keep tokens and logits on the GPU (benchmarks, servers).
+ * d_tokens has steps + 1 entries: d_tokens[0] is the input, d_tokens[i + 1] receives step i's
+ * argmax (the ring of metal_inference.rs:298-302). Errors raised on the device are reported by
+ * the next qw_sync. */
+int qw_forward_device(qw_model* model, qw_cache* cache, const uint32_t* d_token, size_t pos,
+                      float* d_logits, void* stream);
+int qw_decode_device(qw_model* model, qw_cache* cache, uint32_t* d_tokens, size_t start_pos,
+                     size_t steps, void* stream);
+int qw_sync(qw_model* model, void* stream);
+
+/* Copy layer `layer`'s K and V for positions [0, n) to host buffers in the reference layout
+ * [t][num_key_value_heads * head_dim] (KVCache, cpu_inference.rs:44-48). */
+int qw_cache_read(qw_cache* cache, size_t layer, size_t n, float* k_out, float* v_out);
+
+/* Streaming-SM count the decode kernel uses (one CTA per SM). */
+int qw_num_ctas(const qw_model* model);
+
+/* The model's own cudaStream_t (what qw_forward/qw_decode run on), e.g. to bracket them with
+ * events. */
+void* qw_model_stream(const qw_model* model);
+
+/* ---- standalone kernels (the device code of the decode kernel, exposed for microbenchmarks) ---- */
+
+/* y = W x, W bf16 [rows][cols] row-major, x/y f32 — the matvec_bf16 kernel
+ * (shaders/inference.metal:143-186, cpu_inference.rs:225-257) as the decode kernel streams it.
+ * cols must be a multiple of 256 (<= 1024, or a multiple of 1024 up to 12288). */
+int qw_gemv_bf16(int device, const uint16_t* d_w, const float* d_x, float* d_y, size_t rows, size_t cols,
+                 void* stream);
+
+/* *d_out = first index of the largest element (tests/common/mod.rs:17-22: ties to the lowest
+ * index, a NaN at index 0 gives 0, other NaNs never win; the GPU argmax of
+ * shaders/inference.metal:300-321). d_workspace holds qw_argmax_workspace_size(n) bytes. */
+size_t qw_argmax_workspace_size(size_t n);
+int qw_argmax_f32(int device, const float* d_x, size_t n, uint32_t* d_out, void* d_workspace, void* stream);
+
+/* Streaming-read probe (tests/read_bandwidth.rs:16-54): sums n_floats floats (n_floats % 4 == 0,
+ * d_src 16-byte aligned) into per-CTA partials d_partials[0 .. n_partials). Returns the number
+ * of partials written through *n_written. */
+int qw_read_probe(int device, const float* d_src, size_t n_floats, float* d_partials, size_t n_partials,
+                  size_t* n_written, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CUDA_INFERENCE_H */

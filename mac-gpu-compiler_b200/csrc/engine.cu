@@ -1,0 +1,587 @@
+// Host engine behind include/cuda_inference.h: model/cache lifetime, weight repacking and upload,
+// launches of the persistent decode kernel (decode_kernel.cuh), token streaming to the host, and
+// the standalone GEMV / argmax / read-probe kernels.
+//
+// Replaces metal_infrence_engine/src/metal_inference.rs. Differences that follow from the
+// hardware: B200 has no unified memory, so load_model copies the weights to HBM (repacking q|k|v
+// into one matrix and interleaving gate/up rows, so one streaming pass per phase reads them);
+// a whole token, and a whole greedy decode, is one cooperative kernel launch instead of ~424
+// dispatches per token.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/cuda_inference.h"
+#include "decode_kernel.cuh"
+#include "model_file.h"
+
+using namespace qw;
+
+namespace {
+
+thread_local std::string g_err;
+
+int set_err(int code, const std::string& msg) {
+    g_err = msg;
+    return code;
+}
+
+int cuda_err(cudaError_t e, const char* what) {
+    return set_err(QW_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+#define QW_CUDA(call)                                            \
+    do {                                                         \
+        cudaError_t e_ = (call);                                 \
+        if (e_ != cudaSuccess) return cuda_err(e_, #call);       \
+    } while (0)
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+long long timeout_ns_from_env() {
+    const char* s = std::getenv("QW_WAIT_TIMEOUT_MS");
+    long long ms = s ? std::atoll(s) : 4000;
+    if (ms < 50) ms = 50;
+    return ms * 1000000LL;
+}
+
+const char* derr_name(int code) {
+    switch (code) {
+        case DERR_TIMEOUT_GRID: return "grid barrier wait expired";
+        case DERR_TIMEOUT_FULL: return "ring-slot data wait expired";
+        case DERR_TIMEOUT_EMPTY: return "ring-slot release wait expired";
+        case DERR_TIMEOUT_KV: return "KV visibility wait expired";
+        case DERR_BAD_TOKEN: return "input token id >= vocab_size";
+        case DERR_TIMEOUT_DRAIN: return "bulk-copy drain wait expired";
+        default: return "unknown device error";
+    }
+}
+
+}  // namespace
+
+namespace qw {
+
+int set_error(int code, const char* msg) { return set_err(code, msg); }
+
+// lazily allocated 16-byte error word per device, for the standalone kernels
+int* device_err_word_for(int device) {
+    static std::mutex mu;
+    static std::vector<int*> words;
+    std::lock_guard<std::mutex> lock(mu);
+    if ((int)words.size() <= device) words.resize(device + 1, nullptr);
+    if (!words[device]) {
+        int* p = nullptr;
+        if (cudaMalloc(&p, 16) != cudaSuccess) return nullptr;
+        cudaMemset(p, 0, 16);
+        words[device] = p;
+    }
+    return words[device];
+}
+
+}  // namespace qw
+
+namespace qw {
+
+// the persistent decode kernel (device code in decode_kernel.cuh)
+__global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
+    __shared__ Smem sm;
+    extern __shared__ __align__(128) uint8_t dyn[];
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < NSLOT; i++) {
+            mbar_init(&sm.full[i], 1);
+            mbar_init(&sm.empty[i], NCW);
+        }
+        sm.progress = 0;
+        sm.abort = 0;
+        sm.token = 0;
+        sm.is_last = 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    Decoder d(p, sm, dyn);
+    if (d.warp == NCW) {
+        if (d.lane == 0) d.produce();
+        return;
+    }
+    d.consume();
+}
+
+}  // namespace qw
+
+struct qw_model {
+    uint64_t id = 0;  // unique per load, so a cache can tell its model from a later one at the same address
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int nctas = 0;
+    ModelConfig cfg;
+    uint64_t wbytes = 0;
+    // weights
+    uint16_t* d_weights = nullptr;  // one allocation: layers | norms | final norm | embed | lm_head
+    uint16_t *d_layer_w = nullptr, *d_layer_n = nullptr, *d_final_norm = nullptr, *d_embed = nullptr, *d_lm_head = nullptr;
+    long long layer_stride = 0, norm_stride = 0;
+    // scratch (one allocation)
+    uint8_t* d_scratch = nullptr;
+    float *d_x = nullptr, *d_qkv = nullptr, *d_att = nullptr, *d_h = nullptr, *d_apart = nullptr, *d_am_val = nullptr,
+          *d_logits = nullptr;
+    unsigned *d_acount = nullptr, *d_am_idx = nullptr;
+    int *d_nan0 = nullptr, *d_err = nullptr;
+    unsigned long long* d_flags = nullptr;
+    // token ring (device) and its mapped host mirror
+    uint32_t* d_tok = nullptr;
+    size_t tok_cap = 0;
+    uint32_t* h_tok = nullptr;   // mapped pinned [cap]
+    unsigned* h_count = nullptr; // mapped pinned
+    uint32_t* h_tok_dev = nullptr;
+    unsigned* h_count_dev = nullptr;
+    size_t h_cap = 0;
+    uint32_t* h_stage = nullptr; // pinned, 1 token
+    float* h_logits = nullptr;   // pinned [vocab]
+    unsigned epoch = 0;
+    int S = 0, part_cap = 0, xs_cap = 0;
+    size_t dyn_smem = 0;
+    long long timeout_ns = 0;
+    bool dirty = false;
+};
+
+// A cache never dereferences its model after qw_cache_new: it keeps what it needs (device,
+// geometry), so caches and models may be freed in either order. `m` is only compared.
+struct qw_cache {
+    const qw_model* m = nullptr;
+    uint64_t model_id = 0;
+    int device = 0;
+    uint64_t layers = 0, kv_heads = 0, head_dim = 0;
+    size_t max_seq = 0;
+    float* d_k = nullptr;
+    float* d_v = nullptr;
+    float2* d_rope = nullptr;
+};
+
+namespace {
+
+int ensure_token_capacity(qw_model* m, size_t n) {
+    if (n > m->tok_cap) {
+        size_t cap = std::max<size_t>(n, 2 * m->tok_cap);
+        uint32_t* d = nullptr;
+        if (cudaMalloc(&d, cap * 4) != cudaSuccess) return set_err(QW_ERR_NOMEM, "token ring allocation failed");
+        if (m->d_tok) cudaFree(m->d_tok);
+        m->d_tok = d;
+        m->tok_cap = cap;
+    }
+    if (n > m->h_cap) {
+        size_t cap = std::max<size_t>(n, 2 * m->h_cap);
+        void* h = nullptr;
+        if (cudaHostAlloc(&h, cap * 4 + 64, cudaHostAllocMapped) != cudaSuccess)
+            return set_err(QW_ERR_NOMEM, "pinned token ring allocation failed");
+        if (m->h_tok) cudaFreeHost(m->h_tok);
+        m->h_tok = static_cast<uint32_t*>(h);
+        m->h_count = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(h) + cap * 4 + 32);
+        QW_CUDA(cudaHostGetDevicePointer((void**)&m->h_tok_dev, m->h_tok, 0));
+        QW_CUDA(cudaHostGetDevicePointer((void**)&m->h_count_dev, m->h_count, 0));
+        m->h_cap = cap;
+    }
+    return QW_OK;
+}
+
+int launch_decode(qw_model* m, qw_cache* c, const uint32_t* tok_in, uint32_t* tok_out, bool stream_to_host,
+                  float* logits, size_t start_pos, size_t steps, cudaStream_t s) {
+    const ModelConfig& g = m->cfg;
+    if (m->dirty) {
+        QW_CUDA(cudaMemsetAsync(m->d_acount, 0, g.kv_heads * sizeof(unsigned), s));
+        m->dirty = false;
+    }
+    DecodeParams p{};
+    p.layer_w = m->d_layer_w;
+    p.layer_n = m->d_layer_n;
+    p.final_norm = m->d_final_norm;
+    p.embed = m->d_embed;
+    p.lm_head = m->d_lm_head;
+    p.kc = c->d_k;
+    p.vc = c->d_v;
+    p.rope = c->d_rope;
+    p.x = m->d_x;
+    p.qkv = m->d_qkv;
+    p.att = m->d_att;
+    p.hbuf = m->d_h;
+    p.apart = m->d_apart;
+    p.acount = m->d_acount;
+    p.am_val = m->d_am_val;
+    p.am_idx = m->d_am_idx;
+    p.nan0 = m->d_nan0;
+    p.flags = m->d_flags;
+    p.err = m->d_err;
+    p.logits = logits;
+    p.tok_in = tok_in;
+    p.tok_out = tok_out;
+    p.host_tok = stream_to_host ? m->h_tok_dev : nullptr;
+    p.host_count = stream_to_host ? m->h_count_dev : nullptr;
+    p.layer_stride = m->layer_stride;
+    p.norm_stride = m->norm_stride;
+    p.H = (int)g.hidden;
+    p.I = (int)g.inter;
+    p.L = (int)g.layers;
+    p.NQ = (int)g.heads;
+    p.NKV = (int)g.kv_heads;
+    p.V = (int)g.vocab;
+    p.max_seq = (int)c->max_seq;
+    p.start_pos = (int)start_pos;
+    p.steps = (int)steps;
+    p.epoch = ++m->epoch;
+    p.eps = g.eps;
+    p.scale = 1.0f / sqrtf((float)g.head_dim);  // cpu_inference.rs:144
+    p.S = m->S;
+    p.part_cap = m->part_cap;
+    p.xs_cap = m->xs_cap;
+    p.timeout_ns = m->timeout_ns;
+    void* args[] = {&p};
+    cudaError_t e = cudaLaunchCooperativeKernel((const void*)decode_kernel, dim3(m->nctas), dim3(NTHREADS), args,
+                                                m->dyn_smem, s);
+    if (e != cudaSuccess) return cuda_err(e, "decode kernel launch");
+    return QW_OK;
+}
+
+// reads and clears the device error word after a synchronisation
+int check_device_err(qw_model* m) {
+    int err[4] = {0, 0, 0, 0};
+    QW_CUDA(cudaMemcpy(err, m->d_err, sizeof err, cudaMemcpyDeviceToHost));
+    if (err[0] == 0 && err[3] == 0) return QW_OK;
+    QW_CUDA(cudaMemset(m->d_err, 0, sizeof err));
+    m->dirty = true;
+    char buf[256];
+    std::snprintf(buf, sizeof buf, "device: %s (cta %d, at %d)%s", derr_name(err[0]), err[1], err[2],
+                  err[3] ? "; a bulk-copy drain also expired" : "");
+    return set_err(err[0] == DERR_BAD_TOKEN ? QW_ERR_ARG : QW_ERR_DEVICE_TIMEOUT, buf);
+}
+
+cudaStream_t pick_stream(qw_model* m, void* s) { return s ? static_cast<cudaStream_t>(s) : m->stream; }
+
+}  // namespace
+
+extern "C" {
+
+const char* qw_last_error(void) { return g_err.c_str(); }
+
+int qw_inspect(const char* path, qw_config* out) {
+    if (!path || !out) return set_err(QW_ERR_ARG, "null argument");
+    ModelFile f;
+    std::string msg;
+    int rc = f.open(path, msg);
+    if (rc) return set_err(rc, msg);
+    const ModelConfig& c = f.config();
+    *out = qw_config{c.hidden, c.inter, c.layers, c.heads, c.kv_heads, c.head_dim, c.vocab, c.eps, c.theta, c.eos};
+    return QW_OK;
+}
+
+int qw_load(const char* path, int device, qw_model** out) {
+    if (!path || !out) return set_err(QW_ERR_ARG, "null argument");
+    *out = nullptr;
+    ModelFile f;
+    std::string msg;
+    int rc = f.open(path, msg);
+    if (rc) return set_err(rc, msg);
+    const ModelConfig& c = f.config();
+
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) return set_err(QW_ERR_CUDA, "no CUDA device");
+    if (device < 0 || device >= ndev) return set_err(QW_ERR_ARG, "device index out of range");
+    QW_CUDA(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    QW_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major < 10) return set_err(QW_ERR_UNSUPPORTED, "the kernels are built for sm_100a (B200)");
+    if (!prop.cooperativeLaunch) return set_err(QW_ERR_UNSUPPORTED, "device lacks cooperative launch");
+
+    static std::atomic<uint64_t> next_id{1};
+    auto m = new qw_model();
+    m->id = next_id.fetch_add(1);
+    m->device = device;
+    m->cfg = c;
+    m->wbytes = f.weight_bytes_per_token();
+    m->timeout_ns = timeout_ns_from_env();
+    int nctas = prop.multiProcessorCount;
+    if (const char* e = std::getenv("QW_CTAS")) nctas = std::max(1, std::min(nctas, std::atoi(e)));
+    if ((uint64_t)nctas < c.kv_heads) { delete m; return set_err(QW_ERR_UNSUPPORTED, "fewer SMs than KV heads"); }
+    m->nctas = nctas;
+    m->S = nctas / (int)c.kv_heads;
+
+    const uint64_t H = c.hidden, I = c.inter, QD = c.heads * c.head_dim, KVD = c.kv_heads * c.head_dim;
+    const uint64_t QKVR = QD + 2 * KVD;
+    m->layer_stride = (long long)(QKVR * H + H * QD + 2 * I * H + H * I);
+    m->norm_stride = (long long)align_up(2 * H + 2 * c.head_dim, 64);
+    const size_t n_layer_w = (size_t)m->layer_stride * c.layers;
+    const size_t n_layer_n = (size_t)m->norm_stride * c.layers;
+    const size_t off_n = align_up(n_layer_w, 128);
+    const size_t off_f = off_n + align_up(n_layer_n, 128);
+    const size_t off_e = off_f + align_up(H, 128);
+    const size_t off_l = off_e + align_up(c.vocab * H, 128);
+    const size_t total = off_l + c.vocab * H;
+
+    auto fail = [&](int code, const std::string& why) {
+        qw_free(m);
+        return set_err(code, why);
+    };
+    if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) return fail(QW_ERR_CUDA, "stream creation failed");
+    if (cudaMalloc(&m->d_weights, total * 2) != cudaSuccess) return fail(QW_ERR_NOMEM, "weight allocation failed");
+    m->d_layer_w = m->d_weights;
+    m->d_layer_n = m->d_weights + off_n;
+    m->d_final_norm = m->d_weights + off_f;
+    m->d_embed = m->d_weights + off_e;
+    m->d_lm_head = m->d_weights + off_l;
+
+    // repack each layer into one block: q|k|v rows, o, gate/up interleaved by row, down
+    {
+        std::vector<uint16_t> blk((size_t)m->layer_stride);
+        std::vector<uint16_t> nb((size_t)m->norm_stride * c.layers, 0);
+        for (uint64_t l = 0; l < c.layers; l++) {
+            const std::string p = "model.layers." + std::to_string(l) + ".";
+            auto w = [&](const char* n) { return reinterpret_cast<const uint16_t*>(f.data(p + n)); };
+            uint16_t* d = blk.data();
+            std::memcpy(d, w("self_attn.q_proj.weight"), QD * H * 2);
+            d += QD * H;
+            std::memcpy(d, w("self_attn.k_proj.weight"), KVD * H * 2);
+            d += KVD * H;
+            std::memcpy(d, w("self_attn.v_proj.weight"), KVD * H * 2);
+            d += KVD * H;
+            std::memcpy(d, w("self_attn.o_proj.weight"), H * QD * 2);
+            d += H * QD;
+            const uint16_t* gt = w("mlp.gate_proj.weight");
+            const uint16_t* up = w("mlp.up_proj.weight");
+            for (uint64_t i = 0; i < I; i++) {
+                std::memcpy(d + (2 * i) * H, gt + i * H, H * 2);
+                std::memcpy(d + (2 * i + 1) * H, up + i * H, H * 2);
+            }
+            d += 2 * I * H;
+            std::memcpy(d, w("mlp.down_proj.weight"), H * I * 2);
+            if (cudaMemcpy(m->d_layer_w + l * m->layer_stride, blk.data(), blk.size() * 2, cudaMemcpyHostToDevice) != cudaSuccess)
+                return fail(QW_ERR_CUDA, "weight upload failed");
+            uint16_t* n = nb.data() + l * m->norm_stride;
+            std::memcpy(n, w("input_layernorm.weight"), H * 2);
+            std::memcpy(n + H, w("post_attention_layernorm.weight"), H * 2);
+            std::memcpy(n + 2 * H, w("self_attn.q_norm.weight"), c.head_dim * 2);
+            std::memcpy(n + 2 * H + c.head_dim, w("self_attn.k_norm.weight"), c.head_dim * 2);
+        }
+        if (cudaMemcpy(m->d_layer_n, nb.data(), nb.size() * 2, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(m->d_final_norm, f.data("model.norm.weight"), H * 2, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(m->d_embed, f.data("model.embed_tokens.weight"), c.vocab * H * 2, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(m->d_lm_head, f.data("lm_head.weight"), c.vocab * H * 2, cudaMemcpyHostToDevice) != cudaSuccess)
+            return fail(QW_ERR_CUDA, "weight upload failed");
+    }
+
+    // scratch
+    const int G = (int)(c.heads / c.kv_heads);
+    auto ceil_div = [](uint64_t a, uint64_t b) { return (a + b - 1) / b; };
+    auto phase_cap = [&](uint64_t rows, uint64_t K) { return (uint64_t)seg_count((int)K) * (ceil_div(rows, nctas) + 2); };
+    uint64_t pc = std::max({phase_cap(QKVR, H), phase_cap(H, QD), phase_cap(2 * I, H) + 2, phase_cap(H, I), phase_cap(c.vocab, H)});
+    m->part_cap = (int)align_up(pc, 4);
+    m->xs_cap = (int)align_up(std::max({H, QD, I}), 4);
+    m->dyn_smem = (size_t)NSLOT * SLOT_BYTES + ((size_t)m->part_cap + m->xs_cap) * 4;
+    if (m->dyn_smem + sizeof(Smem) > (size_t)prop.sharedMemPerBlockOptin)
+        return fail(QW_ERR_UNSUPPORTED, "model too large for the kernel's shared-memory plan (vocab or widths)");
+    if (cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->dyn_smem) != cudaSuccess)
+        return fail(QW_ERR_CUDA, "cannot raise the decode kernel's shared-memory limit");
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_kernel, NTHREADS, m->dyn_smem) != cudaSuccess || per_sm < 1)
+        return fail(QW_ERR_UNSUPPORTED, "decode kernel does not fit on an SM");
+
+    struct Piece { size_t bytes; void** dst; };
+    const size_t sz_apart = (size_t)c.kv_heads * m->S * G * APART_STRIDE * 4;
+    std::vector<Piece> pieces = {
+        {H * 4, (void**)&m->d_x}, {QKVR * 4, (void**)&m->d_qkv}, {QD * 4, (void**)&m->d_att},
+        {I * 4, (void**)&m->d_h}, {sz_apart, (void**)&m->d_apart}, {c.kv_heads * 4, (void**)&m->d_acount},
+        {(size_t)nctas * 4, (void**)&m->d_am_val}, {(size_t)nctas * 4, (void**)&m->d_am_idx}, {16, (void**)&m->d_nan0},
+        {(size_t)nctas * 8, (void**)&m->d_flags}, {16, (void**)&m->d_err}, {c.vocab * 4, (void**)&m->d_logits}};
+    size_t scratch = 0;
+    for (auto& pc2 : pieces) scratch += align_up(pc2.bytes, 256);
+    if (cudaMalloc(&m->d_scratch, scratch) != cudaSuccess) return fail(QW_ERR_NOMEM, "scratch allocation failed");
+    if (cudaMemset(m->d_scratch, 0, scratch) != cudaSuccess) return fail(QW_ERR_CUDA, "scratch memset failed");
+    size_t off = 0;
+    for (auto& pc2 : pieces) {
+        *pc2.dst = m->d_scratch + off;
+        off += align_up(pc2.bytes, 256);
+    }
+    if (cudaHostAlloc(&m->h_stage, 64, cudaHostAllocDefault) != cudaSuccess ||
+        cudaHostAlloc(&m->h_logits, c.vocab * 4, cudaHostAllocDefault) != cudaSuccess)
+        return fail(QW_ERR_NOMEM, "pinned host allocation failed");
+    if (int e = ensure_token_capacity(m, 1024)) { qw_free(m); return e; }
+    if (cudaDeviceSynchronize() != cudaSuccess) return fail(QW_ERR_CUDA, "device synchronisation failed after load");
+    *out = m;
+    return QW_OK;
+}
+
+void qw_free(qw_model* m) {
+    if (!m) return;
+    cudaSetDevice(m->device);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    cudaFree(m->d_weights);
+    cudaFree(m->d_scratch);
+    cudaFree(m->d_tok);
+    if (m->h_tok) cudaFreeHost(m->h_tok);
+    if (m->h_stage) cudaFreeHost(m->h_stage);
+    if (m->h_logits) cudaFreeHost(m->h_logits);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+}
+
+int qw_config_get(const qw_model* m, qw_config* out) {
+    if (!m || !out) return set_err(QW_ERR_ARG, "null argument");
+    const ModelConfig& c = m->cfg;
+    *out = qw_config{c.hidden, c.inter, c.layers, c.heads, c.kv_heads, c.head_dim, c.vocab, c.eps, c.theta, c.eos};
+    return QW_OK;
+}
+
+uint64_t qw_weight_bytes_per_token(const qw_model* m) { return m ? m->wbytes : 0; }
+
+int qw_num_ctas(const qw_model* m) { return m ? m->nctas : 0; }
+
+void* qw_model_stream(const qw_model* m) { return m ? static_cast<void*>(m->stream) : nullptr; }
+
+int qw_cache_new(qw_model* m, size_t max_seq, qw_cache** out) {
+    if (!m || !out) return set_err(QW_ERR_ARG, "null argument");
+    *out = nullptr;
+    if (max_seq == 0 || max_seq > (1u << 30)) return set_err(QW_ERR_ARG, "max_seq out of range");
+    QW_CUDA(cudaSetDevice(m->device));
+    const ModelConfig& c = m->cfg;
+    auto cc = new qw_cache();
+    cc->m = m;
+    cc->model_id = m->id;
+    cc->device = m->device;
+    cc->layers = c.layers;
+    cc->kv_heads = c.kv_heads;
+    cc->head_dim = c.head_dim;
+    cc->max_seq = max_seq;
+    const size_t kv = c.layers * c.kv_heads * max_seq * c.head_dim * 4;
+    const size_t half = c.head_dim / 2;
+    if (cudaMalloc(&cc->d_k, kv) != cudaSuccess || cudaMalloc(&cc->d_v, kv) != cudaSuccess ||
+        cudaMalloc(&cc->d_rope, max_seq * half * sizeof(float2)) != cudaSuccess) {
+        qw_cache_free(cc);
+        return set_err(QW_ERR_NOMEM, "KV cache allocation failed");
+    }
+    cudaMemset(cc->d_k, 0, kv);
+    cudaMemset(cc->d_v, 0, kv);
+    // RoPE table, same math as the reference's (metal_inference.rs:141-154 == cpu_inference.rs:204-215):
+    // freq_i = theta^(-2i/head_dim) in f32, then sin/cos of (pos as f32) * freq_i
+    std::vector<float> freqs(half);
+    for (size_t i = 0; i < half; i++) freqs[i] = powf(c.theta, -2.0f * (float)i / (float)c.head_dim);
+    std::vector<float2> tab(max_seq * half);
+    for (size_t pos = 0; pos < max_seq; pos++)
+        for (size_t i = 0; i < half; i++) {
+            const float a = (float)pos * freqs[i];
+            tab[pos * half + i] = make_float2(cosf(a), sinf(a));
+        }
+    if (cudaMemcpy(cc->d_rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice) != cudaSuccess) {
+        qw_cache_free(cc);
+        return set_err(QW_ERR_CUDA, "RoPE table upload failed");
+    }
+    *out = cc;
+    return QW_OK;
+}
+
+void qw_cache_free(qw_cache* c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    cudaFree(c->d_k);  // cudaFree synchronises with work still using the buffers
+    cudaFree(c->d_v);
+    cudaFree(c->d_rope);
+    delete c;
+}
+
+size_t qw_cache_max_seq(const qw_cache* c) { return c ? c->max_seq : 0; }
+
+int qw_forward(qw_model* m, qw_cache* c, uint32_t token, size_t pos, float* logits_out) {
+    if (!m || !c || !logits_out || c->m != m || c->model_id != m->id) return set_err(QW_ERR_ARG, "null or mismatched handle");
+    if (token >= m->cfg.vocab) return set_err(QW_ERR_ARG, "token id >= vocab_size");
+    if (pos >= c->max_seq) return set_err(QW_ERR_ARG, "pos exceeds the KV cache size");  // metal_inference.rs:321
+    QW_CUDA(cudaSetDevice(m->device));
+    m->h_stage[0] = token;
+    QW_CUDA(cudaMemcpyAsync(m->d_tok, m->h_stage, 4, cudaMemcpyHostToDevice, m->stream));
+    if (int e = launch_decode(m, c, m->d_tok, nullptr, false, m->d_logits, pos, 1, m->stream)) return e;
+    QW_CUDA(cudaMemcpyAsync(m->h_logits, m->d_logits, m->cfg.vocab * 4, cudaMemcpyDeviceToHost, m->stream));
+    QW_CUDA(cudaStreamSynchronize(m->stream));
+    if (int e = check_device_err(m)) return e;
+    std::memcpy(logits_out, m->h_logits, m->cfg.vocab * 4);
+    return QW_OK;
+}
+
+int qw_decode(qw_model* m, qw_cache* c, uint32_t first, size_t start_pos, size_t steps, qw_token_fn on_token, void* user) {
+    if (!m || !c || c->m != m || c->model_id != m->id) return set_err(QW_ERR_ARG, "null or mismatched handle");
+    if (steps == 0) return QW_OK;
+    if (first >= m->cfg.vocab) return set_err(QW_ERR_ARG, "token id >= vocab_size");
+    if (start_pos + steps > c->max_seq) return set_err(QW_ERR_ARG, "start_pos + steps exceeds the KV cache size");
+    QW_CUDA(cudaSetDevice(m->device));
+    if (int e = ensure_token_capacity(m, steps + 1)) return e;
+    m->h_stage[0] = first;
+    __atomic_store_n(m->h_count, 0u, __ATOMIC_RELEASE);
+    QW_CUDA(cudaMemcpyAsync(m->d_tok, m->h_stage, 4, cudaMemcpyHostToDevice, m->stream));
+    if (int e = launch_decode(m, c, m->d_tok, m->d_tok, true, nullptr, start_pos, steps, m->stream)) return e;
+    // hand each token to on_token as soon as the GPU publishes it
+    size_t done = 0;
+    unsigned polls = 0;
+    for (;;) {
+        const unsigned cnt = __atomic_load_n(m->h_count, __ATOMIC_ACQUIRE);
+        while (done < cnt && done < steps) {
+            ++done;
+            if (on_token) on_token(user, m->h_tok[done]);
+        }
+        if (done >= steps) break;
+        if ((++polls & 63) == 0) {
+            cudaError_t q = cudaStreamQuery(m->stream);
+            if (q != cudaErrorNotReady) {
+                const unsigned fin = __atomic_load_n(m->h_count, __ATOMIC_ACQUIRE);
+                while (done < fin && done < steps) {
+                    ++done;
+                    if (on_token) on_token(user, m->h_tok[done]);
+                }
+                break;
+            }
+        }
+    }
+    QW_CUDA(cudaStreamSynchronize(m->stream));
+    if (int e = check_device_err(m)) return e;
+    if (done != steps) return set_err(QW_ERR_CUDA, "decode ended before producing every token");
+    return QW_OK;
+}
+
+int qw_forward_device(qw_model* m, qw_cache* c, const uint32_t* d_token, size_t pos, float* d_logits, void* stream) {
+    if (!m || !c || !d_token || c->m != m || c->model_id != m->id) return set_err(QW_ERR_ARG, "null or mismatched handle");
+    if (pos >= c->max_seq) return set_err(QW_ERR_ARG, "pos exceeds the KV cache size");
+    QW_CUDA(cudaSetDevice(m->device));
+    return launch_decode(m, c, d_token, nullptr, false, d_logits, pos, 1, pick_stream(m, stream));
+}
+
+int qw_decode_device(qw_model* m, qw_cache* c, uint32_t* d_tokens, size_t start_pos, size_t steps, void* stream) {
+    if (!m || !c || !d_tokens || c->m != m || c->model_id != m->id) return set_err(QW_ERR_ARG, "null or mismatched handle");
+    if (steps == 0) return QW_OK;
+    if (start_pos + steps > c->max_seq) return set_err(QW_ERR_ARG, "start_pos + steps exceeds the KV cache size");
+    QW_CUDA(cudaSetDevice(m->device));
+    return launch_decode(m, c, d_tokens, d_tokens, false, nullptr, start_pos, steps, pick_stream(m, stream));
+}
+
+int qw_sync(qw_model* m, void* stream) {
+    if (!m) return set_err(QW_ERR_ARG, "null handle");
+    QW_CUDA(cudaSetDevice(m->device));
+    QW_CUDA(cudaStreamSynchronize(pick_stream(m, stream)));
+    return check_device_err(m);
+}
+
+int qw_cache_read(qw_cache* c, size_t layer, size_t n, float* k_out, float* v_out) {
+    if (!c || !k_out || !v_out) return set_err(QW_ERR_ARG, "null argument");
+    if (layer >= c->layers || n > c->max_seq) return set_err(QW_ERR_ARG, "layer or n out of range");
+    if (n == 0) return QW_OK;
+    QW_CUDA(cudaSetDevice(c->device));
+    QW_CUDA(cudaDeviceSynchronize());
+    const size_t D = c->head_dim, KVD = c->kv_heads * D;
+    for (size_t h = 0; h < c->kv_heads; h++) {
+        const size_t src = ((layer * c->kv_heads + h) * c->max_seq) * D;
+        QW_CUDA(cudaMemcpy2D(k_out + h * D, KVD * 4, c->d_k + src, D * 4, D * 4, n, cudaMemcpyDeviceToHost));
+        QW_CUDA(cudaMemcpy2D(v_out + h * D, KVD * 4, c->d_v + src, D * 4, D * 4, n, cudaMemcpyDeviceToHost));
+    }
+    return QW_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,238 @@
+"""Python binding of ``libcuda_inference.so`` (include/cuda_inference.h).
+
+The surface mirrors the reference's GPU engine, ``metal_infrence_engine/src/metal_inference.rs``:
+``CudaModel.load_model(path)`` (metal_inference.rs:157), ``model.config`` (:170),
+``model.forward(token, pos, cache) -> logits`` (:286), ``model.decode(first, start_pos, steps,
+cache, on_token)`` (:297) and ``CudaKVCache(model, max_seq)`` (:129, ``max_seq`` :121), so tests
+and benchmarks read like the reference's ``tests/metal_parity.rs`` and ``src/bin/bench.rs``.
+
+There is no fallback: if the shared library is missing or a call fails, an exception is raised.
+Where the reference panics (missing tensor, non-BF16 weights, ``pos >= max_seq``), the C ABI
+returns a status code and this module raises ``QwError``.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from pathlib import Path
+from typing import Callable
+
+import numpy as np
+
+_HERE = Path(__file__).resolve().parent
+LIB_PATH = _HERE / "libcuda_inference.so"
+HEADER = _HERE.parent / "include" / "cuda_inference.h"
+
+QW_OK, QW_ERR_IO, QW_ERR_FORMAT, QW_ERR_UNSUPPORTED, QW_ERR_ARG, QW_ERR_CUDA, QW_ERR_DEVICE_TIMEOUT, QW_ERR_NOMEM = range(8)
+_ERR_NAMES = ["OK", "IO", "FORMAT", "UNSUPPORTED", "ARG", "CUDA", "DEVICE_TIMEOUT", "NOMEM"]
+
+
+class QwError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        self.code = code
+        name = _ERR_NAMES[code] if 0 <= code < len(_ERR_NAMES) else str(code)
+        super().__init__(f"QW_ERR_{name}: {msg}")
+
+
+class _Config(ctypes.Structure):
+    _fields_ = [("hidden_size", ctypes.c_uint64), ("intermediate_size", ctypes.c_uint64),
+                ("num_hidden_layers", ctypes.c_uint64), ("num_attention_heads", ctypes.c_uint64),
+                ("num_key_value_heads", ctypes.c_uint64), ("head_dim", ctypes.c_uint64),
+                ("vocab_size", ctypes.c_uint64), ("rms_norm_eps", ctypes.c_float),
+                ("rope_theta", ctypes.c_float), ("eos_token_id", ctypes.c_uint32)]
+
+
+@dataclass
+class Config:
+    """cpu_inference.rs:21-33"""
+    hidden_size: int
+    intermediate_size: int
+    num_hidden_layers: int
+    num_attention_heads: int
+    num_key_value_heads: int
+    head_dim: int
+    vocab_size: int
+    rms_norm_eps: float
+    rope_theta: float
+    eos_token_id: int
+
+    @classmethod
+    def _from(cls, c: _Config) -> "Config":
+        return cls(*(int(getattr(c, f)) for f, _ in _Config._fields_[:7]), float(c.rms_norm_eps),
+                   float(c.rope_theta), int(c.eos_token_id))
+
+
+TOKEN_FN = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_uint32)
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load libcuda_inference.so (raises if it was not built: there is no fallback path)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise ImportError(f"{LIB_PATH} is missing; build it with `python {_HERE / 'build.py'}`")
+        L = ctypes.CDLL(str(LIB_PATH))
+        vp, sz, i32, u32, u64 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int, ctypes.c_uint32, ctypes.c_uint64
+        sig = {
+            "qw_last_error": (ctypes.c_char_p, []),
+            "qw_inspect": (i32, [ctypes.c_char_p, ctypes.POINTER(_Config)]),
+            "qw_load": (i32, [ctypes.c_char_p, i32, ctypes.POINTER(vp)]),
+            "qw_free": (None, [vp]),
+            "qw_config_get": (i32, [vp, ctypes.POINTER(_Config)]),
+            "qw_weight_bytes_per_token": (u64, [vp]),
+            "qw_cache_new": (i32, [vp, sz, ctypes.POINTER(vp)]),
+            "qw_cache_free": (None, [vp]),
+            "qw_cache_max_seq": (sz, [vp]),
+            "qw_forward": (i32, [vp, vp, u32, sz, vp]),
+            "qw_decode": (i32, [vp, vp, u32, sz, sz, TOKEN_FN, vp]),
+            "qw_forward_device": (i32, [vp, vp, vp, sz, vp, vp]),
+            "qw_decode_device": (i32, [vp, vp, vp, sz, sz, vp]),
+            "qw_sync": (i32, [vp, vp]),
+            "qw_cache_read": (i32, [vp, sz, sz, vp, vp]),
+            "qw_num_ctas": (i32, [vp]),
+            "qw_model_stream": (vp, [vp]),
+            "qw_gemv_bf16": (i32, [i32, vp, vp, vp, sz, sz, vp]),
+            "qw_argmax_workspace_size": (sz, [sz]),
+            "qw_argmax_f32": (i32, [i32, vp, sz, vp, vp, vp]),
+            "qw_read_probe": (i32, [i32, vp, sz, vp, sz, ctypes.POINTER(sz), vp]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _check(rc: int) -> None:
+    if rc != QW_OK:
+        raise QwError(rc, lib().qw_last_error().decode(errors="replace"))
+
+
+def inspect(path: str | Path) -> Config:
+    """Parse and validate a checkpoint directory's safetensors + config.json (no GPU needed)."""
+    c = _Config()
+    _check(lib().qw_inspect(str(path).encode(), ctypes.byref(c)))
+    return Config._from(c)
+
+
+class CudaModel:
+    """metal_inference.rs:100-113 MetalModel — weights on one B200, one stream."""
+
+    def __init__(self, handle: ctypes.c_void_p, device: int):
+        self._h = handle
+        self.device = device
+        c = _Config()
+        _check(lib().qw_config_get(handle, ctypes.byref(c)))
+        self.config = Config._from(c)
+
+    @classmethod
+    def load_model(cls, path: str | Path, device: int = 0) -> "CudaModel":
+        h = ctypes.c_void_p()
+        _check(lib().qw_load(str(path).encode(), device, ctypes.byref(h)))
+        return cls(h, device)
+
+    def weight_bytes_per_token(self) -> int:
+        """tests/mbu.rs:151-160"""
+        return int(lib().qw_weight_bytes_per_token(self._h))
+
+    @property
+    def num_ctas(self) -> int:
+        return int(lib().qw_num_ctas(self._h))
+
+    @property
+    def stream(self) -> int:
+        """The model's cudaStream_t handle (forward/decode run on it)."""
+        return int(lib().qw_model_stream(self._h) or 0)
+
+    def forward(self, token: int, pos: int, cache: "CudaKVCache") -> np.ndarray:
+        out = np.empty(self.config.vocab_size, np.float32)
+        _check(lib().qw_forward(self._h, cache._h, token, pos, out.ctypes.data))
+        return out
+
+    def decode(self, first: int, start_pos: int, steps: int, cache: "CudaKVCache",
+               on_token: Callable[[int], None] | None = None) -> list[int]:
+        """Greedy decode; on_token(t) is called as each token arrives. Returns the tokens too."""
+        got: list[int] = []
+
+        def cb(_user, tok):
+            got.append(int(tok))
+            if on_token is not None:
+                on_token(int(tok))
+
+        fn = TOKEN_FN(cb)
+        _check(lib().qw_decode(self._h, cache._h, first, start_pos, steps, fn, None))
+        return got
+
+    # device-resident variants: raw device pointers (ints) and an optional cudaStream_t handle
+    def forward_device(self, cache: "CudaKVCache", d_token: int, pos: int, d_logits: int, stream: int = 0) -> None:
+        _check(lib().qw_forward_device(self._h, cache._h, d_token, pos, d_logits, stream or None))
+
+    def decode_device(self, cache: "CudaKVCache", d_tokens: int, start_pos: int, steps: int, stream: int = 0) -> None:
+        _check(lib().qw_decode_device(self._h, cache._h, d_tokens, start_pos, steps, stream or None))
+
+    def sync(self, stream: int = 0) -> None:
+        _check(lib().qw_sync(self._h, stream or None))
+
+    def close(self) -> None:
+        if getattr(self, "_h", None) and _lib is not None:
+            _lib.qw_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+
+class CudaKVCache:
+    """metal_inference.rs:115-137 MetalKVCache — f32 K/V for max_seq positions + RoPE table."""
+
+    def __init__(self, model: CudaModel, max_seq: int):
+        self._model = model
+        self._h = ctypes.c_void_p()
+        _check(lib().qw_cache_new(model._h, max_seq, ctypes.byref(self._h)))
+        self.max_seq = int(lib().qw_cache_max_seq(self._h))
+
+    def layer(self, l: int, n: int) -> tuple[np.ndarray, np.ndarray]:
+        """K, V of layer l for positions [0, n) in the reference layout [t][kv_heads*head_dim]."""
+        c = self._model.config
+        kvd = c.num_key_value_heads * c.head_dim
+        k = np.empty((n, kvd), np.float32)
+        v = np.empty((n, kvd), np.float32)
+        _check(lib().qw_cache_read(self._h, l, n, k.ctypes.data, v.ctypes.data))
+        return k, v
+
+    def close(self) -> None:
+        if getattr(self, "_h", None) and _lib is not None:
+            _lib.qw_cache_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+
+# ---- standalone kernels ----------------------------------------------------------------------
+def gemv_bf16(device: int, d_w: int, d_x: int, d_y: int, rows: int, cols: int, stream: int = 0) -> None:
+    _check(lib().qw_gemv_bf16(device, d_w, d_x, d_y, rows, cols, stream or None))
+
+
+def argmax_workspace_size(n: int) -> int:
+    return int(lib().qw_argmax_workspace_size(n))
+
+
+def argmax_f32(device: int, d_x: int, n: int, d_out: int, d_workspace: int, stream: int = 0) -> None:
+    _check(lib().qw_argmax_f32(device, d_x, n, d_out, d_workspace, stream or None))
+
+
+def read_probe(device: int, d_src: int, n_floats: int, d_partials: int, n_partials: int, stream: int = 0) -> int:
+    n = ctypes.c_size_t()
+    _check(lib().qw_read_probe(device, d_src, n_floats, d_partials, n_partials, ctypes.byref(n), stream or None))
+    return int(n.value)
+
+
+def declared_symbols() -> list[str]:
+    """Every function the C header declares (what the ABI promises to export)."""
+    import re
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(qw_[a-z0-9_]+)\s*\(", text)))
