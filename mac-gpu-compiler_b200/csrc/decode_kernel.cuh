@@ -12,21 +12,27 @@
 //     24 KB shared-memory ring with 1-D TMA bulk copies (cp.async.bulk, no multicast). None of
 //     those bytes depends on the token being decoded, so the producer runs ahead of the math by
 //     up to 192 KB per SM across phase, layer and token boundaries: HBM keeps streaming while
-//     the consumers wait on the grid-wide dependencies below.
+//     the consumers wait for their inputs.
 //   * warps 0..11 are CONSUMERS. Each GEMV phase gives every CTA a contiguous block of output
 //     rows; a ring slot holds whole rows, and a (row, 1024-column segment) unit is one warp's dot
 //     product against the activation vector it holds in registers. Epilogues are fused: q|k|v
-//     rows are written raw; o/down add the residual; gate/up rows are interleaved so the SiLU*up
-//     product is formed in the CTA; lm_head rows feed a per-CTA argmax partial.
-//   * Dependencies between phases (every GEMV output feeds every CTA of the next phase) are
-//     grid barriers built from per-CTA release flags (flag = epoch << 32 | barrier number): a CTA
-//     publishes with st.release.gpu and waits with ld.acquire.gpu polls of all flags. No atomics
-//     on the barrier path, and no reset between launches (the host bumps `epoch`).
+//     rows are written raw; o/down add the residual (each CTA keeps its residual rows in shared
+//     memory); gate/up rows are interleaved so the SiLU*up product is formed in the CTA; lm_head
+//     rows feed a per-CTA argmax partial.
+//   * Hand-off between phases uses TAGGED WORDS: every activation element crosses CTAs as one
+//     64-bit word {f32 value, 32-bit tag}, the tag naming the launch (epoch) and the phase that
+//     wrote it. 8-byte stores are single-copy atomic, so a consumer that reads the tag it expects
+//     has the value that goes with it: polling the input IS the synchronisation, with no fence and
+//     no separate flag round trip. A buffer is rewritten only after every CTA has consumed the
+//     previous contents (each phase needs all of the previous phase's outputs), so tags never
+//     race with a reader.
 //   * Attention: each KV head's positions are split into up to S contiguous chunks, one CTA per
-//     (kv head, chunk). A CTA applies q_norm/k_norm + RoPE itself, the CTA whose chunk holds `pos`
-//     also writes the new K/V into the cache, each CTA keeps an online-softmax partial for its
-//     G query heads, and the last CTA to finish a KV head (atomic ticket) merges the partials in
-//     chunk order (deterministic) into the attention output.
+//     (kv head, chunk). A CTA applies q_norm/k_norm + RoPE itself; the CTA whose chunk holds `pos`
+//     also writes the new K/V into the cache; each CTA publishes an online-softmax partial for its
+//     G query heads as tagged words, and the chunk-0 CTA merges them in chunk order
+//     (deterministic) into the attention output.
+//   * One grid barrier per token (after lm_head: the argmax needs every CTA's partial, and the next
+//     token's K/V reads need the previous token's K/V writes) built from per-CTA release flags.
 //
 // Every wait is bounded in time; on expiry the kernel records an error, stops waiting anywhere
 // (fast-forwards to the end without blocking), waits (bounded) for its own bulk copies in flight
@@ -47,13 +53,17 @@ constexpr int SLOT_BYTES = 24 * 1024;         // bytes per slot
 constexpr int HD = 128;                       // head_dim (the reference's attention kernel also fixes it)
 constexpr int ATT_P = SLOT_BYTES / (2 * HD * 4);  // cached positions per attention ring slot (24)
 constexpr int MAX_G = 3;                      // query heads per KV head
-constexpr int MIN_CHUNK = 8;                  // fewest positions per attention split
-constexpr int APART_STRIDE = HD + 4;          // floats per attention partial: acc[128], m, l, pad
+constexpr int MAX_S = 18;                     // attention chunks per KV head
+constexpr int MIN_CHUNK = 8;                  // fewest positions per attention chunk
+constexpr int APART_STRIDE = HD + 4;          // words per attention partial: acc[128], m, l, pad
+constexpr int GP = 2;                         // tagged word pairs a consumer thread polls at once
 constexpr uint32_t NONE_IDX = 0xFFFFFFFFu;
 
 // error codes written to DecodeParams::err[0]
 enum : int { DERR_NONE = 0, DERR_TIMEOUT_GRID = 1, DERR_TIMEOUT_FULL = 2, DERR_TIMEOUT_EMPTY = 3,
-             DERR_TIMEOUT_KV = 4, DERR_BAD_TOKEN = 5, DERR_TIMEOUT_DRAIN = 6 };
+             DERR_TIMEOUT_KV = 4, DERR_BAD_TOKEN = 5, DERR_TIMEOUT_DRAIN = 6, DERR_TIMEOUT_DATA = 7 };
+
+typedef unsigned long long u64;
 
 struct DecodeParams {
     // weights (bf16 bit patterns)
@@ -66,18 +76,18 @@ struct DecodeParams {
     float* kc;
     float* vc;
     const float2* rope;
-    // scratch
-    float* x;                    // [H] residual stream
-    float* qkv;                  // [QD + 2*KVD] raw projections
-    float* att;                  // [QD] attention output
-    float* hbuf;                 // [I] SiLU(gate)*up
-    float* apart;                // [KVH][S][G][APART_STRIDE]
-    unsigned* acount;            // [KVH] arrival tickets (returned to 0 by the last arriver)
-    float* am_val;               // [grid] argmax partials
+    // tagged activation words {f32 value | tag << 32}
+    u64* x;                      // [H] residual stream
+    u64* qkv;                    // [QD + 2*KVD] raw projections
+    u64* att;                    // [QD] attention output
+    u64* hbuf;                   // [I] SiLU(gate)*up
+    u64* apart;                  // [KVH][S][G][APART_STRIDE] attention partials
+    // argmax partials and the per-token barrier
+    float* am_val;               // [grid]
     unsigned* am_idx;            // [grid]
     int* nan0;                   // logits[0] is NaN (the CPU argmax then returns 0)
-    unsigned long long* flags;   // [grid] barrier flags
-    int* err;                    // [4] code, cta, barrier/piece, detail
+    u64* flags;                  // [grid] barrier flags: epoch << 32 | tokens finished
+    int* err;                    // [4] code, cta, where, detail
     float* logits;               // [V] or null (decode skips it)
     // tokens
     const uint32_t* tok_in;      // step 0 input token (device memory)
@@ -90,9 +100,10 @@ struct DecodeParams {
     int start_pos, steps;
     unsigned epoch;
     float eps, scale;
-    int S;                       // attention splits per KV head
+    int S;                       // attention chunks per KV head (<= MAX_S)
     int part_cap;                // floats in the shared partial-sum buffer
     int xs_cap;                  // floats in the shared activation buffer
+    int xloc_cap;                // floats in the shared residual-rows buffer
     long long timeout_ns;
 };
 
@@ -150,19 +161,20 @@ __device__ inline AttnItem attn_item(const DecodeParams& p, int cta, int pos) {
 }
 
 struct Smem {
+    GemvGeo geo[5];              // this CTA's rows of phases A (q|k|v), C (o), D (gate|up), E (down), F (lm_head)
     float qs[MAX_G][HD];
     float ks[HD];
     float vs[HD];
     float sc[2][MAX_G][ATT_P];
+    float ml[MAX_S][MAX_G][2];   // attention partials' (m, l) gathered by the merging CTA
     float red[64];
     float redv[NCW];
     unsigned redi[NCW];
     uint64_t full[NSLOT];
     uint64_t empty[NSLOT];
-    uint32_t progress;   // grid barriers passed by this CTA's consumers
+    uint32_t progress;   // tokens whose end-of-token barrier this CTA's consumers have passed
     int abort;           // set once any wait expired
     unsigned token;
-    int is_last;
 };
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -190,6 +202,10 @@ __device__ __forceinline__ bool am_better(float av, unsigned ai, float bv, unsig
     return av > bv || (av == bv && ai < bi);
 }
 
+__device__ __forceinline__ uint32_t word_tag(u64 w) { return (uint32_t)(w >> 32); }
+__device__ __forceinline__ float word_val(u64 w) { return __uint_as_float((uint32_t)w); }
+__device__ __forceinline__ u64 tagged(float v, uint32_t tag) { return ((u64)tag << 32) | __float_as_uint(v); }
+
 class Decoder {
 public:
     const DecodeParams& p;
@@ -197,18 +213,21 @@ public:
     uint8_t* ring;
     float* xs;
     float* part;
+    float* xloc;
     int cta, n, warp, lane, tid;
     int QD, KVD, G, QKVR;
-    GemvGeo gA, gC, gD, gE, gF;
-    uint32_t bar_no = 0;   // grid barriers passed / published so far in this launch
+    // the CTA's static row partition per phase lives in shared memory (computed once by thread 0
+    // in init_geometry), not in registers
+    const GemvGeo &gA, &gC, &gD, &gE, &gF;
     uint32_t it = 0;       // ring pieces consumed (consumer) or walked (producer)
     uint32_t n_issued = 0; // producer: pieces whose copies were issued (all before any abort)
 
     __device__ Decoder(const DecodeParams& p_, Smem& sm_, uint8_t* dyn)
-        : p(p_), sm(sm_) {
+        : p(p_), sm(sm_), gA(sm_.geo[0]), gC(sm_.geo[1]), gD(sm_.geo[2]), gE(sm_.geo[3]), gF(sm_.geo[4]) {
         ring = dyn;
         xs = reinterpret_cast<float*>(dyn + NSLOT * SLOT_BYTES);
         part = xs + p.xs_cap;
+        xloc = part + p.part_cap;
         cta = blockIdx.x;
         n = gridDim.x;
         tid = threadIdx.x;
@@ -218,15 +237,27 @@ public:
         KVD = p.NKV * HD;
         G = p.NQ / p.NKV;
         QKVR = QD + 2 * KVD;
-        const long long offC = (long long)QKVR * p.H;
+    }
+
+    // one thread, before the CTA-wide barrier that follows mbarrier initialisation
+    __device__ static void init_geometry(const DecodeParams& p, Smem& sm) {
+        const int cta = blockIdx.x, n = gridDim.x;
+        const long long QD = (long long)p.NQ * HD, KVD = (long long)p.NKV * HD, QKVR = QD + 2 * KVD;
+        const long long offC = QKVR * p.H;
         const long long offD = offC + (long long)p.H * QD;
         const long long offE = offD + 2LL * p.I * p.H;
-        gA = make_geo(QKVR, p.H, cta, n, 0, 0);
-        gC = make_geo(p.H, QD, cta, n, offC, 0);
-        gD = make_geo(2LL * p.I, p.H, cta, n, offD, 1);
-        gE = make_geo(p.H, p.I, cta, n, offE, 0);
-        gF = make_geo(p.V, p.H, cta, n, 0, 0);
+        sm.geo[0] = make_geo(QKVR, p.H, cta, n, 0, 0);
+        sm.geo[1] = make_geo(p.H, (int)QD, cta, n, offC, 0);
+        sm.geo[2] = make_geo(2LL * p.I, p.H, cta, n, offD, 1);
+        sm.geo[3] = make_geo(p.H, p.I, cta, n, offE, 0);
+        sm.geo[4] = make_geo(p.V, p.H, cta, n, 0, 0);
     }
+
+    // phase sequence numbers within the launch -> tags (12 bits of epoch, 20 bits of sequence)
+    __device__ uint32_t seq(int step, int l, int ph) const {  // ph: 1 A, 2 B, 3 C, 4 D, 5 E
+        return (uint32_t)step * (uint32_t)(5 * p.L + 1) + (uint32_t)(5 * l + ph);
+    }
+    __device__ uint32_t tag(uint32_t sq) const { return ((p.epoch & 0xFFFu) << 20) | (sq & 0xFFFFFu); }
 
     // ------------------------------------------------------------------ errors and waits
     __device__ bool aborted() const { return *reinterpret_cast<volatile const int*>(&sm.abort) != 0; }
@@ -240,64 +271,88 @@ public:
         }
     }
 
+    // called between unsuccessful polls; returns true when the caller must stop waiting
+    __device__ bool wait_expired(uint32_t& spins, uint64_t& t0, int code, int where) {
+        ++spins;
+        if (spins == 8) t0 = globaltimer_ns();
+        if (spins > 8 && (spins & 15) == 0) {
+            if (aborted()) return true;
+            if (ld_volatile_s32(p.err) != 0) { *reinterpret_cast<volatile int*>(&sm.abort) = 1; return true; }
+            if (globaltimer_ns() - t0 > (uint64_t)p.timeout_ns) { fail(code, where); return true; }
+        }
+        return false;
+    }
+
     __device__ bool wait_mbar(uint64_t* bar, uint32_t parity, int code) {
         if (aborted()) return false;
         uint32_t spins = 0;
         uint64_t t0 = 0;
-        while (!mbar_try_wait(bar, parity)) {
-            ++spins;
-            if (spins == 16) t0 = globaltimer_ns();
-            else if (spins > 16 && (spins & 63) == 0) {
-                if (aborted()) return false;
-                if (ld_volatile_s32(p.err) != 0) { *reinterpret_cast<volatile int*>(&sm.abort) = 1; return false; }
-                if (globaltimer_ns() - t0 > (uint64_t)p.timeout_ns) { fail(code, (int)it); return false; }
-            }
-        }
+        while (!mbar_try_wait(bar, parity))
+            if (wait_expired(spins, t0, code, (int)it)) return false;
         return true;
     }
 
-    // consumers: wait until every CTA published barrier `b` (b >= 1), then release all consumers
-    __device__ void grid_wait(uint32_t b) {
+    // xs[0..K) <- values of the tagged words src[0..K) once each carries `tg` (K even, src 16-byte aligned)
+    __device__ void gather(const u64* src, int K, uint32_t tg) {
+        const int npairs = K >> 1;
+        for (int base = 0; base < npairs; base += NCT * GP) {
+            unsigned pending = 0;
+#pragma unroll
+            for (int j = 0; j < GP; j++)
+                if (base + tid + j * NCT < npairs) pending |= 1u << j;
+            uint32_t spins = 0;
+            uint64_t t0 = 0;
+            while (pending && !aborted()) {
+                ulonglong2 w[GP];
+#pragma unroll
+                for (int j = 0; j < GP; j++)
+                    if (pending & (1u << j)) w[j] = ld_relaxed_v2u64(src + 2 * (base + tid + j * NCT));
+#pragma unroll
+                for (int j = 0; j < GP; j++) {
+                    if ((pending & (1u << j)) && word_tag(w[j].x) == tg && word_tag(w[j].y) == tg) {
+                        const int i = 2 * (base + tid + j * NCT);
+                        xs[i] = word_val(w[j].x);
+                        xs[i + 1] = word_val(w[j].y);
+                        pending &= ~(1u << j);
+                    }
+                }
+                if (pending && wait_expired(spins, t0, DERR_TIMEOUT_DATA, (int)tg)) break;
+            }
+        }
+        named_bar_sync(1, NCT);
+    }
+
+    // one end-of-token grid barrier: every CTA has published `done` finished tokens
+    __device__ void token_barrier(uint32_t done) {
+        named_bar_sync(1, NCT);
+        const u64 target = ((u64)p.epoch << 32) | done;
+        if (tid == 0) {
+            fence_acq_rel_gpu();
+            st_relaxed_u64(p.flags + cta, target);
+        }
         if (warp == 0 && !aborted()) {
-            const unsigned long long target = ((unsigned long long)p.epoch << 32) | b;
             uint32_t spins = 0;
             uint64_t t0 = 0;
             for (;;) {
                 bool ok = true;
-                for (int j = lane; j < n; j += 32) ok &= ld_acquire_gpu(p.flags + j) >= target;
-                if (__all_sync(0xFFFFFFFFu, ok)) break;
-                ++spins;
-                if (spins == 64) t0 = globaltimer_ns();
-                if (spins > 64 && (spins & 31) == 0) {
-                    int bad = 0;
-                    if (lane == 0) {
-                        if (ld_volatile_s32(p.err) != 0) bad = 1;
-                        else if (globaltimer_ns() - t0 > (uint64_t)p.timeout_ns) bad = 2;
-                    }
-                    bad = __shfl_sync(0xFFFFFFFFu, bad, 0);
-                    if (bad) {
-                        if (lane == 0) {
-                            if (bad == 2) fail(DERR_TIMEOUT_GRID, (int)b);
-                            else *reinterpret_cast<volatile int*>(&sm.abort) = 1;
-                        }
-                        break;
-                    }
+                u64 v[8];
+#pragma unroll
+                for (int k = 0; k < 8; k++) {
+                    const int j = lane + 32 * k;
+                    v[k] = j < n ? ld_relaxed_u64(p.flags + j) : target;
                 }
+#pragma unroll
+                for (int k = 0; k < 8; k++) ok &= v[k] >= target;
+                for (int j = lane + 256; j < n; j += 32) ok &= ld_relaxed_u64(p.flags + j) >= target;
+                if (__all_sync(0xFFFFFFFFu, ok)) break;
+                int stop = 0;
+                if (lane == 0) stop = wait_expired(spins, t0, DERR_TIMEOUT_GRID, (int)done);
+                if (__shfl_sync(0xFFFFFFFFu, stop, 0)) break;
             }
+            fence_acq_rel_gpu();
         }
         named_bar_sync(1, NCT);
-        // after the barrier every poller's acquire is ordered before this release
-        if (tid == 0) st_release_cta_shared(&sm.progress, b);
-    }
-
-    // consumers: all epilogue writes done -> publish barrier number ++bar_no
-    __device__ void grid_arrive() {
-        named_bar_sync(1, NCT);
-        ++bar_no;
-        if (tid == 0) {
-            __threadfence();
-            st_release_gpu(p.flags + cta, ((unsigned long long)p.epoch << 32) | bar_no);
-        }
+        if (tid == 0) st_release_cta_shared(&sm.progress, done);
     }
 
     // ------------------------------------------------------------------ consumer helpers
@@ -314,27 +369,27 @@ public:
         return sm.red[32];
     }
 
-    // xs[i] = src[i] * (1/sqrt(mean(src^2) + eps)) * w[i]   (cpu_inference.rs:189-194)
-    // src is the residual stream x, or (from_embed) the embedding row of `token`, in which case the
-    // CTA also initialises its own rows [x_r0, x_r1) of the global residual stream.
-    __device__ void norm_prologue(const uint16_t* w, bool from_embed, unsigned token) {
+    // xs <- rmsnorm(src) * w  (cpu_inference.rs:189-194). src is the tagged residual stream, or
+    // (from_embed) the embedding row of `token`, in which case the CTA also initialises its own
+    // residual rows xloc from that row.
+    __device__ void norm_prologue(const uint16_t* w, bool from_embed, unsigned token, uint32_t tg) {
         const int H = p.H;
-        float ss = 0.f;
-        const uint16_t* erow = p.embed + (size_t)token * H;
-        for (int i = tid; i < H; i += NCT) {
-            float v = from_embed ? bf16_to_f32(__ldg(erow + i)) : __ldcg(p.x + i);
-            xs[i] = v;
-            ss = fmaf(v, v, ss);
-            if (from_embed && i >= gC.r0 && i < gC.r1) __stcg(p.x + i, v);
+        if (from_embed) {
+            const uint16_t* erow = p.embed + (size_t)token * H;
+            for (int i = tid; i < H; i += NCT) {
+                const float v = bf16_to_f32(__ldg(erow + i));
+                xs[i] = v;
+                if (i >= gC.r0 && i < gC.r1) xloc[i - gC.r0] = v;
+            }
+            named_bar_sync(1, NCT);
+        } else {
+            gather(p.x, H, tg);
         }
+        float ss = 0.f;
+        for (int i = tid; i < H; i += NCT) ss = fmaf(xs[i], xs[i], ss);
         const float tot = block_sum(ss);
         const float s = 1.0f / sqrtf(tot / (float)H + p.eps);
         for (int i = tid; i < H; i += NCT) xs[i] = xs[i] * s * bf16_to_f32(__ldg(w + i));
-        named_bar_sync(1, NCT);
-    }
-
-    __device__ void load_prologue(const float* src, int K) {
-        for (int i = tid; i < K; i += NCT) xs[i] = __ldcg(src + i);
         named_bar_sync(1, NCT);
     }
 
@@ -387,10 +442,26 @@ public:
     }
 
     // ------------------------------------------------------------------ attention (phase B)
-    // per-head RMSNorm (q_norm/k_norm) then rotate-half RoPE, one warp per 128-vector
+    // one warp: gather a tagged 128-vector, per-head RMSNorm (q_norm/k_norm), rotate-half RoPE
     // (cpu_inference.rs:134-138, :196-215; the table is the one MetalKVCache builds, :141-154)
-    __device__ void head_norm_rope(const float* src, const uint16_t* nw, const float2* rrow, float* dst) {
-        float4 v = __ldcg(reinterpret_cast<const float4*>(src) + lane);
+    __device__ float4 gather_head(const u64* src, uint32_t tg) {
+        uint32_t spins = 0;
+        uint64_t t0 = 0;
+        ulonglong2 a = make_ulonglong2(0, 0), b = make_ulonglong2(0, 0);
+        bool ok = false;
+        while (!aborted()) {
+            a = ld_relaxed_v2u64(src + lane * 4);
+            b = ld_relaxed_v2u64(src + lane * 4 + 2);
+            ok = word_tag(a.x) == tg && word_tag(a.y) == tg && word_tag(b.x) == tg && word_tag(b.y) == tg;
+            if (__all_sync(0xFFFFFFFFu, ok)) break;
+            int stop = 0;
+            if (lane == 0) stop = wait_expired(spins, t0, DERR_TIMEOUT_DATA, (int)tg);
+            if (__shfl_sync(0xFFFFFFFFu, stop, 0)) break;
+        }
+        return make_float4(word_val(a.x), word_val(a.y), word_val(b.x), word_val(b.y));
+    }
+
+    __device__ void head_norm_rope(float4 v, const uint16_t* nw, const float2* rrow, float* dst) {
         float ss = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
         ss = warp_sum(ss);
         const float s = 1.0f / sqrtf(ss / (float)HD + p.eps);
@@ -414,10 +485,13 @@ public:
                                float& m, float& l, float& acc) {
         for (int pp = warp; pp < np; pp += NCW) {
             const float4 k4 = reinterpret_cast<const float4*>(Kb + pp * HD)[lane];
-            for (int h = 0; h < G; h++) {
-                float d = q4[h].x * k4.x + q4[h].y * k4.y + q4[h].z * k4.z + q4[h].w * k4.w;
-                d = warp_sum(d);
-                if (lane == 0) sm.sc[buf][h][pp] = d * p.scale;
+#pragma unroll
+            for (int h = 0; h < MAX_G; h++) {
+                if (h < G) {
+                    float d = q4[h].x * k4.x + q4[h].y * k4.y + q4[h].z * k4.z + q4[h].w * k4.w;
+                    d = warp_sum(d);
+                    if (lane == 0) sm.sc[buf][h][pp] = d * p.scale;
+                }
             }
         }
         named_bar_sync(1, NCT);
@@ -438,27 +512,29 @@ public:
         }
     }
 
-    __device__ void attention_consume(int l, int pos) {
+    __device__ void attention_consume(int step, int l, int pos) {
         const AttnItem a = attn_item(p, cta, pos);
         if (!a.active) return;   // uniform over the CTA
         const uint16_t* nrm = p.layer_n + (size_t)l * p.norm_stride;
         const uint16_t* qn = nrm + 2 * p.H;
         const uint16_t* kn = qn + HD;
         const float2* rrow = p.rope + (size_t)pos * (HD / 2);
+        const uint32_t tgA = tag(seq(step, l, 1)), tgB = tag(seq(step, l, 2));
         // q heads g*G .. g*G+G-1, and (last chunk) this position's k and v
-        if (warp < G) head_norm_rope(p.qkv + (size_t)(a.g * G + warp) * HD, qn, rrow, sm.qs[warp]);
+        if (warp < G) head_norm_rope(gather_head(p.qkv + (size_t)(a.g * G + warp) * HD, tgA), qn, rrow, sm.qs[warp]);
         if (a.has_cur) {
-            if (warp == G) head_norm_rope(p.qkv + QD + (size_t)a.g * HD, kn, rrow, sm.ks);
-            if (warp == G + 1) reinterpret_cast<float4*>(sm.vs)[lane] =
-                __ldcg(reinterpret_cast<const float4*>(p.qkv + QD + KVD + (size_t)a.g * HD) + lane);
+            if (warp == G) head_norm_rope(gather_head(p.qkv + QD + (size_t)a.g * HD, tgA), kn, rrow, sm.ks);
+            if (warp == G + 1)
+                reinterpret_cast<float4*>(sm.vs)[lane] = gather_head(p.qkv + QD + KVD + (size_t)a.g * HD, tgA);
         }
         named_bar_sync(1, NCT);
         if (a.has_cur && tid < 2 * HD) {  // append K/V at slot `pos` (cpu_inference.rs:140-141)
             const size_t off = (((size_t)l * p.NKV + a.g) * p.max_seq + pos) * HD;
-            if (tid < HD) __stcg(p.kc + off + tid, sm.ks[tid]);
-            else __stcg(p.vc + off + tid - HD, sm.vs[tid - HD]);
+            if (tid < HD) p.kc[off + tid] = sm.ks[tid];
+            else p.vc[off + tid - HD] = sm.vs[tid - HD];
         }
         float4 q4[MAX_G];
+#pragma unroll
         for (int h = 0; h < MAX_G; h++)
             q4[h] = h < G ? reinterpret_cast<const float4*>(sm.qs[h])[lane] : make_float4(0, 0, 0, 0);
         float m = -INFINITY, lsum = 0.f, acc = 0.f;
@@ -481,38 +557,81 @@ public:
             attn_block(sm.ks, sm.vs, 1, buf, q4, m, lsum, acc);
             buf ^= 1;
         }
-        // publish this chunk's partial, then the last chunk of the KV head merges them
+        const size_t head_base = (size_t)a.g * p.S * G;  // partial (s, h) at apart[((head_base + s*G + h) * APART_STRIDE]
+        if (a.s != 0) {
+            // publish this chunk's partial as tagged words for the chunk-0 CTA of this KV head
+            if (tid < G * HD) {
+                const int h = tid >> 7, d = tid & (HD - 1);
+                u64* dst = p.apart + (head_base + (size_t)a.s * G + h) * APART_STRIDE;
+                st_relaxed_u64(dst + d, tagged(acc, tgB));
+                if (d == 0) {
+                    st_relaxed_u64(dst + HD, tagged(m, tgB));
+                    st_relaxed_u64(dst + HD + 1, tagged(lsum, tgB));
+                }
+            }
+            return;
+        }
+        // chunk 0 merges the partials of chunks 0..S_eff-1 in chunk order. Every thread keeps its
+        // polls in flight together: an accumulator thread (h, d) polls word d of chunks 1.., and the
+        // first (S_eff-1)*G*2 threads also poll one (m or l) word each (bit 0 of `pending`).
+        if (tid < G * HD && (tid & (HD - 1)) == 0) {
+            sm.ml[0][tid >> 7][0] = m;
+            sm.ml[0][tid >> 7][1] = lsum;
+        }
+        float av[MAX_S];
+        av[0] = acc;
+        {
+            const int h = tid >> 7, d = tid & (HD - 1);
+            uint32_t pending = 0;
+            if (tid < G * HD) {
+#pragma unroll
+                for (int s = 1; s < MAX_S; s++)
+                    if (s < a.S_eff) pending |= 1u << s;
+            }
+            const u64* mlsrc = nullptr;
+            float* mldst = nullptr;
+            if (tid < (a.S_eff - 1) * G * 2) {
+                const int s = 1 + tid / (2 * G), hh = (tid >> 1) % G, which = tid & 1;
+                mlsrc = p.apart + (head_base + (size_t)s * G + hh) * APART_STRIDE + HD + which;
+                mldst = &sm.ml[s][hh][which];
+                pending |= 1u;
+            }
+            uint32_t spins = 0;
+            uint64_t t0 = 0;
+            while (pending && !aborted()) {
+                u64 w[MAX_S];
+                if (pending & 1u) w[0] = ld_relaxed_u64(mlsrc);
+#pragma unroll
+                for (int s = 1; s < MAX_S; s++)
+                    if (pending & (1u << s)) w[s] = ld_relaxed_u64(p.apart + (head_base + (size_t)s * G + h) * APART_STRIDE + d);
+                if ((pending & 1u) && word_tag(w[0]) == tgB) {
+                    *mldst = word_val(w[0]);
+                    pending &= ~1u;
+                }
+#pragma unroll
+                for (int s = 1; s < MAX_S; s++)
+                    if ((pending & (1u << s)) && word_tag(w[s]) == tgB) {
+                        av[s] = word_val(w[s]);
+                        pending &= ~(1u << s);
+                    }
+                if (pending && wait_expired(spins, t0, DERR_TIMEOUT_DATA, (int)tgB)) break;
+            }
+        }
+        named_bar_sync(1, NCT);
         if (tid < G * HD) {
             const int h = tid >> 7, d = tid & (HD - 1);
-            float* dst = p.apart + ((size_t)(a.g * p.S + a.s) * G + h) * APART_STRIDE;
-            __stcg(dst + d, acc);
-            if (d == 0) { __stcg(dst + HD, m); __stcg(dst + HD + 1, lsum); }
-        }
-        named_bar_sync(1, NCT);
-        if (tid == 0) {
-            __threadfence();
-            const unsigned old = atomicAdd(p.acount + a.g, 1u);
-            const int last = (old == (unsigned)(a.S_eff - 1));
-            if (last) {
-                p.acount[a.g] = 0u;
-                __threadfence();
-            }
-            sm.is_last = last;
-        }
-        named_bar_sync(1, NCT);
-        if (sm.is_last && tid < G * HD) {
-            const int h = tid >> 7, d = tid & (HD - 1);
             float M = -INFINITY;
-            for (int s = 0; s < a.S_eff; s++)
-                M = fmaxf(M, __ldcg(p.apart + ((size_t)(a.g * p.S + s) * G + h) * APART_STRIDE + HD));
+            for (int s = 0; s < a.S_eff; s++) M = fmaxf(M, sm.ml[s][h][0]);
             float Lt = 0.f, O = 0.f;
-            for (int s = 0; s < a.S_eff; s++) {
-                const float* src = p.apart + ((size_t)(a.g * p.S + s) * G + h) * APART_STRIDE;
-                const float w = expf(__ldcg(src + HD) - M);
-                Lt = fmaf(w, __ldcg(src + HD + 1), Lt);
-                O = fmaf(w, __ldcg(src + d), O);
+#pragma unroll
+            for (int s = 0; s < MAX_S; s++) {
+                if (s < a.S_eff) {
+                    const float w = expf(sm.ml[s][h][0] - M);
+                    Lt = fmaf(w, sm.ml[s][h][1], Lt);
+                    O = fmaf(w, av[s], O);
+                }
             }
-            __stcg(p.att + (size_t)(a.g * G + h) * HD + d, O / Lt);
+            st_relaxed_u64(p.att + (size_t)(a.g * G + h) * HD + d, tagged(O / Lt, tgB));
         }
     }
 
@@ -545,7 +664,7 @@ public:
         }
     }
 
-    // after the lm_head barrier: every CTA reduces the partials to the same next token
+    // after the end-of-token barrier: every CTA reduces the partials to the same next token
     __device__ unsigned argmax_combine() {
         if (warp == 0) {
             float bv = -INFINITY;
@@ -571,6 +690,18 @@ public:
         return sm.token;
     }
 
+    __device__ void store_rows(u64* dst, const GemvGeo& g, uint32_t tg) {
+        for (int i = tid; i < g.r1 - g.r0; i += NCT) st_relaxed_u64(dst + g.r0 + i, tagged(row_value(g, i), tg));
+    }
+
+    __device__ void residual_rows(const GemvGeo& g, uint32_t tg) {  // x[r] += y[r] on this CTA's rows
+        for (int i = tid; i < g.r1 - g.r0; i += NCT) {
+            const float v = xloc[i] + row_value(g, i);
+            xloc[i] = v;
+            st_relaxed_u64(p.x + g.r0 + i, tagged(v, tg));
+        }
+    }
+
     // ------------------------------------------------------------------ consumer main loop
     __device__ void consume() {
         unsigned token = __ldcg(p.tok_in);
@@ -582,47 +713,36 @@ public:
             const int pos = p.start_pos + step;
             for (int l = 0; l < p.L; l++) {
                 const uint16_t* nrm = p.layer_n + (size_t)l * p.norm_stride;
-                // A: rmsnorm -> q|k|v
-                if (l > 0) grid_wait(bar_no);
-                norm_prologue(nrm, l == 0, token);
+                // A: rmsnorm(x) -> q|k|v rows
+                norm_prologue(nrm, l == 0, token, l == 0 ? 0u : tag(seq(step, l - 1, 5)));
                 gemv_consume(gA);
-                for (int i = tid; i < gA.r1 - gA.r0; i += NCT) __stcg(p.qkv + gA.r0 + i, row_value(gA, i));
-                grid_arrive();
-                // B: q/k norm + rope, KV append, attention
-                grid_wait(bar_no);
-                attention_consume(l, pos);
-                grid_arrive();
+                store_rows(p.qkv, gA, tag(seq(step, l, 1)));
+                // B: q/k norm + rope, KV append, attention (partials, then the chunk-0 merge)
+                attention_consume(step, l, pos);
                 // C: o_proj + residual
-                grid_wait(bar_no);
-                load_prologue(p.att, QD);
+                gather(p.att, QD, tag(seq(step, l, 2)));
                 gemv_consume(gC);
-                for (int i = tid; i < gC.r1 - gC.r0; i += NCT)
-                    __stcg(p.x + gC.r0 + i, __ldcg(p.x + gC.r0 + i) + row_value(gC, i));
-                grid_arrive();
-                // D: rmsnorm -> gate|up -> silu(gate) * up
-                grid_wait(bar_no);
-                norm_prologue(nrm + p.H, false, 0);
+                residual_rows(gC, tag(seq(step, l, 3)));
+                // D: rmsnorm(x) -> gate|up -> silu(gate) * up
+                norm_prologue(nrm + p.H, false, 0, tag(seq(step, l, 3)));
                 gemv_consume(gD);
-                for (int i = tid; i < (gD.r1 - gD.r0) / 2; i += NCT) {
-                    const float gt = row_value(gD, 2 * i), up = row_value(gD, 2 * i + 1);
-                    __stcg(p.hbuf + gD.r0 / 2 + i, gt / (1.0f + expf(-gt)) * up);
+                {
+                    const uint32_t tg = tag(seq(step, l, 4));
+                    for (int i = tid; i < (gD.r1 - gD.r0) / 2; i += NCT) {
+                        const float gt = row_value(gD, 2 * i), up = row_value(gD, 2 * i + 1);
+                        st_relaxed_u64(p.hbuf + gD.r0 / 2 + i, tagged(gt / (1.0f + expf(-gt)) * up, tg));
+                    }
                 }
-                grid_arrive();
                 // E: down_proj + residual
-                grid_wait(bar_no);
-                load_prologue(p.hbuf, p.I);
+                gather(p.hbuf, p.I, tag(seq(step, l, 4)));
                 gemv_consume(gE);
-                for (int i = tid; i < gE.r1 - gE.r0; i += NCT)
-                    __stcg(p.x + gE.r0 + i, __ldcg(p.x + gE.r0 + i) + row_value(gE, i));
-                grid_arrive();
+                residual_rows(gE, tag(seq(step, l, 5)));
             }
-            // F: final rmsnorm -> lm_head -> argmax partials
-            grid_wait(bar_no);
-            norm_prologue(p.final_norm, false, 0);
+            // F: final rmsnorm -> lm_head -> argmax partials -> end-of-token barrier -> next token
+            norm_prologue(p.final_norm, false, 0, tag(seq(step, p.L - 1, 5)));
             gemv_consume(gF);
             lm_epilogue();
-            grid_arrive();
-            grid_wait(bar_no);
+            token_barrier((uint32_t)step + 1);
             token = argmax_combine();
             if (cta == 0 && tid == 0 && !aborted()) {
                 if (p.tok_out) p.tok_out[step + 1] = token;
@@ -657,26 +777,20 @@ public:
         }
     }
 
-    // barrier number after which step `step`'s attention of layer `l` is globally complete
-    __device__ uint32_t attn_barrier(int step, int l) const {
-        return (uint32_t)step * (uint32_t)(5 * p.L + 1) + (uint32_t)(5 * l + 2);
-    }
-
     __device__ void attn_produce(int step, int l, int pos) {
         const AttnItem a = attn_item(p, cta, pos);
         if (!a.active) return;
         const int tc1 = a.has_cur ? pos : a.t1;
         if (a.t0 >= tc1) return;
-        // K/V rows up to pos-1 are written by other CTAs in earlier steps of this launch: wait until
-        // this CTA's consumers have seen that step's attention barrier, then order the async-proxy
-        // reads after it.
-        if (step > 0 && !aborted()) {
-            const uint32_t need = attn_barrier(step - 1, l);
-            uint64_t t0 = globaltimer_ns();
-            while (ld_acquire_cta_shared(&sm.progress) < need) {
-                if (aborted()) break;
-                if (globaltimer_ns() - t0 > (uint64_t)p.timeout_ns) { fail(DERR_TIMEOUT_KV, (int)need); break; }
-                __nanosleep(64);
+        // K/V rows of earlier positions may have been written by other CTAs in earlier steps of this
+        // launch: wait until this CTA's consumers have passed the previous token's barrier, then order
+        // the async-proxy reads after it.
+        if (step > 0 && !aborted() && l == 0) {
+            uint32_t spins = 0;
+            uint64_t t0 = 0;
+            while (ld_acquire_cta_shared(&sm.progress) < (uint32_t)step) {
+                if (wait_expired(spins, t0, DERR_TIMEOUT_KV, step)) break;
+                __nanosleep(32);
             }
             fence_proxy_async_global();
         }

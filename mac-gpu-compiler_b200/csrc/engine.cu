@@ -91,7 +91,8 @@ int* device_err_word_for(int device) {
 namespace qw {
 
 // the persistent decode kernel (device code in decode_kernel.cuh)
-__global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
+// 416 threads x 152 registers fit one CTA per SM (65536 registers)
+__global__ void __maxnreg__(152) decode_kernel(const __grid_constant__ DecodeParams p) {
     __shared__ Smem sm;
     extern __shared__ __align__(128) uint8_t dyn[];
     if (threadIdx.x == 0) {
@@ -102,7 +103,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
         sm.progress = 0;
         sm.abort = 0;
         sm.token = 0;
-        sm.is_last = 0;
+        Decoder::init_geometry(p, sm);
         fence_mbar_init();
     }
     __syncthreads();
@@ -129,11 +130,11 @@ struct qw_model {
     long long layer_stride = 0, norm_stride = 0;
     // scratch (one allocation)
     uint8_t* d_scratch = nullptr;
-    float *d_x = nullptr, *d_qkv = nullptr, *d_att = nullptr, *d_h = nullptr, *d_apart = nullptr, *d_am_val = nullptr,
-          *d_logits = nullptr;
-    unsigned *d_acount = nullptr, *d_am_idx = nullptr;
+    u64 *d_x = nullptr, *d_qkv = nullptr, *d_att = nullptr, *d_h = nullptr, *d_apart = nullptr;  // tagged words
+    float *d_am_val = nullptr, *d_logits = nullptr;
+    unsigned* d_am_idx = nullptr;
     int *d_nan0 = nullptr, *d_err = nullptr;
-    unsigned long long* d_flags = nullptr;
+    u64* d_flags = nullptr;
     // token ring (device) and its mapped host mirror
     uint32_t* d_tok = nullptr;
     size_t tok_cap = 0;
@@ -145,10 +146,9 @@ struct qw_model {
     uint32_t* h_stage = nullptr; // pinned, 1 token
     float* h_logits = nullptr;   // pinned [vocab]
     unsigned epoch = 0;
-    int S = 0, part_cap = 0, xs_cap = 0;
+    int S = 0, part_cap = 0, xs_cap = 0, xloc_cap = 0;
     size_t dyn_smem = 0;
     long long timeout_ns = 0;
-    bool dirty = false;
 };
 
 // A cache never dereferences its model after qw_cache_new: it keeps what it needs (device,
@@ -193,10 +193,6 @@ int ensure_token_capacity(qw_model* m, size_t n) {
 int launch_decode(qw_model* m, qw_cache* c, const uint32_t* tok_in, uint32_t* tok_out, bool stream_to_host,
                   float* logits, size_t start_pos, size_t steps, cudaStream_t s) {
     const ModelConfig& g = m->cfg;
-    if (m->dirty) {
-        QW_CUDA(cudaMemsetAsync(m->d_acount, 0, g.kv_heads * sizeof(unsigned), s));
-        m->dirty = false;
-    }
     DecodeParams p{};
     p.layer_w = m->d_layer_w;
     p.layer_n = m->d_layer_n;
@@ -211,7 +207,6 @@ int launch_decode(qw_model* m, qw_cache* c, const uint32_t* tok_in, uint32_t* to
     p.att = m->d_att;
     p.hbuf = m->d_h;
     p.apart = m->d_apart;
-    p.acount = m->d_acount;
     p.am_val = m->d_am_val;
     p.am_idx = m->d_am_idx;
     p.nan0 = m->d_nan0;
@@ -239,6 +234,7 @@ int launch_decode(qw_model* m, qw_cache* c, const uint32_t* tok_in, uint32_t* to
     p.S = m->S;
     p.part_cap = m->part_cap;
     p.xs_cap = m->xs_cap;
+    p.xloc_cap = m->xloc_cap;
     p.timeout_ns = m->timeout_ns;
     void* args[] = {&p};
     cudaError_t e = cudaLaunchCooperativeKernel((const void*)decode_kernel, dim3(m->nctas), dim3(NTHREADS), args,
@@ -253,7 +249,6 @@ int check_device_err(qw_model* m) {
     QW_CUDA(cudaMemcpy(err, m->d_err, sizeof err, cudaMemcpyDeviceToHost));
     if (err[0] == 0 && err[3] == 0) return QW_OK;
     QW_CUDA(cudaMemset(m->d_err, 0, sizeof err));
-    m->dirty = true;
     char buf[256];
     std::snprintf(buf, sizeof buf, "device: %s (cta %d, at %d)%s", derr_name(err[0]), err[1], err[2],
                   err[3] ? "; a bulk-copy drain also expired" : "");
@@ -306,9 +301,13 @@ int qw_load(const char* path, int device, qw_model** out) {
     m->timeout_ns = timeout_ns_from_env();
     int nctas = prop.multiProcessorCount;
     if (const char* e = std::getenv("QW_CTAS")) nctas = std::max(1, std::min(nctas, std::atoi(e)));
+    // Buffers are reused across phases on the premise that every CTA contributes to every GEMV
+    // phase (so a CTA that sees a phase's complete input knows every CTA has finished reading the
+    // previous contents): every CTA must own at least one row of q|k|v, o/down and gate|up.
+    nctas = (int)std::min<uint64_t>({(uint64_t)nctas, c.hidden, c.inter, c.heads * c.head_dim + 2 * c.kv_heads * c.head_dim});
     if ((uint64_t)nctas < c.kv_heads) { delete m; return set_err(QW_ERR_UNSUPPORTED, "fewer SMs than KV heads"); }
     m->nctas = nctas;
-    m->S = nctas / (int)c.kv_heads;
+    m->S = std::min(MAX_S, nctas / (int)c.kv_heads);
 
     const uint64_t H = c.hidden, I = c.inter, QD = c.heads * c.head_dim, KVD = c.kv_heads * c.head_dim;
     const uint64_t QKVR = QD + 2 * KVD;
@@ -380,7 +379,8 @@ int qw_load(const char* path, int device, qw_model** out) {
     uint64_t pc = std::max({phase_cap(QKVR, H), phase_cap(H, QD), phase_cap(2 * I, H) + 2, phase_cap(H, I), phase_cap(c.vocab, H)});
     m->part_cap = (int)align_up(pc, 4);
     m->xs_cap = (int)align_up(std::max({H, QD, I}), 4);
-    m->dyn_smem = (size_t)NSLOT * SLOT_BYTES + ((size_t)m->part_cap + m->xs_cap) * 4;
+    m->xloc_cap = (int)align_up(ceil_div(H, nctas) + 2, 4);
+    m->dyn_smem = (size_t)NSLOT * SLOT_BYTES + ((size_t)m->part_cap + m->xs_cap + m->xloc_cap) * 4;
     if (m->dyn_smem + sizeof(Smem) > (size_t)prop.sharedMemPerBlockOptin)
         return fail(QW_ERR_UNSUPPORTED, "model too large for the kernel's shared-memory plan (vocab or widths)");
     if (cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->dyn_smem) != cudaSuccess)
@@ -390,10 +390,10 @@ int qw_load(const char* path, int device, qw_model** out) {
         return fail(QW_ERR_UNSUPPORTED, "decode kernel does not fit on an SM");
 
     struct Piece { size_t bytes; void** dst; };
-    const size_t sz_apart = (size_t)c.kv_heads * m->S * G * APART_STRIDE * 4;
+    const size_t sz_apart = (size_t)c.kv_heads * m->S * G * APART_STRIDE * 8;
     std::vector<Piece> pieces = {
-        {H * 4, (void**)&m->d_x}, {QKVR * 4, (void**)&m->d_qkv}, {QD * 4, (void**)&m->d_att},
-        {I * 4, (void**)&m->d_h}, {sz_apart, (void**)&m->d_apart}, {c.kv_heads * 4, (void**)&m->d_acount},
+        {H * 8, (void**)&m->d_x}, {QKVR * 8, (void**)&m->d_qkv}, {QD * 8, (void**)&m->d_att},
+        {I * 8, (void**)&m->d_h}, {sz_apart, (void**)&m->d_apart},
         {(size_t)nctas * 4, (void**)&m->d_am_val}, {(size_t)nctas * 4, (void**)&m->d_am_idx}, {16, (void**)&m->d_nan0},
         {(size_t)nctas * 8, (void**)&m->d_flags}, {16, (void**)&m->d_err}, {c.vocab * 4, (void**)&m->d_logits}};
     size_t scratch = 0;

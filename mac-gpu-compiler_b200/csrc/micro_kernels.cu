@@ -33,6 +33,7 @@ gemv_kernel(const __grid_constant__ DecodeParams p, const uint16_t* w, const flo
         }
         sm.progress = 0;
         sm.abort = 0;
+        Decoder::init_geometry(p, sm);
         fence_mbar_init();
     }
     __syncthreads();
@@ -45,7 +46,8 @@ gemv_kernel(const __grid_constant__ DecodeParams p, const uint16_t* w, const flo
         }
         return;
     }
-    d.load_prologue(x, cols);
+    for (int i = d.tid; i < cols; i += NCT) d.xs[i] = x[i];
+    named_bar_sync(1, NCT);
     d.gemv_consume(g);
     for (int i = d.tid; i < g.r1 - g.r0; i += NCT) y[g.r0 + i] = d.row_value(g, i);
 }
@@ -171,8 +173,9 @@ int qw_gemv_bf16(int device, const uint16_t* d_w, const float* d_x, float* d_y, 
     p.S = 1;
     p.xs_cap = (int)((cols + 3) / 4 * 4);
     p.part_cap = (int)(((rows_per + 2) * seg_count((int)cols) + 3) / 4 * 4);
+    p.xloc_cap = 4;
     p.timeout_ns = 4000000000LL;
-    const size_t smem = (size_t)NSLOT * SLOT_BYTES + ((size_t)p.xs_cap + p.part_cap) * 4;
+    const size_t smem = (size_t)NSLOT * SLOT_BYTES + ((size_t)p.xs_cap + p.part_cap + p.xloc_cap) * 4;
     if (smem + sizeof(Smem) > 227 * 1024) return set_error(QW_ERR_UNSUPPORTED, "rows too large for one launch");
     if (cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return set_error(QW_ERR_CUDA, "cannot raise the gemv kernel's shared-memory limit");
