@@ -111,11 +111,22 @@ int qw_num_ctas(const qw_model* model);
  * events. */
 void* qw_model_stream(const qw_model* model);
 
+/* Phase timeline (tracing): when enabled, every launch records, for its first step, per CTA,
+ * qw_trace_stride() globaltimer stamps (ns): 12 per layer at the phase hand-offs, then 4 for the
+ * lm_head / argmax tail; then, for CTA 0, 4 stamps per weight/KV ring piece (up to 1024 pieces:
+ * issued, wait started, data ready, released). qw_read_trace copies
+ * num_ctas * stride + 4096 stamps of the most recent launch.
+ * The reference measured its per-part breakdown by ablation (README.md:64-71); this records it. */
+size_t qw_trace_stride(const qw_model* model);
+int qw_set_trace(qw_model* model, int enable);
+int qw_read_trace(qw_model* model, uint64_t* out, size_t capacity);
+
 /* ---- standalone kernels (the device code of the decode kernel, exposed for microbenchmarks) ---- */
 
 /* y = W x, W bf16 [rows][cols] row-major, x/y f32 — the matvec_bf16 kernel
  * (shaders/inference.metal:143-186, cpu_inference.rs:225-257) as the decode kernel streams it.
- * cols must be a multiple of 256 (<= 1024, or a multiple of 1024 up to 12288). */
+ * cols must split into 1, 2, 3, 4, 6 or 12 segments of 256, 512, 768 or 1024 columns
+ * (e.g. 256, 512, 768, 1024, 2048, 3072, 4096, 6144, 12288). */
 int qw_gemv_bf16(int device, const uint16_t* d_w, const float* d_x, float* d_y, size_t rows, size_t cols,
                  void* stream);
 

@@ -38,6 +38,7 @@
 // (fast-forwards to the end without blocking), waits (bounded) for its own bulk copies in flight
 // and returns. The host reports the error.
 #pragma once
+#include <cstddef>
 #include <cstdint>
 #include <cuda_runtime.h>
 
@@ -54,10 +55,21 @@ constexpr int HD = 128;                       // head_dim (the reference's atten
 constexpr int ATT_P = SLOT_BYTES / (2 * HD * 4);  // cached positions per attention ring slot (24)
 constexpr int MAX_G = 3;                      // query heads per KV head
 constexpr int MAX_S = 18;                     // attention chunks per KV head
-constexpr int MIN_CHUNK = 8;                  // fewest positions per attention chunk
+constexpr int MIN_CHUNK = 32;                 // fewest positions per attention chunk
+constexpr uint32_t LM_PREFETCH_BYTES = 256u * 1024;  // lm_head bytes per CTA warmed into L2 ahead of use
 constexpr int APART_STRIDE = HD + 4;          // words per attention partial: acc[128], m, l, pad
-constexpr int GP = 2;                         // tagged word pairs a consumer thread polls at once
+constexpr int GP = 4;                         // tagged word pairs a consumer thread polls at once
 constexpr uint32_t NONE_IDX = 0xFFFFFFFFu;
+// phase timeline (optional): per layer, stamps after: 0 layer start, 1 A input ready (x gathered +
+// rmsnorm), 2 A rows stored, 3 B inputs ready (q/k/v gathered, norm+RoPE), 4 B chunk done,
+// 5 B merged/published, 6 C input ready (att gathered), 7 C rows stored, 8 D input ready,
+// 9 D rows stored, 10 E input ready (h gathered), 11 E rows stored, 12 (merging CTAs) partials
+// polled, 13 (merging CTAs) attention output published; then 4 stamps for the token
+// tail: lm_head input ready, lm_head done, end-of-token barrier passed, next token known
+constexpr int TRACE_PER_LAYER = 14;
+// ...followed (after all CTAs' stamps) by CTA 0's ring timeline of step 0: per ring piece
+// {producer issued, consumer started waiting, data ready, consumer done}, up to TRACE_PIECES pieces
+constexpr int TRACE_PIECES = 1024;
 
 // error codes written to DecodeParams::err[0]
 enum : int { DERR_NONE = 0, DERR_TIMEOUT_GRID = 1, DERR_TIMEOUT_FULL = 2, DERR_TIMEOUT_EMPTY = 3,
@@ -89,6 +101,7 @@ struct DecodeParams {
     u64* flags;                  // [grid] barrier flags: epoch << 32 | tokens finished
     int* err;                    // [4] code, cta, where, detail
     float* logits;               // [V] or null (decode skips it)
+    u64* trace;                  // [grid][TRACE_PER_LAYER * L + 4] globaltimer stamps of step 0, or null
     // tokens
     const uint32_t* tok_in;      // step 0 input token (device memory)
     uint32_t* tok_out;           // [steps + 1] or null: tok_out[i + 1] = argmax of step i
@@ -105,6 +118,7 @@ struct DecodeParams {
     int xs_cap;                  // floats in the shared activation buffer
     int xloc_cap;                // floats in the shared residual-rows buffer
     long long timeout_ns;
+    int poll_ns;                 // back-off between unsuccessful polling rounds of tagged words (0 = none)
 };
 
 // static row partition of a GEMV phase for one CTA
@@ -112,13 +126,20 @@ struct GemvGeo {
     int r0, r1;       // output rows [r0, r1)
     int K;            // columns
     int rpp;          // rows per ring slot
-    int segs;         // 1024-column segments per row (K / segw)
-    int segw;         // columns per segment
+    int segs;         // column segments per row (K / segw), see seg_count
+    int segw;         // columns per segment (256, 512, 768 or 1024)
     int cpl;          // 16-byte chunks per lane per segment (segw / 256)
     long long woff;   // element offset of the matrix inside a layer block
 };
 
-__host__ __device__ inline int seg_count(int K) { return K <= 1024 ? 1 : K / 1024; }
+// Column segments per row: the narrowest segment width (256, 512, 768 or 1024 columns) whose count
+// divides the 12 consumer warps, so that each warp keeps one fixed segment of x in registers
+// (segw / 32 values) and covers 1024 / segw rows of every ring piece.
+__host__ __device__ inline int seg_count(int K) {
+    for (int segw = 256; segw <= 1024; segw += 256)
+        if (K % segw == 0 && 12 % (K / segw) == 0) return K / segw;
+    return 0;  // unsupported (rejected on the host)
+}
 
 __device__ inline GemvGeo make_geo(long long rows, int K, int cta, int n, long long woff, int pair) {
     GemvGeo g;
@@ -161,10 +182,11 @@ __device__ inline AttnItem attn_item(const DecodeParams& p, int cta, int pos) {
 }
 
 struct Smem {
+    // qs / ks / vs are accessed as float4: keep them 16-byte aligned
+    __align__(16) float qs[MAX_G][HD];
+    __align__(16) float ks[HD];
+    __align__(16) float vs[HD];
     GemvGeo geo[5];              // this CTA's rows of phases A (q|k|v), C (o), D (gate|up), E (down), F (lm_head)
-    float qs[MAX_G][HD];
-    float ks[HD];
-    float vs[HD];
     float sc[2][MAX_G][ATT_P];
     float ml[MAX_S][MAX_G][2];   // attention partials' (m, l) gathered by the merging CTA
     float red[64];
@@ -176,6 +198,10 @@ struct Smem {
     int abort;           // set once any wait expired
     unsigned token;
 };
+
+static_assert(offsetof(Smem, qs) % 16 == 0 && offsetof(Smem, ks) % 16 == 0 && offsetof(Smem, vs) % 16 == 0,
+              "float4-accessed shared arrays must be 16-byte aligned");
+static_assert(offsetof(Smem, full) % 8 == 0 && offsetof(Smem, empty) % 8 == 0, "mbarriers must be 8-byte aligned");
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -206,51 +232,53 @@ __device__ __forceinline__ uint32_t word_tag(u64 w) { return (uint32_t)(w >> 32)
 __device__ __forceinline__ float word_val(u64 w) { return __uint_as_float((uint32_t)w); }
 __device__ __forceinline__ u64 tagged(float v, uint32_t tag) { return ((u64)tag << 32) | __float_as_uint(v); }
 
+// the kernels' shared memory: fixed-size state, then (dynamic) ring | xs | part | xloc
+__shared__ Smem qw_sm;
+extern __shared__ __align__(128) uint8_t qw_dyn[];
+
+// Per-thread state is kept to the two ring counters: everything else is re-derived from special
+// registers, the (constant-bank) kernel parameters and fixed shared-memory addresses, which keeps
+// the whole kernel within the 128 registers a 13-warp CTA can have per thread.
 class Decoder {
 public:
     const DecodeParams& p;
-    Smem& sm;
-    uint8_t* ring;
-    float* xs;
-    float* part;
-    float* xloc;
-    int cta, n, warp, lane, tid;
-    int QD, KVD, G, QKVR;
-    // the CTA's static row partition per phase lives in shared memory (computed once by thread 0
-    // in init_geometry), not in registers
-    const GemvGeo &gA, &gC, &gD, &gE, &gF;
     uint32_t it = 0;       // ring pieces consumed (consumer) or walked (producer)
     uint32_t n_issued = 0; // producer: pieces whose copies were issued (all before any abort)
 
-    __device__ Decoder(const DecodeParams& p_, Smem& sm_, uint8_t* dyn)
-        : p(p_), sm(sm_), gA(sm_.geo[0]), gC(sm_.geo[1]), gD(sm_.geo[2]), gE(sm_.geo[3]), gF(sm_.geo[4]) {
-        ring = dyn;
-        xs = reinterpret_cast<float*>(dyn + NSLOT * SLOT_BYTES);
-        part = xs + p.xs_cap;
-        xloc = part + p.part_cap;
-        cta = blockIdx.x;
-        n = gridDim.x;
-        tid = threadIdx.x;
-        warp = tid >> 5;
-        lane = tid & 31;
-        QD = p.NQ * HD;
-        KVD = p.NKV * HD;
-        G = p.NQ / p.NKV;
-        QKVR = QD + 2 * KVD;
-    }
+    __device__ explicit Decoder(const DecodeParams& p_) : p(p_) {}
+
+    __device__ __forceinline__ static int tid() { return (int)threadIdx.x; }
+    __device__ __forceinline__ static int warp() { return (int)(threadIdx.x >> 5); }
+    __device__ __forceinline__ static int lane() { return (int)(threadIdx.x & 31); }
+    __device__ __forceinline__ static int cta() { return (int)blockIdx.x; }
+    __device__ __forceinline__ static int nctas() { return (int)gridDim.x; }
+    __device__ __forceinline__ static uint8_t* ring() { return qw_dyn; }
+    __device__ __forceinline__ static float* xs() { return reinterpret_cast<float*>(qw_dyn + NSLOT * SLOT_BYTES); }
+    __device__ __forceinline__ float* part() const { return xs() + p.xs_cap; }
+    __device__ __forceinline__ float* xloc() const { return part() + p.part_cap; }
+    __device__ __forceinline__ int QD() const { return p.NQ * HD; }
+    __device__ __forceinline__ int KVD() const { return p.NKV * HD; }
+    __device__ __forceinline__ int G() const { return p.NQ / p.NKV; }
+    __device__ __forceinline__ int QKVR() const { return QD() + 2 * KVD(); }
+    // this CTA's static row partition of phases A (q|k|v), C (o), D (gate|up), E (down), F (lm_head)
+    __device__ __forceinline__ static const GemvGeo& gA() { return qw_sm.geo[0]; }
+    __device__ __forceinline__ static const GemvGeo& gC() { return qw_sm.geo[1]; }
+    __device__ __forceinline__ static const GemvGeo& gD() { return qw_sm.geo[2]; }
+    __device__ __forceinline__ static const GemvGeo& gE() { return qw_sm.geo[3]; }
+    __device__ __forceinline__ static const GemvGeo& gF() { return qw_sm.geo[4]; }
 
     // one thread, before the CTA-wide barrier that follows mbarrier initialisation
-    __device__ static void init_geometry(const DecodeParams& p, Smem& sm) {
-        const int cta = blockIdx.x, n = gridDim.x;
-        const long long QD = (long long)p.NQ * HD, KVD = (long long)p.NKV * HD, QKVR = QD + 2 * KVD;
-        const long long offC = QKVR * p.H;
-        const long long offD = offC + (long long)p.H * QD;
+    __device__ static void init_geometry(const DecodeParams& p) {
+        const int c = blockIdx.x, nc = gridDim.x;
+        const long long qd = (long long)p.NQ * HD, kvd = (long long)p.NKV * HD, qkvr = qd + 2 * kvd;
+        const long long offC = qkvr * p.H;
+        const long long offD = offC + (long long)p.H * qd;
         const long long offE = offD + 2LL * p.I * p.H;
-        sm.geo[0] = make_geo(QKVR, p.H, cta, n, 0, 0);
-        sm.geo[1] = make_geo(p.H, (int)QD, cta, n, offC, 0);
-        sm.geo[2] = make_geo(2LL * p.I, p.H, cta, n, offD, 1);
-        sm.geo[3] = make_geo(p.H, p.I, cta, n, offE, 0);
-        sm.geo[4] = make_geo(p.V, p.H, cta, n, 0, 0);
+        qw_sm.geo[0] = make_geo(qkvr, p.H, c, nc, 0, 0);
+        qw_sm.geo[1] = make_geo(p.H, (int)qd, c, nc, offC, 0);
+        qw_sm.geo[2] = make_geo(2LL * p.I, p.H, c, nc, offD, 1);
+        qw_sm.geo[3] = make_geo(p.H, p.I, c, nc, offE, 0);
+        qw_sm.geo[4] = make_geo(p.V, p.H, c, nc, 0, 0);
     }
 
     // phase sequence numbers within the launch -> tags (12 bits of epoch, 20 bits of sequence)
@@ -259,27 +287,44 @@ public:
     }
     __device__ uint32_t tag(uint32_t sq) const { return ((p.epoch & 0xFFFu) << 20) | (sq & 0xFFFFFu); }
 
-    // ------------------------------------------------------------------ errors and waits
-    __device__ bool aborted() const { return *reinterpret_cast<volatile const int*>(&sm.abort) != 0; }
+    __device__ __forceinline__ void stamp(int step, int idx) const {
+        if (p.trace != nullptr && step == 0 && tid() == 0)
+            p.trace[(size_t)cta() * (TRACE_PER_LAYER * p.L + 4) + idx] = globaltimer_ns();
+    }
+    // CTA 0's per-piece ring timeline (field 0 producer issue, 1 wait start, 2 ready, 3 done)
+    __device__ __forceinline__ void piece_stamp(uint32_t piece, int field) const {
+        if (p.trace != nullptr && cta() == 0 && piece < (uint32_t)TRACE_PIECES && (field == 0 || tid() == 0))
+            p.trace[(size_t)nctas() * (TRACE_PER_LAYER * p.L + 4) + piece * 4 + field] = globaltimer_ns();
+    }
 
-    __device__ void fail(int code, int where) {
-        *reinterpret_cast<volatile int*>(&sm.abort) = 1;
+    // ------------------------------------------------------------------ errors and waits
+    __device__ bool aborted() const { return *reinterpret_cast<volatile const int*>(&qw_sm.abort) != 0; }
+
+    __device__ __noinline__ void fail(int code, int where) {
+        *reinterpret_cast<volatile int*>(&qw_sm.abort) = 1;
         if (atomicCAS(&p.err[0], 0, code) == 0) {
-            p.err[1] = cta;
+            p.err[1] = cta();
             p.err[2] = where;
             __threadfence();
         }
     }
 
-    // called between unsuccessful polls; returns true when the caller must stop waiting
-    __device__ bool wait_expired(uint32_t& spins, uint64_t& t0, int code, int where) {
+    // called between unsuccessful polls; returns true when the caller must stop waiting. Cheap on
+    // the fast path: only every 32nd call reads the timer and the CTA's abort flag; the global error
+    // word (another CTA gave up) is read only after 50 us of waiting, since a global load here would
+    // add an L2 round trip to every ring hand-off.
+    __device__ __noinline__ bool wait_expired(uint32_t& spins, uint64_t& t0, int code, int where) {
         ++spins;
-        if (spins == 8) t0 = globaltimer_ns();
-        if (spins > 8 && (spins & 15) == 0) {
-            if (aborted()) return true;
-            if (ld_volatile_s32(p.err) != 0) { *reinterpret_cast<volatile int*>(&sm.abort) = 1; return true; }
-            if (globaltimer_ns() - t0 > (uint64_t)p.timeout_ns) { fail(code, where); return true; }
+        if ((spins & 31) != 0) return false;
+        if (aborted()) return true;
+        const uint64_t now = globaltimer_ns();
+        if (spins == 32) { t0 = now; return false; }
+        const uint64_t waited = now - t0;
+        if (waited > 50000 && (spins & 1023) == 0 && ld_volatile_s32(p.err) != 0) {
+            *reinterpret_cast<volatile int*>(&qw_sm.abort) = 1;
+            return true;
         }
+        if (waited > (uint64_t)p.timeout_ns) { fail(code, where); return true; }
         return false;
     }
 
@@ -293,44 +338,47 @@ public:
     }
 
     // xs[0..K) <- values of the tagged words src[0..K) once each carries `tg` (K even, src 16-byte aligned)
-    __device__ void gather(const u64* src, int K, uint32_t tg) {
+    __device__ __noinline__ void gather(const u64* src, int K, uint32_t tg) {
         const int npairs = K >> 1;
         for (int base = 0; base < npairs; base += NCT * GP) {
             unsigned pending = 0;
 #pragma unroll
             for (int j = 0; j < GP; j++)
-                if (base + tid + j * NCT < npairs) pending |= 1u << j;
+                if (base + tid() + j * NCT < npairs) pending |= 1u << j;
             uint32_t spins = 0;
             uint64_t t0 = 0;
             while (pending && !aborted()) {
                 ulonglong2 w[GP];
 #pragma unroll
                 for (int j = 0; j < GP; j++)
-                    if (pending & (1u << j)) w[j] = ld_relaxed_v2u64(src + 2 * (base + tid + j * NCT));
+                    if (pending & (1u << j)) w[j] = ld_relaxed_v2u64(src + 2 * (base + tid() + j * NCT));
 #pragma unroll
                 for (int j = 0; j < GP; j++) {
                     if ((pending & (1u << j)) && word_tag(w[j].x) == tg && word_tag(w[j].y) == tg) {
-                        const int i = 2 * (base + tid + j * NCT);
-                        xs[i] = word_val(w[j].x);
-                        xs[i + 1] = word_val(w[j].y);
+                        const int i = 2 * (base + tid() + j * NCT);
+                        xs()[i] = word_val(w[j].x);
+                        xs()[i + 1] = word_val(w[j].y);
                         pending &= ~(1u << j);
                     }
                 }
-                if (pending && wait_expired(spins, t0, DERR_TIMEOUT_DATA, (int)tg)) break;
+                if (pending) {
+                    if (wait_expired(spins, t0, DERR_TIMEOUT_DATA, (int)tg)) break;
+                    if (p.poll_ns) __nanosleep(p.poll_ns);
+                }
             }
         }
         named_bar_sync(1, NCT);
     }
 
     // one end-of-token grid barrier: every CTA has published `done` finished tokens
-    __device__ void token_barrier(uint32_t done) {
+    __device__ __noinline__ void token_barrier(uint32_t done) {
         named_bar_sync(1, NCT);
         const u64 target = ((u64)p.epoch << 32) | done;
-        if (tid == 0) {
+        if (tid() == 0) {
             fence_acq_rel_gpu();
-            st_relaxed_u64(p.flags + cta, target);
+            st_relaxed_u64(p.flags + cta(), target);
         }
-        if (warp == 0 && !aborted()) {
+        if (warp() == 0 && !aborted()) {
             uint32_t spins = 0;
             uint64_t t0 = 0;
             for (;;) {
@@ -338,69 +386,77 @@ public:
                 u64 v[8];
 #pragma unroll
                 for (int k = 0; k < 8; k++) {
-                    const int j = lane + 32 * k;
-                    v[k] = j < n ? ld_relaxed_u64(p.flags + j) : target;
+                    const int j = lane() + 32 * k;
+                    v[k] = j < nctas() ? ld_relaxed_u64(p.flags + j) : target;
                 }
 #pragma unroll
                 for (int k = 0; k < 8; k++) ok &= v[k] >= target;
-                for (int j = lane + 256; j < n; j += 32) ok &= ld_relaxed_u64(p.flags + j) >= target;
+                for (int j = lane() + 256; j < nctas(); j += 32) ok &= ld_relaxed_u64(p.flags + j) >= target;
                 if (__all_sync(0xFFFFFFFFu, ok)) break;
                 int stop = 0;
-                if (lane == 0) stop = wait_expired(spins, t0, DERR_TIMEOUT_GRID, (int)done);
+                if (lane() == 0) stop = wait_expired(spins, t0, DERR_TIMEOUT_GRID, (int)done);
                 if (__shfl_sync(0xFFFFFFFFu, stop, 0)) break;
             }
             fence_acq_rel_gpu();
         }
         named_bar_sync(1, NCT);
-        if (tid == 0) st_release_cta_shared(&sm.progress, done);
+        if (tid() == 0) st_release_cta_shared(&qw_sm.progress, done);
     }
 
     // ------------------------------------------------------------------ consumer helpers
     __device__ float block_sum(float v) {
         v = warp_sum(v);
-        if (lane == 0) sm.red[warp] = v;
+        if (lane() == 0) qw_sm.red[warp()] = v;
         named_bar_sync(1, NCT);
-        if (warp == 0) {
-            float t = lane < NCW ? sm.red[lane] : 0.f;
+        if (warp() == 0) {
+            float t = lane() < NCW ? qw_sm.red[lane()] : 0.f;
             t = warp_sum(t);
-            if (lane == 0) sm.red[32] = t;
+            if (lane() == 0) qw_sm.red[32] = t;
         }
         named_bar_sync(1, NCT);
-        return sm.red[32];
+        return qw_sm.red[32];
     }
 
     // xs <- rmsnorm(src) * w  (cpu_inference.rs:189-194). src is the tagged residual stream, or
     // (from_embed) the embedding row of `token`, in which case the CTA also initialises its own
     // residual rows xloc from that row.
-    __device__ void norm_prologue(const uint16_t* w, bool from_embed, unsigned token, uint32_t tg) {
+    __device__ __noinline__ void norm_prologue(const uint16_t* w, bool from_embed, unsigned token, uint32_t tg) {
         const int H = p.H;
         if (from_embed) {
             const uint16_t* erow = p.embed + (size_t)token * H;
-            for (int i = tid; i < H; i += NCT) {
+            for (int i = tid(); i < H; i += NCT) {
                 const float v = bf16_to_f32(__ldg(erow + i));
-                xs[i] = v;
-                if (i >= gC.r0 && i < gC.r1) xloc[i - gC.r0] = v;
+                xs()[i] = v;
+                if (i >= gC().r0 && i < gC().r1) xloc()[i - gC().r0] = v;
             }
             named_bar_sync(1, NCT);
         } else {
             gather(p.x, H, tg);
         }
         float ss = 0.f;
-        for (int i = tid; i < H; i += NCT) ss = fmaf(xs[i], xs[i], ss);
+        for (int i = tid(); i < H; i += NCT) ss = fmaf(xs()[i], xs()[i], ss);
         const float tot = block_sum(ss);
         const float s = 1.0f / sqrtf(tot / (float)H + p.eps);
-        for (int i = tid; i < H; i += NCT) xs[i] = xs[i] * s * bf16_to_f32(__ldg(w + i));
+        for (int i = tid(); i < H; i += NCT) xs()[i] = xs()[i] * s * bf16_to_f32(__ldg(w + i));
         named_bar_sync(1, NCT);
     }
 
-    // all ring pieces of one GEMV phase: part[(row - r0) * segs + seg] = partial dot product
-    __device__ void gemv_consume(const GemvGeo& g) {
-        const int myseg = warp % g.segs;
+    // All ring pieces of one GEMV phase: part[(row - r0) * segs + seg] = partial dot product.
+    // Warp w owns column segment w % segs (its x values sit in registers: segw / 32 per lane) and
+    // rows w / segs, + 12 / segs, ... of every piece: R = 1024 / segw rows (1, 2 or 4). Lane l reads
+    // 16-byte chunks l, l + 32, ... of the segment, so every shared-memory load is one contiguous
+    // 512-byte warp access; the R row sums are then reduced together by a transposing butterfly
+    // (R = 4: 6 shuffles for the 4 rows instead of 20).
+    __device__ __noinline__ void gemv_consume(const GemvGeo& gs) {
+        const GemvGeo g = gs;  // loop-invariant: keep the phase geometry in registers
+        const int myseg = warp() % g.segs;
+        const int group = warp() / g.segs, ngroups = NCW / g.segs;
+        const int R = 1024 / g.segw;
         float xr[32];
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             if (i < g.cpl) {
-                const float4* xp = reinterpret_cast<const float4*>(xs + myseg * g.segw + (i * 32 + lane) * 8);
+                const float4* xp = reinterpret_cast<const float4*>(xs() + myseg * g.segw + (i * 32 + lane()) * 8);
                 float4 a = xp[0], b = xp[1];
                 xr[i * 8 + 0] = a.x; xr[i * 8 + 1] = a.y; xr[i * 8 + 2] = a.z; xr[i * 8 + 3] = a.w;
                 xr[i * 8 + 4] = b.x; xr[i * 8 + 5] = b.y; xr[i * 8 + 6] = b.z; xr[i * 8 + 7] = b.w;
@@ -411,25 +467,58 @@ public:
         }
         for (int r = g.r0; r < g.r1; r += g.rpp) {
             const int nr = min(g.rpp, g.r1 - r);
-            const int units = nr * g.segs;
-            const int slot = it % NSLOT;
-            const uint32_t par = (it / NSLOT) & 1;
-            const bool ok = wait_mbar(&sm.full[slot], par, DERR_TIMEOUT_FULL);
+            piece_stamp(it, 1);
+            const bool ok = wait_mbar(&qw_sm.full[it % NSLOT], (it / NSLOT) & 1, DERR_TIMEOUT_FULL);
+            piece_stamp(it, 2);
             if (ok) {
-                const uint8_t* base = ring + slot * SLOT_BYTES;
-                for (int u = warp; u < units; u += NCW) {
-                    const int rl = u / g.segs;  // u % segs == myseg because NCW % segs == 0
-                    const uint4* wp = reinterpret_cast<const uint4*>(base + ((size_t)rl * g.K + (size_t)myseg * g.segw) * 2);
-                    float acc = 0.f;
+                const uint8_t* base = ring() + (it % NSLOT) * SLOT_BYTES + (size_t)myseg * g.segw * 2;
+                float v[4];
 #pragma unroll
-                    for (int i = 0; i < 4; i++)
-                        if (i < g.cpl) acc += dot8(wp[i * 32 + lane], xr + i * 8);
-                    acc = warp_sum(acc);
-                    if (lane == 0) part[(r - g.r0 + rl) * g.segs + myseg] = acc;
+                for (int k = 0; k < 4; k++) {
+                    v[k] = 0.f;
+                    const int rl = group + k * ngroups;
+                    if (k < R && rl < nr) {
+                        const uint4* wp = reinterpret_cast<const uint4*>(base + (size_t)rl * g.K * 2);
+#pragma unroll
+                        for (int i = 0; i < 4; i++)
+                            if (i < g.cpl) v[k] += dot8(wp[i * 32 + lane()], xr + i * 8);
+                    }
                 }
+                // transposing butterfly: afterwards lane l holds the total of row k(l)
+                int k_of_lane = 0;
+                float tot;
+                if (R == 4) {
+                    const bool hi16 = lane() & 16;
+                    float keep0 = hi16 ? v[2] : v[0], keep1 = hi16 ? v[3] : v[1];
+                    keep0 += __shfl_xor_sync(0xFFFFFFFFu, hi16 ? v[0] : v[2], 16);
+                    keep1 += __shfl_xor_sync(0xFFFFFFFFu, hi16 ? v[1] : v[3], 16);
+                    const bool hi8 = lane() & 8;
+                    tot = hi8 ? keep1 : keep0;
+                    tot += __shfl_xor_sync(0xFFFFFFFFu, hi8 ? keep0 : keep1, 8);
+                    k_of_lane = (hi16 ? 2 : 0) + (hi8 ? 1 : 0);
+                    tot += __shfl_xor_sync(0xFFFFFFFFu, tot, 4);
+                } else if (R == 2) {
+                    const bool hi16 = lane() & 16;
+                    tot = hi16 ? v[1] : v[0];
+                    tot += __shfl_xor_sync(0xFFFFFFFFu, hi16 ? v[0] : v[1], 16);
+                    k_of_lane = hi16 ? 1 : 0;
+                    tot += __shfl_xor_sync(0xFFFFFFFFu, tot, 8);
+                    tot += __shfl_xor_sync(0xFFFFFFFFu, tot, 4);
+                } else {
+                    tot = v[0];
+                    tot += __shfl_xor_sync(0xFFFFFFFFu, tot, 16);
+                    tot += __shfl_xor_sync(0xFFFFFFFFu, tot, 8);
+                    tot += __shfl_xor_sync(0xFFFFFFFFu, tot, 4);
+                }
+                tot += __shfl_xor_sync(0xFFFFFFFFu, tot, 2);
+                tot += __shfl_xor_sync(0xFFFFFFFFu, tot, 1);
+                const int rl = group + k_of_lane * ngroups;
+                if ((lane() & 7) == 0 && k_of_lane < R && rl < nr)
+                    part()[(r - g.r0 + rl) * g.segs + myseg] = tot;
             }
             __syncwarp();
-            if (lane == 0 && ok) mbar_arrive(&sm.empty[slot]);  // a slot is released only after its data landed
+            if (lane() == 0 && ok) mbar_arrive(&qw_sm.empty[it % NSLOT]);  // a slot is released only after its data landed
+            piece_stamp(it, 3);
             ++it;
         }
         named_bar_sync(1, NCT);
@@ -437,7 +526,7 @@ public:
 
     __device__ __forceinline__ float row_value(const GemvGeo& g, int rl) const {
         float y = 0.f;
-        for (int sgi = 0; sgi < g.segs; sgi++) y += part[rl * g.segs + sgi];
+        for (int sgi = 0; sgi < g.segs; sgi++) y += part()[rl * g.segs + sgi];
         return y;
     }
 
@@ -450,13 +539,14 @@ public:
         ulonglong2 a = make_ulonglong2(0, 0), b = make_ulonglong2(0, 0);
         bool ok = false;
         while (!aborted()) {
-            a = ld_relaxed_v2u64(src + lane * 4);
-            b = ld_relaxed_v2u64(src + lane * 4 + 2);
+            a = ld_relaxed_v2u64(src + lane() * 4);
+            b = ld_relaxed_v2u64(src + lane() * 4 + 2);
             ok = word_tag(a.x) == tg && word_tag(a.y) == tg && word_tag(b.x) == tg && word_tag(b.y) == tg;
             if (__all_sync(0xFFFFFFFFu, ok)) break;
             int stop = 0;
-            if (lane == 0) stop = wait_expired(spins, t0, DERR_TIMEOUT_DATA, (int)tg);
+            if (lane() == 0) stop = wait_expired(spins, t0, DERR_TIMEOUT_DATA, (int)tg);
             if (__shfl_sync(0xFFFFFFFFu, stop, 0)) break;
+            if (p.poll_ns) __nanosleep(p.poll_ns);
         }
         return make_float4(word_val(a.x), word_val(a.y), word_val(b.x), word_val(b.y));
     }
@@ -465,7 +555,7 @@ public:
         float ss = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
         ss = warp_sum(ss);
         const float s = 1.0f / sqrtf(ss / (float)HD + p.eps);
-        const int d0 = lane * 4;
+        const int d0 = lane() * 4;
         float e[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int j = 0; j < 4; j++) e[j] = e[j] * s * bf16_to_f32(__ldg(nw + d0 + j));
@@ -474,37 +564,37 @@ public:
         for (int j = 0; j < 4; j++) {
             const float other = __shfl_xor_sync(0xFFFFFFFFu, e[j], 16);  // element d +- 64
             const float2 cs = rrow[(d0 + j) & 63];
-            if (lane < 16) o[j] = e[j] * cs.x - other * cs.y;   // x[i]      = a*cos - b*sin
+            if (lane() < 16) o[j] = e[j] * cs.x - other * cs.y;   // x[i]      = a*cos - b*sin
             else o[j] = e[j] * cs.x + other * cs.y;             // x[i+half] = b*cos + a*sin
         }
-        reinterpret_cast<float4*>(dst)[lane] = make_float4(o[0], o[1], o[2], o[3]);
+        reinterpret_cast<float4*>(dst)[lane()] = make_float4(o[0], o[1], o[2], o[3]);
     }
 
     // online-softmax update over np positions whose K/V rows (128 f32 each) are in shared memory
     __device__ void attn_block(const float* Kb, const float* Vb, int np, int buf, const float4* q4,
                                float& m, float& l, float& acc) {
-        for (int pp = warp; pp < np; pp += NCW) {
-            const float4 k4 = reinterpret_cast<const float4*>(Kb + pp * HD)[lane];
+        for (int pp = warp(); pp < np; pp += NCW) {
+            const float4 k4 = reinterpret_cast<const float4*>(Kb + pp * HD)[lane()];
 #pragma unroll
             for (int h = 0; h < MAX_G; h++) {
-                if (h < G) {
+                if (h < G()) {
                     float d = q4[h].x * k4.x + q4[h].y * k4.y + q4[h].z * k4.z + q4[h].w * k4.w;
                     d = warp_sum(d);
-                    if (lane == 0) sm.sc[buf][h][pp] = d * p.scale;
+                    if (lane() == 0) qw_sm.sc[buf][h][pp] = d * p.scale;
                 }
             }
         }
         named_bar_sync(1, NCT);
-        if (tid < G * HD) {
-            const int h = tid >> 7, d = tid & (HD - 1);
+        if (tid() < G() * HD) {
+            const int h = tid() >> 7, d = tid() & (HD - 1);
             float mp = -INFINITY;
-            for (int pp = 0; pp < np; pp++) mp = fmaxf(mp, sm.sc[buf][h][pp]);
+            for (int pp = 0; pp < np; pp++) mp = fmaxf(mp, qw_sm.sc[buf][h][pp]);
             const float mn = fmaxf(m, mp);
             const float corr = (m == -INFINITY) ? 0.f : expf(m - mn);
             l *= corr;
             acc *= corr;
             for (int pp = 0; pp < np; pp++) {
-                const float e = expf(sm.sc[buf][h][pp] - mn);
+                const float e = expf(qw_sm.sc[buf][h][pp] - mn);
                 l += e;
                 acc = fmaf(e, Vb[pp * HD + d], acc);
             }
@@ -512,8 +602,8 @@ public:
         }
     }
 
-    __device__ void attention_consume(int step, int l, int pos) {
-        const AttnItem a = attn_item(p, cta, pos);
+    __device__ __noinline__ void attention_consume(int step, int l, int pos) {
+        const AttnItem a = attn_item(p, cta(), pos);
         if (!a.active) return;   // uniform over the CTA
         const uint16_t* nrm = p.layer_n + (size_t)l * p.norm_stride;
         const uint16_t* qn = nrm + 2 * p.H;
@@ -521,22 +611,23 @@ public:
         const float2* rrow = p.rope + (size_t)pos * (HD / 2);
         const uint32_t tgA = tag(seq(step, l, 1)), tgB = tag(seq(step, l, 2));
         // q heads g*G .. g*G+G-1, and (last chunk) this position's k and v
-        if (warp < G) head_norm_rope(gather_head(p.qkv + (size_t)(a.g * G + warp) * HD, tgA), qn, rrow, sm.qs[warp]);
+        if (warp() < G()) head_norm_rope(gather_head(p.qkv + (size_t)(a.g * G() + warp()) * HD, tgA), qn, rrow, qw_sm.qs[warp()]);
         if (a.has_cur) {
-            if (warp == G) head_norm_rope(gather_head(p.qkv + QD + (size_t)a.g * HD, tgA), kn, rrow, sm.ks);
-            if (warp == G + 1)
-                reinterpret_cast<float4*>(sm.vs)[lane] = gather_head(p.qkv + QD + KVD + (size_t)a.g * HD, tgA);
+            if (warp() == G()) head_norm_rope(gather_head(p.qkv + QD() + (size_t)a.g * HD, tgA), kn, rrow, qw_sm.ks);
+            if (warp() == G() + 1)
+                reinterpret_cast<float4*>(qw_sm.vs)[lane()] = gather_head(p.qkv + QD() + KVD() + (size_t)a.g * HD, tgA);
         }
         named_bar_sync(1, NCT);
-        if (a.has_cur && tid < 2 * HD) {  // append K/V at slot `pos` (cpu_inference.rs:140-141)
+        stamp(step, l * TRACE_PER_LAYER + 3);
+        if (a.has_cur && tid() < 2 * HD) {  // append K/V at slot `pos` (cpu_inference.rs:140-141)
             const size_t off = (((size_t)l * p.NKV + a.g) * p.max_seq + pos) * HD;
-            if (tid < HD) p.kc[off + tid] = sm.ks[tid];
-            else p.vc[off + tid - HD] = sm.vs[tid - HD];
+            if (tid() < HD) p.kc[off + tid()] = qw_sm.ks[tid()];
+            else p.vc[off + tid() - HD] = qw_sm.vs[tid() - HD];
         }
         float4 q4[MAX_G];
 #pragma unroll
         for (int h = 0; h < MAX_G; h++)
-            q4[h] = h < G ? reinterpret_cast<const float4*>(sm.qs[h])[lane] : make_float4(0, 0, 0, 0);
+            q4[h] = h < G() ? reinterpret_cast<const float4*>(qw_sm.qs[h])[lane()] : make_float4(0, 0, 0, 0);
         float m = -INFINITY, lsum = 0.f, acc = 0.f;
         int buf = 0;
         const int tc1 = a.has_cur ? pos : a.t1;  // cached positions [t0, tc1)
@@ -544,25 +635,26 @@ public:
             const int np = min(ATT_P, tc1 - t);
             const int slot = it % NSLOT;
             const uint32_t par = (it / NSLOT) & 1;
-            const bool ok = wait_mbar(&sm.full[slot], par, DERR_TIMEOUT_FULL);
-            const float* Kb = reinterpret_cast<const float*>(ring + slot * SLOT_BYTES);
+            const bool ok = wait_mbar(&qw_sm.full[slot], par, DERR_TIMEOUT_FULL);
+            const float* Kb = reinterpret_cast<const float*>(ring() + slot * SLOT_BYTES);
             const float* Vb = Kb + ATT_P * HD;
             attn_block(Kb, Vb, np, buf, q4, m, lsum, acc);
             __syncwarp();
-            if (lane == 0 && ok) mbar_arrive(&sm.empty[slot]);
+            if (lane() == 0 && ok) mbar_arrive(&qw_sm.empty[slot]);
             ++it;
             buf ^= 1;
         }
         if (a.has_cur) {
-            attn_block(sm.ks, sm.vs, 1, buf, q4, m, lsum, acc);
+            attn_block(qw_sm.ks, qw_sm.vs, 1, buf, q4, m, lsum, acc);
             buf ^= 1;
         }
-        const size_t head_base = (size_t)a.g * p.S * G;  // partial (s, h) at apart[((head_base + s*G + h) * APART_STRIDE]
+        stamp(step, l * TRACE_PER_LAYER + 4);
+        const size_t head_base = (size_t)a.g * p.S * G();  // partial (s, h) at apart[((head_base + s*G + h) * APART_STRIDE]
         if (a.s != 0) {
             // publish this chunk's partial as tagged words for the chunk-0 CTA of this KV head
-            if (tid < G * HD) {
-                const int h = tid >> 7, d = tid & (HD - 1);
-                u64* dst = p.apart + (head_base + (size_t)a.s * G + h) * APART_STRIDE;
+            if (tid() < G() * HD) {
+                const int h = tid() >> 7, d = tid() & (HD - 1);
+                u64* dst = p.apart + (head_base + (size_t)a.s * G() + h) * APART_STRIDE;
                 st_relaxed_u64(dst + d, tagged(acc, tgB));
                 if (d == 0) {
                     st_relaxed_u64(dst + HD, tagged(m, tgB));
@@ -571,77 +663,80 @@ public:
             }
             return;
         }
-        // chunk 0 merges the partials of chunks 0..S_eff-1 in chunk order. Every thread keeps its
-        // polls in flight together: an accumulator thread (h, d) polls word d of chunks 1.., and the
-        // first (S_eff-1)*G*2 threads also poll one (m or l) word each (bit 0 of `pending`).
-        if (tid < G * HD && (tid & (HD - 1)) == 0) {
-            sm.ml[0][tid >> 7][0] = m;
-            sm.ml[0][tid >> 7][1] = lsum;
+        // chunk 0 merges the partials of chunks 0..S_eff-1 in chunk order: an accumulator thread
+        // (h, d) polls word d of chunks 1.. (four chunks in flight per round) into the shared stage,
+        // and the first (S_eff-1)*G*2 threads also poll one (m or l) word each.
+        if (tid() < G() * HD && (tid() & (HD - 1)) == 0) {
+            qw_sm.ml[0][tid() >> 7][0] = m;
+            qw_sm.ml[0][tid() >> 7][1] = lsum;
         }
-        float av[MAX_S];
-        av[0] = acc;
+        float* stage = part();  // chunk s >= 1 partial words, [s - 1][G * HD] (part is free during phase B)
         {
-            const int h = tid >> 7, d = tid & (HD - 1);
-            uint32_t pending = 0;
-            if (tid < G * HD) {
-#pragma unroll
-                for (int s = 1; s < MAX_S; s++)
-                    if (s < a.S_eff) pending |= 1u << s;
-            }
+            const int h = tid() >> 7, d = tid() & (HD - 1);
             const u64* mlsrc = nullptr;
             float* mldst = nullptr;
-            if (tid < (a.S_eff - 1) * G * 2) {
-                const int s = 1 + tid / (2 * G), hh = (tid >> 1) % G, which = tid & 1;
-                mlsrc = p.apart + (head_base + (size_t)s * G + hh) * APART_STRIDE + HD + which;
-                mldst = &sm.ml[s][hh][which];
-                pending |= 1u;
+            if (tid() < (a.S_eff - 1) * G() * 2) {  // the first (S_eff-1)*G*2 threads also fetch one (m or l) word
+                const int s = 1 + tid() / (2 * G()), hh = (tid() >> 1) % G(), which = tid() & 1;
+                mlsrc = p.apart + (head_base + (size_t)s * G() + hh) * APART_STRIDE + HD + which;
+                mldst = &qw_sm.ml[s][hh][which];
             }
-            uint32_t spins = 0;
-            uint64_t t0 = 0;
-            while (pending && !aborted()) {
-                u64 w[MAX_S];
-                if (pending & 1u) w[0] = ld_relaxed_u64(mlsrc);
+            // up to four chunks' words (bits 0-3) and the (m, l) word (bit 4) in flight per round
+            for (int s0 = 1; s0 < a.S_eff || mlsrc; s0 += 4) {
+                uint32_t pending = mlsrc ? 16u : 0u;  // the (m, l) word is polled in the first round only
 #pragma unroll
-                for (int s = 1; s < MAX_S; s++)
-                    if (pending & (1u << s)) w[s] = ld_relaxed_u64(p.apart + (head_base + (size_t)s * G + h) * APART_STRIDE + d);
-                if ((pending & 1u) && word_tag(w[0]) == tgB) {
-                    *mldst = word_val(w[0]);
-                    pending &= ~1u;
-                }
+                for (int j = 0; j < 4; j++)
+                    if (tid() < G() * HD && s0 + j < a.S_eff) pending |= 1u << j;
+                uint32_t spins = 0;
+                uint64_t t0 = 0;
+                while (pending && !aborted()) {
+                    u64 w[5];
 #pragma unroll
-                for (int s = 1; s < MAX_S; s++)
-                    if ((pending & (1u << s)) && word_tag(w[s]) == tgB) {
-                        av[s] = word_val(w[s]);
-                        pending &= ~(1u << s);
+                    for (int j = 0; j < 4; j++)
+                        if (pending & (1u << j)) w[j] = ld_relaxed_u64(p.apart + (head_base + (size_t)(s0 + j) * G() + h) * APART_STRIDE + d);
+                    if (pending & 16u) w[4] = ld_relaxed_u64(mlsrc);
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+                        if ((pending & (1u << j)) && word_tag(w[j]) == tgB) {
+                            stage[(s0 + j - 1) * (G() * HD) + tid()] = word_val(w[j]);
+                            pending &= ~(1u << j);
+                        }
+                    if ((pending & 16u) && word_tag(w[4]) == tgB) {
+                        *mldst = word_val(w[4]);
+                        pending &= ~16u;
                     }
-                if (pending && wait_expired(spins, t0, DERR_TIMEOUT_DATA, (int)tgB)) break;
-            }
-        }
-        named_bar_sync(1, NCT);
-        if (tid < G * HD) {
-            const int h = tid >> 7, d = tid & (HD - 1);
-            float M = -INFINITY;
-            for (int s = 0; s < a.S_eff; s++) M = fmaxf(M, sm.ml[s][h][0]);
-            float Lt = 0.f, O = 0.f;
-#pragma unroll
-            for (int s = 0; s < MAX_S; s++) {
-                if (s < a.S_eff) {
-                    const float w = expf(sm.ml[s][h][0] - M);
-                    Lt = fmaf(w, sm.ml[s][h][1], Lt);
-                    O = fmaf(w, av[s], O);
+                    if (pending) {
+                        if (wait_expired(spins, t0, DERR_TIMEOUT_DATA, (int)tgB)) break;
+                        if (p.poll_ns) __nanosleep(p.poll_ns);
+                    }
                 }
+                mlsrc = nullptr;
             }
-            st_relaxed_u64(p.att + (size_t)(a.g * G + h) * HD + d, tagged(O / Lt, tgB));
         }
+        stamp(step, l * TRACE_PER_LAYER + 12);
+        named_bar_sync(1, NCT);
+        if (tid() < G() * HD) {
+            const int h = tid() >> 7, d = tid() & (HD - 1);
+            float M = -INFINITY;
+            for (int s = 0; s < a.S_eff; s++) M = fmaxf(M, qw_sm.ml[s][h][0]);
+            float Lt = 0.f, O = 0.f;
+            for (int s = 0; s < a.S_eff; s++) {
+                const float w = expf(qw_sm.ml[s][h][0] - M);
+                Lt = fmaf(w, qw_sm.ml[s][h][1], Lt);
+                O = fmaf(w, s == 0 ? acc : stage[(s - 1) * (G() * HD) + tid()], O);
+            }
+            st_relaxed_u64(p.att + (size_t)(a.g * G() + h) * HD + d, tagged(O / Lt, tgB));
+        }
+        stamp(step, l * TRACE_PER_LAYER + 13);
+        named_bar_sync(1, NCT);  // the stage lives in part, which the next phase's GEMV overwrites
     }
 
     // ------------------------------------------------------------------ lm_head + argmax
-    __device__ void lm_epilogue() {
-        const GemvGeo& g = gF;
+    __device__ __noinline__ void lm_epilogue() {
+        const GemvGeo& g = gF();
         const int nloc = g.r1 - g.r0;
         float bv = -INFINITY;
         unsigned bi = NONE_IDX;
-        for (int i = tid; i < nloc; i += NCT) {
+        for (int i = tid(); i < nloc; i += NCT) {
             const float y = row_value(g, i);
             const unsigned row = (unsigned)(g.r0 + i);
             if (p.logits) __stcg(p.logits + row, y);
@@ -654,22 +749,22 @@ public:
             const unsigned oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
             if (am_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
         }
-        if (lane == 0) { sm.redv[warp] = bv; sm.redi[warp] = bi; }
+        if (lane() == 0) { qw_sm.redv[warp()] = bv; qw_sm.redi[warp()] = bi; }
         named_bar_sync(1, NCT);
-        if (tid == 0) {
+        if (tid() == 0) {
             for (int w = 1; w < NCW; w++)
-                if (am_better(sm.redv[w], sm.redi[w], bv, bi)) { bv = sm.redv[w]; bi = sm.redi[w]; }
-            __stcg(p.am_val + cta, bv);
-            __stcg(p.am_idx + cta, bi);
+                if (am_better(qw_sm.redv[w], qw_sm.redi[w], bv, bi)) { bv = qw_sm.redv[w]; bi = qw_sm.redi[w]; }
+            __stcg(p.am_val + cta(), bv);
+            __stcg(p.am_idx + cta(), bi);
         }
     }
 
     // after the end-of-token barrier: every CTA reduces the partials to the same next token
-    __device__ unsigned argmax_combine() {
-        if (warp == 0) {
+    __device__ __noinline__ unsigned argmax_combine() {
+        if (warp() == 0) {
             float bv = -INFINITY;
             unsigned bi = NONE_IDX;
-            for (int j = lane; j < n; j += 32) {
+            for (int j = lane(); j < nctas(); j += 32) {
                 const float v = __ldcg(p.am_val + j);
                 const unsigned i = __ldcg(p.am_idx + j);
                 if (am_better(v, i, bv, bi)) { bv = v; bi = i; }
@@ -680,24 +775,24 @@ public:
                 const unsigned oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
                 if (am_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
             }
-            if (lane == 0) {
+            if (lane() == 0) {
                 unsigned t = bi;
                 if (__ldcg(p.nan0) != 0 || t == NONE_IDX || t >= (unsigned)p.V) t = 0;  // first-strict-max rule
-                sm.token = t;
+                qw_sm.token = t;
             }
         }
         named_bar_sync(1, NCT);
-        return sm.token;
+        return qw_sm.token;
     }
 
-    __device__ void store_rows(u64* dst, const GemvGeo& g, uint32_t tg) {
-        for (int i = tid; i < g.r1 - g.r0; i += NCT) st_relaxed_u64(dst + g.r0 + i, tagged(row_value(g, i), tg));
+    __device__ __noinline__ void store_rows(u64* dst, const GemvGeo& g, uint32_t tg) {
+        for (int i = tid(); i < g.r1 - g.r0; i += NCT) st_relaxed_u64(dst + g.r0 + i, tagged(row_value(g, i), tg));
     }
 
-    __device__ void residual_rows(const GemvGeo& g, uint32_t tg) {  // x[r] += y[r] on this CTA's rows
-        for (int i = tid; i < g.r1 - g.r0; i += NCT) {
-            const float v = xloc[i] + row_value(g, i);
-            xloc[i] = v;
+    __device__ __noinline__ void residual_rows(const GemvGeo& g, uint32_t tg) {  // x[r] += y[r] on this CTA's rows
+        for (int i = tid(); i < g.r1 - g.r0; i += NCT) {
+            const float v = xloc()[i] + row_value(g, i);
+            xloc()[i] = v;
             st_relaxed_u64(p.x + g.r0 + i, tagged(v, tg));
         }
     }
@@ -706,7 +801,7 @@ public:
     __device__ void consume() {
         unsigned token = __ldcg(p.tok_in);
         if (token >= (unsigned)p.V) {
-            if (tid == 0) fail(DERR_BAD_TOKEN, (int)token);
+            if (tid() == 0) fail(DERR_BAD_TOKEN, (int)token);
             token = 0;
         }
         for (int step = 0; step < p.steps; step++) {
@@ -714,37 +809,53 @@ public:
             for (int l = 0; l < p.L; l++) {
                 const uint16_t* nrm = p.layer_n + (size_t)l * p.norm_stride;
                 // A: rmsnorm(x) -> q|k|v rows
+                const int tb = l * TRACE_PER_LAYER;
+                stamp(step, tb + 0);
                 norm_prologue(nrm, l == 0, token, l == 0 ? 0u : tag(seq(step, l - 1, 5)));
-                gemv_consume(gA);
-                store_rows(p.qkv, gA, tag(seq(step, l, 1)));
+                stamp(step, tb + 1);
+                gemv_consume(gA());
+                store_rows(p.qkv, gA(), tag(seq(step, l, 1)));
+                stamp(step, tb + 2);
                 // B: q/k norm + rope, KV append, attention (partials, then the chunk-0 merge)
                 attention_consume(step, l, pos);
+                stamp(step, tb + 5);
                 // C: o_proj + residual
-                gather(p.att, QD, tag(seq(step, l, 2)));
-                gemv_consume(gC);
-                residual_rows(gC, tag(seq(step, l, 3)));
+                gather(p.att, QD(), tag(seq(step, l, 2)));
+                stamp(step, tb + 6);
+                gemv_consume(gC());
+                residual_rows(gC(), tag(seq(step, l, 3)));
+                stamp(step, tb + 7);
                 // D: rmsnorm(x) -> gate|up -> silu(gate) * up
                 norm_prologue(nrm + p.H, false, 0, tag(seq(step, l, 3)));
-                gemv_consume(gD);
+                stamp(step, tb + 8);
+                gemv_consume(gD());
                 {
                     const uint32_t tg = tag(seq(step, l, 4));
-                    for (int i = tid; i < (gD.r1 - gD.r0) / 2; i += NCT) {
-                        const float gt = row_value(gD, 2 * i), up = row_value(gD, 2 * i + 1);
-                        st_relaxed_u64(p.hbuf + gD.r0 / 2 + i, tagged(gt / (1.0f + expf(-gt)) * up, tg));
+                    for (int i = tid(); i < (gD().r1 - gD().r0) / 2; i += NCT) {
+                        const float gt = row_value(gD(), 2 * i), up = row_value(gD(), 2 * i + 1);
+                        st_relaxed_u64(p.hbuf + gD().r0 / 2 + i, tagged(gt / (1.0f + expf(-gt)) * up, tg));
                     }
                 }
                 // E: down_proj + residual
+                stamp(step, tb + 9);
                 gather(p.hbuf, p.I, tag(seq(step, l, 4)));
-                gemv_consume(gE);
-                residual_rows(gE, tag(seq(step, l, 5)));
+                stamp(step, tb + 10);
+                gemv_consume(gE());
+                residual_rows(gE(), tag(seq(step, l, 5)));
+                stamp(step, tb + 11);
             }
             // F: final rmsnorm -> lm_head -> argmax partials -> end-of-token barrier -> next token
+            const int tt = p.L * TRACE_PER_LAYER;
             norm_prologue(p.final_norm, false, 0, tag(seq(step, p.L - 1, 5)));
-            gemv_consume(gF);
+            stamp(step, tt + 0);
+            gemv_consume(gF());
             lm_epilogue();
+            stamp(step, tt + 1);
             token_barrier((uint32_t)step + 1);
+            stamp(step, tt + 2);
             token = argmax_combine();
-            if (cta == 0 && tid == 0 && !aborted()) {
+            stamp(step, tt + 3);
+            if (cta() == 0 && tid() == 0 && !aborted()) {
                 if (p.tok_out) p.tok_out[step + 1] = token;
                 if (p.host_tok) {
                     volatile uint32_t* ht = p.host_tok;
@@ -760,25 +871,26 @@ public:
     __device__ bool slot_acquire(uint32_t& slot) {
         slot = it % NSLOT;
         const uint32_t par = ((it / NSLOT) & 1) ^ 1;
-        return wait_mbar(&sm.empty[slot], par, DERR_TIMEOUT_EMPTY);
+        return wait_mbar(&qw_sm.empty[slot], par, DERR_TIMEOUT_EMPTY);
     }
 
-    __device__ void gemv_produce(const GemvGeo& g, const uint16_t* wbase, uint64_t pol) {
+    __device__ __noinline__ void gemv_produce(const GemvGeo& g, const uint16_t* wbase, uint64_t pol) {
         for (int r = g.r0; r < g.r1; r += g.rpp) {
             const int nr = min(g.rpp, g.r1 - r);
             uint32_t slot;
             if (slot_acquire(slot)) {
                 const uint32_t bytes = (uint32_t)nr * (uint32_t)g.K * 2u;
-                mbar_arrive_expect_tx(&sm.full[slot], bytes);
-                bulk_g2s_evict_first(ring + slot * SLOT_BYTES, wbase + g.woff + (size_t)r * g.K, bytes, &sm.full[slot], pol);
+                mbar_arrive_expect_tx(&qw_sm.full[slot], bytes);
+                bulk_g2s_evict_first(ring() + slot * SLOT_BYTES, wbase + g.woff + (size_t)r * g.K, bytes, &qw_sm.full[slot], pol);
+                piece_stamp(it, 0);
                 n_issued = it + 1;
             }
             ++it;
         }
     }
 
-    __device__ void attn_produce(int step, int l, int pos) {
-        const AttnItem a = attn_item(p, cta, pos);
+    __device__ __noinline__ void attn_produce(int step, int l, int pos) {
+        const AttnItem a = attn_item(p, cta(), pos);
         if (!a.active) return;
         const int tc1 = a.has_cur ? pos : a.t1;
         if (a.t0 >= tc1) return;
@@ -788,7 +900,7 @@ public:
         if (step > 0 && !aborted() && l == 0) {
             uint32_t spins = 0;
             uint64_t t0 = 0;
-            while (ld_acquire_cta_shared(&sm.progress) < (uint32_t)step) {
+            while (ld_acquire_cta_shared(&qw_sm.progress) < (uint32_t)step) {
                 if (wait_expired(spins, t0, DERR_TIMEOUT_KV, step)) break;
                 __nanosleep(32);
             }
@@ -800,29 +912,52 @@ public:
             uint32_t slot;
             if (slot_acquire(slot)) {
                 const uint32_t bytes = (uint32_t)np * HD * 4u;
-                mbar_arrive_expect_tx(&sm.full[slot], 2u * bytes);
-                uint8_t* dst = ring + slot * SLOT_BYTES;
-                bulk_g2s(dst, p.kc + (head + t) * HD, bytes, &sm.full[slot]);
-                bulk_g2s(dst + ATT_P * HD * 4, p.vc + (head + t) * HD, bytes, &sm.full[slot]);
+                mbar_arrive_expect_tx(&qw_sm.full[slot], 2u * bytes);
+                uint8_t* dst = ring() + slot * SLOT_BYTES;
+                bulk_g2s(dst, p.kc + (head + t) * HD, bytes, &qw_sm.full[slot]);
+                bulk_g2s(dst + ATT_P * HD * 4, p.vc + (head + t) * HD, bytes, &qw_sm.full[slot]);
                 n_issued = it + 1;
             }
             ++it;
         }
     }
 
+    // warm L2 with this CTA's rows of one layer (A, C, D, E), so the ring's bulk copies of that
+    // layer hit L2: the ring holds less than a layer, and without this the next layer's first
+    // pieces would be fetched from HBM only once the current layer's last pieces are released
+    __device__ __noinline__ void prefetch_layer(const uint16_t* W) const {
+        const GemvGeo* gs[4] = {&gA(), &gC(), &gD(), &gE()};
+        for (int k = 0; k < 4; k++) {
+            const GemvGeo& g = *gs[k];
+            const uint32_t bytes = (uint32_t)(g.r1 - g.r0) * (uint32_t)g.K * 2u;
+            if (bytes) bulk_prefetch_l2(W + g.woff + (size_t)g.r0 * g.K, bytes);
+        }
+    }
+
+    __device__ void prefetch_lm_head() const {
+        const GemvGeo& g = gF();
+        const uint32_t all = (uint32_t)(g.r1 - g.r0) * (uint32_t)g.K * 2u;
+        const uint32_t bytes = all < LM_PREFETCH_BYTES ? all : LM_PREFETCH_BYTES;
+        if (bytes) bulk_prefetch_l2(p.lm_head + (size_t)g.r0 * g.K, bytes);
+    }
+
     __device__ void produce() {
         const uint64_t pol = policy_evict_first();
+        prefetch_layer(p.layer_w);
         for (int step = 0; step < p.steps; step++) {
             const int pos = p.start_pos + step;
             for (int l = 0; l < p.L; l++) {
                 const uint16_t* W = p.layer_w + (size_t)l * p.layer_stride;
-                gemv_produce(gA, W, pol);
+                if (l + 1 < p.L) prefetch_layer(W + p.layer_stride);
+                else prefetch_lm_head();
+                gemv_produce(gA(), W, pol);
                 attn_produce(step, l, pos);
-                gemv_produce(gC, W, pol);
-                gemv_produce(gD, W, pol);
-                gemv_produce(gE, W, pol);
+                gemv_produce(gC(), W, pol);
+                gemv_produce(gD(), W, pol);
+                gemv_produce(gE(), W, pol);
             }
-            gemv_produce(gF, p.lm_head, pol);
+            if (step + 1 < p.steps) prefetch_layer(p.layer_w);
+            gemv_produce(gF(), p.lm_head, pol);
         }
         drain();
     }
@@ -831,14 +966,14 @@ public:
     // abort, wait (bounded) for the copies still in flight before the CTA may exit. Consumers stop
     // releasing slots once they abort, so only the last NSLOT issued pieces can be outstanding,
     // one per slot.
-    __device__ void drain() {
+    __device__ __noinline__ void drain() {
         if (aborted()) {
             const uint32_t first = n_issued > NSLOT ? n_issued - NSLOT : 0;
             for (uint32_t j = first; j < n_issued; j++) {
                 const int slot = j % NSLOT;
                 const uint32_t par = (j / NSLOT) & 1;
                 const uint64_t t0 = globaltimer_ns();
-                while (!mbar_try_wait(&sm.full[slot], par)) {
+                while (!mbar_try_wait(&qw_sm.full[slot], par)) {
                     if (globaltimer_ns() - t0 > (uint64_t)p.timeout_ns) {
                         atomicCAS(&p.err[3], 0, DERR_TIMEOUT_DRAIN);
                         break;

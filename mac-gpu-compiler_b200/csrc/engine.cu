@@ -91,25 +91,23 @@ int* device_err_word_for(int device) {
 namespace qw {
 
 // the persistent decode kernel (device code in decode_kernel.cuh)
-// 416 threads x 152 registers fit one CTA per SM (65536 registers)
-__global__ void __maxnreg__(152) decode_kernel(const __grid_constant__ DecodeParams p) {
-    __shared__ Smem sm;
-    extern __shared__ __align__(128) uint8_t dyn[];
+// 13 warps: one SM sub-partition holds 4 of them, so 16K registers / 128 threads caps it at 128 each
+__global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
     if (threadIdx.x == 0) {
         for (int i = 0; i < NSLOT; i++) {
-            mbar_init(&sm.full[i], 1);
-            mbar_init(&sm.empty[i], NCW);
+            mbar_init(&qw_sm.full[i], 1);
+            mbar_init(&qw_sm.empty[i], NCW);
         }
-        sm.progress = 0;
-        sm.abort = 0;
-        sm.token = 0;
-        Decoder::init_geometry(p, sm);
+        qw_sm.progress = 0;
+        qw_sm.abort = 0;
+        qw_sm.token = 0;
+        Decoder::init_geometry(p);
         fence_mbar_init();
     }
     __syncthreads();
-    Decoder d(p, sm, dyn);
-    if (d.warp == NCW) {
-        if (d.lane == 0) d.produce();
+    Decoder d(p);
+    if (Decoder::warp() == NCW) {
+        if (Decoder::lane() == 0) d.produce();
         return;
     }
     d.consume();
@@ -147,8 +145,10 @@ struct qw_model {
     float* h_logits = nullptr;   // pinned [vocab]
     unsigned epoch = 0;
     int S = 0, part_cap = 0, xs_cap = 0, xloc_cap = 0;
+    u64* d_trace = nullptr;      // phase timeline of the most recent launch's first step, if enabled
     size_t dyn_smem = 0;
     long long timeout_ns = 0;
+    int poll_ns = 0;
 };
 
 // A cache never dereferences its model after qw_cache_new: it keeps what it needs (device,
@@ -213,6 +213,7 @@ int launch_decode(qw_model* m, qw_cache* c, const uint32_t* tok_in, uint32_t* to
     p.flags = m->d_flags;
     p.err = m->d_err;
     p.logits = logits;
+    p.trace = m->d_trace;
     p.tok_in = tok_in;
     p.tok_out = tok_out;
     p.host_tok = stream_to_host ? m->h_tok_dev : nullptr;
@@ -236,6 +237,7 @@ int launch_decode(qw_model* m, qw_cache* c, const uint32_t* tok_in, uint32_t* to
     p.xs_cap = m->xs_cap;
     p.xloc_cap = m->xloc_cap;
     p.timeout_ns = m->timeout_ns;
+    p.poll_ns = m->poll_ns;
     void* args[] = {&p};
     cudaError_t e = cudaLaunchCooperativeKernel((const void*)decode_kernel, dim3(m->nctas), dim3(NTHREADS), args,
                                                 m->dyn_smem, s);
@@ -299,6 +301,7 @@ int qw_load(const char* path, int device, qw_model** out) {
     m->cfg = c;
     m->wbytes = f.weight_bytes_per_token();
     m->timeout_ns = timeout_ns_from_env();
+    if (const char* e = std::getenv("QW_POLL_NS")) m->poll_ns = std::max(0, std::min(10000, std::atoi(e)));
     int nctas = prop.multiProcessorCount;
     if (const char* e = std::getenv("QW_CTAS")) nctas = std::max(1, std::min(nctas, std::atoi(e)));
     // Buffers are reused across phases on the premise that every CTA contributes to every GEMV
@@ -377,7 +380,8 @@ int qw_load(const char* path, int device, qw_model** out) {
     auto ceil_div = [](uint64_t a, uint64_t b) { return (a + b - 1) / b; };
     auto phase_cap = [&](uint64_t rows, uint64_t K) { return (uint64_t)seg_count((int)K) * (ceil_div(rows, nctas) + 2); };
     uint64_t pc = std::max({phase_cap(QKVR, H), phase_cap(H, QD), phase_cap(2 * I, H) + 2, phase_cap(H, I), phase_cap(c.vocab, H)});
-    m->part_cap = (int)align_up(pc, 4);
+    // part also stages the attention merge's partials: (S - 1) chunks x G heads x 128
+    m->part_cap = (int)align_up(std::max<uint64_t>(pc, (uint64_t)(m->S - 1) * G * HD), 4);
     m->xs_cap = (int)align_up(std::max({H, QD, I}), 4);
     m->xloc_cap = (int)align_up(ceil_div(H, nctas) + 2, 4);
     m->dyn_smem = (size_t)NSLOT * SLOT_BYTES + ((size_t)m->part_cap + m->xs_cap + m->xloc_cap) * 4;
@@ -421,6 +425,7 @@ void qw_free(qw_model* m) {
     cudaFree(m->d_weights);
     cudaFree(m->d_scratch);
     cudaFree(m->d_tok);
+    cudaFree(m->d_trace);
     if (m->h_tok) cudaFreeHost(m->h_tok);
     if (m->h_stage) cudaFreeHost(m->h_stage);
     if (m->h_logits) cudaFreeHost(m->h_logits);
@@ -440,6 +445,37 @@ uint64_t qw_weight_bytes_per_token(const qw_model* m) { return m ? m->wbytes : 0
 int qw_num_ctas(const qw_model* m) { return m ? m->nctas : 0; }
 
 void* qw_model_stream(const qw_model* m) { return m ? static_cast<void*>(m->stream) : nullptr; }
+
+size_t qw_trace_stride(const qw_model* m) { return m ? (size_t)TRACE_PER_LAYER * m->cfg.layers + 4 : 0; }
+
+// stamps the trace buffer holds: num_ctas * stride phase stamps, then 4 * TRACE_PIECES ring stamps of CTA 0
+static size_t trace_words(const qw_model* m) { return (size_t)m->nctas * qw_trace_stride(m) + 4 * (size_t)TRACE_PIECES; }
+
+int qw_set_trace(qw_model* m, int enable) {
+    if (!m) return set_err(QW_ERR_ARG, "null handle");
+    QW_CUDA(cudaSetDevice(m->device));
+    if (enable && !m->d_trace) {
+        const size_t bytes = trace_words(m) * 8;
+        if (cudaMalloc(&m->d_trace, bytes) != cudaSuccess) return set_err(QW_ERR_NOMEM, "trace allocation failed");
+        QW_CUDA(cudaMemset(m->d_trace, 0, bytes));
+    } else if (!enable && m->d_trace) {
+        QW_CUDA(cudaStreamSynchronize(m->stream));
+        cudaFree(m->d_trace);
+        m->d_trace = nullptr;
+    }
+    return QW_OK;
+}
+
+int qw_read_trace(qw_model* m, uint64_t* out, size_t capacity) {
+    if (!m || !out) return set_err(QW_ERR_ARG, "null argument");
+    if (!m->d_trace) return set_err(QW_ERR_ARG, "tracing is not enabled");
+    const size_t n = trace_words(m);
+    if (capacity < n) return set_err(QW_ERR_ARG, "trace buffer too small");
+    QW_CUDA(cudaSetDevice(m->device));
+    QW_CUDA(cudaStreamSynchronize(m->stream));
+    QW_CUDA(cudaMemcpy(out, m->d_trace, n * 8, cudaMemcpyDeviceToHost));
+    return QW_OK;
+}
 
 int qw_cache_new(qw_model* m, size_t max_seq, qw_cache** out) {
     if (!m || !out) return set_err(QW_ERR_ARG, "null argument");

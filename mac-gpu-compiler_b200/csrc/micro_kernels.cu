@@ -24,32 +24,30 @@ namespace {
 
 __global__ void __launch_bounds__(NTHREADS, 1)
 gemv_kernel(const __grid_constant__ DecodeParams p, const uint16_t* w, const float* x, float* y, int rows, int cols) {
-    __shared__ Smem sm;
-    extern __shared__ __align__(128) uint8_t dyn[];
     if (threadIdx.x == 0) {
         for (int i = 0; i < NSLOT; i++) {
-            mbar_init(&sm.full[i], 1);
-            mbar_init(&sm.empty[i], NCW);
+            mbar_init(&qw_sm.full[i], 1);
+            mbar_init(&qw_sm.empty[i], NCW);
         }
-        sm.progress = 0;
-        sm.abort = 0;
-        Decoder::init_geometry(p, sm);
+        qw_sm.progress = 0;
+        qw_sm.abort = 0;
+        qw_sm.geo[0] = make_geo(rows, cols, blockIdx.x, gridDim.x, 0, 0);
         fence_mbar_init();
     }
     __syncthreads();
-    Decoder d(p, sm, dyn);
-    const GemvGeo g = make_geo(rows, cols, blockIdx.x, gridDim.x, 0, 0);
-    if (d.warp == NCW) {
-        if (d.lane == 0) {
+    Decoder d(p);
+    const GemvGeo& g = qw_sm.geo[0];
+    if (Decoder::warp() == NCW) {
+        if (Decoder::lane() == 0) {
             d.gemv_produce(g, w, policy_evict_first());
             d.drain();
         }
         return;
     }
-    for (int i = d.tid; i < cols; i += NCT) d.xs[i] = x[i];
+    for (int i = Decoder::tid(); i < cols; i += NCT) Decoder::xs()[i] = x[i];
     named_bar_sync(1, NCT);
     d.gemv_consume(g);
-    for (int i = d.tid; i < g.r1 - g.r0; i += NCT) y[g.r0 + i] = d.row_value(g, i);
+    for (int i = Decoder::tid(); i < g.r1 - g.r0; i += NCT) y[g.r0 + i] = d.row_value(g, i);
 }
 
 // argmax with the reference CPU rule, in two levels inside one launch (last-block reduction)
@@ -153,9 +151,8 @@ extern "C" {
 
 int qw_gemv_bf16(int device, const uint16_t* d_w, const float* d_x, float* d_y, size_t rows, size_t cols, void* stream) {
     if (!d_w || !d_x || !d_y || rows == 0) return set_error(QW_ERR_ARG, "bad gemv arguments");
-    const bool ok_cols = cols % 256 == 0 && cols > 0 &&
-                         (cols <= 1024 || (cols % 1024 == 0 && 12 % (cols / 1024) == 0 && cols <= 12288));
-    if (!ok_cols) return set_error(QW_ERR_UNSUPPORTED, "cols must be a multiple of 256 (<= 1024) or of 1024 dividing 12288");
+    if (cols == 0 || cols > 12288 || seg_count((int)cols) == 0)
+        return set_error(QW_ERR_UNSUPPORTED, "cols must split into 1, 2, 3, 4, 6 or 12 segments of 256-1024 columns");
     if (rows >= (1u << 30)) return set_error(QW_ERR_ARG, "rows too large");
     if (cudaSetDevice(device) != cudaSuccess) return set_error(QW_ERR_CUDA, "cudaSetDevice failed");
     int* err = device_err_word_for(device);

@@ -36,6 +36,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
+// non-blocking test of phase `parity` (never suspends the thread)
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+
 // ---- TMA bulk copy (cp.async.bulk, 1-D, no multicast) -------------------------------------
 // dst/src 16-byte aligned, bytes a multiple of 16; completion is signalled on `bar` as tx bytes
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -54,6 +62,11 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
     return p;
+}
+
+// warm L2 with [src, src + bytes) (16-byte aligned, multiple of 16); no completion to track
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
 // orders generic-proxy global writes observed through an acquire before later async-proxy reads
@@ -85,15 +98,17 @@ __device__ __forceinline__ uint32_t ld_acquire_cta_shared(const uint32_t* p) {
 }
 
 // relaxed gpu-scope accesses: served by L2 (never a stale L1 line); 8-byte accesses are single-copy
-// atomic, which the tagged-word hand-off between CTAs relies on
+// atomic, which the tagged-word hand-off between CTAs relies on. The polling loads carry no
+// "memory" clobber: each value is validated by its own tag, so the compiler may keep many of them
+// in flight and schedule other memory operations (spills, shared-memory stores) around them.
 __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
     unsigned long long v;
-    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p));
     return v;
 }
 __device__ __forceinline__ ulonglong2 ld_relaxed_v2u64(const unsigned long long* p) {  // 16-byte aligned
     ulonglong2 v;
-    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(v.x), "=l"(v.y) : "l"(p));
     return v;
 }
 __device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {

@@ -92,6 +92,9 @@ def lib() -> ctypes.CDLL:
             "qw_cache_read": (i32, [vp, sz, sz, vp, vp]),
             "qw_num_ctas": (i32, [vp]),
             "qw_model_stream": (vp, [vp]),
+            "qw_trace_stride": (sz, [vp]),
+            "qw_set_trace": (i32, [vp, i32]),
+            "qw_read_trace": (i32, [vp, ctypes.POINTER(ctypes.c_uint64), sz]),
             "qw_gemv_bf16": (i32, [i32, vp, vp, vp, sz, sz, vp]),
             "qw_argmax_workspace_size": (sz, [sz]),
             "qw_argmax_f32": (i32, [i32, vp, sz, vp, vp, vp]),
@@ -145,6 +148,20 @@ class CudaModel:
     def stream(self) -> int:
         """The model's cudaStream_t handle (forward/decode run on it)."""
         return int(lib().qw_model_stream(self._h) or 0)
+
+    def set_trace(self, enable: bool) -> None:
+        """Record a per-CTA phase timeline of each launch's first step (see include/cuda_inference.h)."""
+        _check(lib().qw_set_trace(self._h, 1 if enable else 0))
+
+    TRACE_PIECES = 1024
+
+    def read_trace(self) -> tuple[np.ndarray, np.ndarray]:
+        """([num_ctas, stride] phase stamps, [TRACE_PIECES, 4] CTA-0 ring stamps), globaltimer ns."""
+        stride = int(lib().qw_trace_stride(self._h))
+        n = self.num_ctas * stride + 4 * self.TRACE_PIECES
+        out = np.zeros(n, np.uint64)
+        _check(lib().qw_read_trace(self._h, out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), out.size))
+        return out[: self.num_ctas * stride].reshape(self.num_ctas, stride), out[self.num_ctas * stride:].reshape(-1, 4)
 
     def forward(self, token: int, pos: int, cache: "CudaKVCache") -> np.ndarray:
         out = np.empty(self.config.vocab_size, np.float32)
