@@ -112,10 +112,8 @@ int qw_num_ctas(const qw_model* model);
 void* qw_model_stream(const qw_model* model);
 
 /* Phase timeline (tracing): when enabled, every launch records, for its first step, per CTA,
- * qw_trace_stride() globaltimer stamps (ns): 12 per layer at the phase hand-offs, then 4 for the
- * lm_head / argmax tail; then, for CTA 0, 4 stamps per weight/KV ring piece (up to 1024 pieces:
- * issued, wait started, data ready, released). qw_read_trace copies
- * num_ctas * stride + 4096 stamps of the most recent launch.
+ * qw_trace_stride() globaltimer stamps (ns): 14 per layer at the phase hand-offs, then 4 for the
+ * lm_head / argmax tail. qw_read_trace copies num_ctas * stride stamps of the most recent launch.
  * The reference measured its per-part breakdown by ablation (README.md:64-71); this records it. */
 size_t qw_trace_stride(const qw_model* model);
 int qw_set_trace(qw_model* model, int enable);

@@ -60,6 +60,10 @@ constexpr uint32_t LM_PREFETCH_BYTES = 256u * 1024;  // lm_head bytes per CTA wa
 constexpr int APART_STRIDE = HD + 4;          // words per attention partial: acc[128], m, l, pad
 constexpr int GP = 4;                         // tagged word pairs a consumer thread polls at once
 constexpr uint32_t NONE_IDX = 0xFFFFFFFFu;
+// Math: the softmax / SiLU exponentials use __expf and the RMSNorm scales rsqrtf (hardware
+// approximations, ~1e-6 relative error): the inline IEEE expansions of expf and 1/sqrtf would
+// roughly double the code that every layer executes, which costs far more in instruction fetch
+// than the accuracy is worth against the 1e-2 logit bar (results stay ~1e-5 from the CPU oracle).
 // phase timeline (optional): per layer, stamps after: 0 layer start, 1 A input ready (x gathered +
 // rmsnorm), 2 A rows stored, 3 B inputs ready (q/k/v gathered, norm+RoPE), 4 B chunk done,
 // 5 B merged/published, 6 C input ready (att gathered), 7 C rows stored, 8 D input ready,
@@ -67,9 +71,6 @@ constexpr uint32_t NONE_IDX = 0xFFFFFFFFu;
 // polled, 13 (merging CTAs) attention output published; then 4 stamps for the token
 // tail: lm_head input ready, lm_head done, end-of-token barrier passed, next token known
 constexpr int TRACE_PER_LAYER = 14;
-// ...followed (after all CTAs' stamps) by CTA 0's ring timeline of step 0: per ring piece
-// {producer issued, consumer started waiting, data ready, consumer done}, up to TRACE_PIECES pieces
-constexpr int TRACE_PIECES = 1024;
 
 // error codes written to DecodeParams::err[0]
 enum : int { DERR_NONE = 0, DERR_TIMEOUT_GRID = 1, DERR_TIMEOUT_FULL = 2, DERR_TIMEOUT_EMPTY = 3,
@@ -127,18 +128,18 @@ struct GemvGeo {
     int K;            // columns
     int rpp;          // rows per ring slot
     int segs;         // column segments per row (K / segw), see seg_count
-    int segw;         // columns per segment (256, 512, 768 or 1024)
+    int segw;         // columns per segment (<= 1024)
     int cpl;          // 16-byte chunks per lane per segment (segw / 256)
     long long woff;   // element offset of the matrix inside a layer block
 };
 
-// Column segments per row: the narrowest segment width (256, 512, 768 or 1024 columns) whose count
-// divides the 12 consumer warps, so that each warp keeps one fixed segment of x in registers
-// (segw / 32 values) and covers 1024 / segw rows of every ring piece.
+// Column segments per row: rows of up to 1024 columns are one segment; wider rows split into
+// 1024-column segments, and their count must divide the 12 consumer warps (so that each warp keeps
+// one fixed segment of x in registers).
 __host__ __device__ inline int seg_count(int K) {
-    for (int segw = 256; segw <= 1024; segw += 256)
-        if (K % segw == 0 && 12 % (K / segw) == 0) return K / segw;
-    return 0;  // unsupported (rejected on the host)
+    if (K <= 0 || K % 256 != 0) return 0;
+    if (K <= 1024) return 1;
+    return (K % 1024 == 0 && 12 % (K / 1024) == 0) ? K / 1024 : 0;
 }
 
 __device__ inline GemvGeo make_geo(long long rows, int K, int cta, int n, long long woff, int pair) {
@@ -291,11 +292,7 @@ public:
         if (p.trace != nullptr && step == 0 && tid() == 0)
             p.trace[(size_t)cta() * (TRACE_PER_LAYER * p.L + 4) + idx] = globaltimer_ns();
     }
-    // CTA 0's per-piece ring timeline (field 0 producer issue, 1 wait start, 2 ready, 3 done)
-    __device__ __forceinline__ void piece_stamp(uint32_t piece, int field) const {
-        if (p.trace != nullptr && cta() == 0 && piece < (uint32_t)TRACE_PIECES && (field == 0 || tid() == 0))
-            p.trace[(size_t)nctas() * (TRACE_PER_LAYER * p.L + 4) + piece * 4 + field] = globaltimer_ns();
-    }
+
 
     // ------------------------------------------------------------------ errors and waits
     __device__ bool aborted() const { return *reinterpret_cast<volatile const int*>(&qw_sm.abort) != 0; }
@@ -309,26 +306,40 @@ public:
         }
     }
 
-    // called between unsuccessful polls; returns true when the caller must stop waiting. Cheap on
-    // the fast path: only every 32nd call reads the timer and the CTA's abort flag; the global error
-    // word (another CTA gave up) is read only after 50 us of waiting, since a global load here would
-    // add an L2 round trip to every ring hand-off.
-    __device__ __noinline__ bool wait_expired(uint32_t& spins, uint64_t& t0, int code, int where) {
-        ++spins;
-        if ((spins & 31) != 0) return false;
-        if (aborted()) return true;
+    // Called between unsuccessful polls; returns true when the caller must stop waiting. Inline and
+    // nearly free on the fast path: only every 32nd call goes out of line to read the timer, the
+    // CTA's abort flag and (after 50 us) the global error word. Arguments pass by value: an
+    // out-of-line call per polling round, or references to the loop counters, would move the
+    // polling state through the stack on every round.
+    __device__ __forceinline__ bool wait_expired(uint32_t& spins, uint64_t& t0, int code, int where) {
+        if ((++spins & 31) != 0) return false;
+        t0 = wait_check(spins, t0, code, where);
+        return t0 == ~0ull;
+    }
+
+    // returns the (possibly started) wait start time, or ~0 when the wait must end
+    __device__ __noinline__ uint64_t wait_check(uint32_t spins, uint64_t t0, int code, int where) {
+        if (aborted()) return ~0ull;
         const uint64_t now = globaltimer_ns();
-        if (spins == 32) { t0 = now; return false; }
+        if (spins == 32) return now;
         const uint64_t waited = now - t0;
         if (waited > 50000 && (spins & 1023) == 0 && ld_volatile_s32(p.err) != 0) {
             *reinterpret_cast<volatile int*>(&qw_sm.abort) = 1;
-            return true;
+            return ~0ull;
         }
-        if (waited > (uint64_t)p.timeout_ns) { fail(code, where); return true; }
-        return false;
+        if (waited > (uint64_t)p.timeout_ns) {
+            fail(code, where);
+            return ~0ull;
+        }
+        return t0;
     }
 
-    __device__ bool wait_mbar(uint64_t* bar, uint32_t parity, int code) {
+    __device__ __forceinline__ bool wait_mbar(uint64_t* bar, uint32_t parity, int code) {
+        if (mbar_try_wait(bar, parity)) return true;  // fast path: the phase already completed
+        return wait_mbar_slow(bar, parity, code);
+    }
+
+    __device__ __noinline__ bool wait_mbar_slow(uint64_t* bar, uint32_t parity, int code) {
         if (aborted()) return false;
         uint32_t spins = 0;
         uint64_t t0 = 0;
@@ -422,8 +433,17 @@ public:
     // residual rows xloc from that row.
     __device__ __noinline__ void norm_prologue(const uint16_t* w, bool from_embed, unsigned token, uint32_t tg) {
         const int H = p.H;
+        // the gains do not depend on the token: fetch them before waiting for the input
+        constexpr int MAXK = 8;  // H <= 8 * 384 keeps them in registers
+        float wg[MAXK];
+#pragma unroll
+        for (int k = 0; k < MAXK; k++) {
+            const int i = tid() + k * NCT;
+            wg[k] = i < H ? bf16_to_f32(__ldg(w + i)) : 0.f;
+        }
         if (from_embed) {
             const uint16_t* erow = p.embed + (size_t)token * H;
+            #pragma unroll 1
             for (int i = tid(); i < H; i += NCT) {
                 const float v = bf16_to_f32(__ldg(erow + i));
                 xs()[i] = v;
@@ -434,29 +454,45 @@ public:
             gather(p.x, H, tg);
         }
         float ss = 0.f;
-        for (int i = tid(); i < H; i += NCT) ss = fmaf(xs()[i], xs()[i], ss);
+#pragma unroll
+        for (int k = 0; k < MAXK; k++) {
+            const int i = tid() + k * NCT;
+            if (i < H) ss = fmaf(xs()[i], xs()[i], ss);
+        }
+        #pragma unroll 1
+        for (int i = tid() + MAXK * NCT; i < H; i += NCT) ss = fmaf(xs()[i], xs()[i], ss);
         const float tot = block_sum(ss);
-        const float s = 1.0f / sqrtf(tot / (float)H + p.eps);
-        for (int i = tid(); i < H; i += NCT) xs()[i] = xs()[i] * s * bf16_to_f32(__ldg(w + i));
+        const float sc = rsqrtf(tot / (float)H + p.eps);
+#pragma unroll
+        for (int k = 0; k < MAXK; k++) {
+            const int i = tid() + k * NCT;
+            if (i < H) xs()[i] = xs()[i] * sc * wg[k];
+        }
+        #pragma unroll 1
+        for (int i = tid() + MAXK * NCT; i < H; i += NCT) xs()[i] = xs()[i] * sc * bf16_to_f32(__ldg(w + i));
         named_bar_sync(1, NCT);
     }
 
     // All ring pieces of one GEMV phase: part[(row - r0) * segs + seg] = partial dot product.
-    // Warp w owns column segment w % segs (its x values sit in registers: segw / 32 per lane) and
-    // rows w / segs, + 12 / segs, ... of every piece: R = 1024 / segw rows (1, 2 or 4). Lane l reads
-    // 16-byte chunks l, l + 32, ... of the segment, so every shared-memory load is one contiguous
-    // 512-byte warp access; the R row sums are then reduced together by a transposing butterfly
-    // (R = 4: 6 shuffles for the 4 rows instead of 20).
-    __device__ __noinline__ void gemv_consume(const GemvGeo& gs) {
+    // Unit u = (row u / segs, segment u % segs) of a piece goes to warp u % 12; since segs divides
+    // 12 a warp always works on the same segment, whose x values it holds in registers. Lane l
+    // reads 16-byte chunks l, l + 32, ... of the segment, so each shared-memory load is one
+    // contiguous 512-byte warp access.
+    // When a piece holds at most one unit per warp (every Qwen3-0.6B phase), pieces are taken in
+    // groups of up to four: wait for all of them, issue all their loads, run the independent FMA
+    // chains, release the slots, then reduce the group's rows together with one transposing
+    // butterfly (6 shuffles for 4 rows). A layer phase (2-4 pieces, resident in shared memory by
+    // the time its input arrives) is then one group: its cost is the shared-memory traffic, not a
+    // per-piece chain of load, FMA and shuffle latencies.
+    __device__ __noinline__ void gemv_generic(const GemvGeo& gs) {
         const GemvGeo g = gs;  // loop-invariant: keep the phase geometry in registers
-        const int myseg = warp() % g.segs;
-        const int group = warp() / g.segs, ngroups = NCW / g.segs;
-        const int R = 1024 / g.segw;
+        const int w = warp(), ln = lane();
+        const int myseg = w % g.segs;
         float xr[32];
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             if (i < g.cpl) {
-                const float4* xp = reinterpret_cast<const float4*>(xs() + myseg * g.segw + (i * 32 + lane()) * 8);
+                const float4* xp = reinterpret_cast<const float4*>(xs() + myseg * g.segw + (i * 32 + ln) * 8);
                 float4 a = xp[0], b = xp[1];
                 xr[i * 8 + 0] = a.x; xr[i * 8 + 1] = a.y; xr[i * 8 + 2] = a.z; xr[i * 8 + 3] = a.w;
                 xr[i * 8 + 4] = b.x; xr[i * 8 + 5] = b.y; xr[i * 8 + 6] = b.z; xr[i * 8 + 7] = b.w;
@@ -465,62 +501,150 @@ public:
                 for (int j = 0; j < 8; j++) xr[i * 8 + j] = 0.f;
             }
         }
-        for (int r = g.r0; r < g.r1; r += g.rpp) {
-            const int nr = min(g.rpp, g.r1 - r);
-            piece_stamp(it, 1);
-            const bool ok = wait_mbar(&qw_sm.full[it % NSLOT], (it / NSLOT) & 1, DERR_TIMEOUT_FULL);
-            piece_stamp(it, 2);
-            if (ok) {
-                const uint8_t* base = ring() + (it % NSLOT) * SLOT_BYTES + (size_t)myseg * g.segw * 2;
-                float v[4];
+        float* const prt = part();
+        const int npieces = (g.r1 - g.r0 + g.rpp - 1) / g.rpp;
+        uint32_t pc = it;
+        if (g.rpp * g.segs <= NCW) {
+            for (int q0 = 0; q0 < npieces; q0 += 4) {
+                const int n = min(4, npieces - q0);
+                bool ok = true;
+                for (int j = 0; j < n; j++)
+                    ok = wait_mbar(&qw_sm.full[(pc + j) % NSLOT], ((pc + j) / NSLOT) & 1, DERR_TIMEOUT_FULL) && ok;
+                float v[4] = {0.f, 0.f, 0.f, 0.f};
+                int dst[4] = {-1, -1, -1, -1};
+                if (ok) {
+                    uint4 wv[4][4];
 #pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    v[k] = 0.f;
-                    const int rl = group + k * ngroups;
-                    if (k < R && rl < nr) {
+                    for (int j = 0; j < 4; j++) {
+                        const int r = g.r0 + (q0 + j) * g.rpp;
+                        const bool have = j < n && w < min(g.rpp, g.r1 - r) * g.segs;
+                        const int rl = w / g.segs;
+                        if (have) dst[j] = (r - g.r0 + rl) * g.segs + myseg;
+                        const uint4* wp = reinterpret_cast<const uint4*>(
+                            ring() + ((pc + j) % NSLOT) * SLOT_BYTES + ((size_t)rl * g.K + (size_t)myseg * g.segw) * 2);
+#pragma unroll
+                        for (int i = 0; i < 4; i++) wv[j][i] = (have && i < g.cpl) ? wp[i * 32 + ln] : make_uint4(0, 0, 0, 0);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+#pragma unroll
+                        for (int i = 0; i < 4; i++) v[j] += dot8(wv[j][i], xr + i * 8);
+                }
+                __syncwarp();
+                if (ln == 0 && ok)  // a slot is released only after its data landed
+                    for (int j = 0; j < n; j++) mbar_arrive(&qw_sm.empty[(pc + j) % NSLOT]);
+                pc += n;
+                // transposing butterfly: afterwards lanes 0, 8, 16, 24 hold the totals of rows 0..3
+                const bool hi16 = ln & 16, hi8 = ln & 8;
+                float k0 = hi16 ? v[2] : v[0], k1 = hi16 ? v[3] : v[1];
+                k0 += __shfl_xor_sync(0xFFFFFFFFu, hi16 ? v[0] : v[2], 16);
+                k1 += __shfl_xor_sync(0xFFFFFFFFu, hi16 ? v[1] : v[3], 16);
+                float t = hi8 ? k1 : k0;
+                t += __shfl_xor_sync(0xFFFFFFFFu, hi8 ? k0 : k1, 8);
+                t += __shfl_xor_sync(0xFFFFFFFFu, t, 4);
+                t += __shfl_xor_sync(0xFFFFFFFFu, t, 2);
+                t += __shfl_xor_sync(0xFFFFFFFFu, t, 1);
+                const int jj = (hi16 ? 2 : 0) + (hi8 ? 1 : 0);
+                int d = dst[0];
+                if (jj == 1) d = dst[1];
+                if (jj == 2) d = dst[2];
+                if (jj == 3) d = dst[3];
+                if ((ln & 7) == 0 && d >= 0) prt[d] = t;
+            }
+        } else {
+            // small K: several units per warp per piece
+            for (int r = g.r0; r < g.r1; r += g.rpp, ++pc) {
+                const int slot = pc % NSLOT;
+                const bool ok = wait_mbar(&qw_sm.full[slot], (pc / NSLOT) & 1, DERR_TIMEOUT_FULL);
+                if (ok) {
+                    const int units = min(g.rpp, g.r1 - r) * g.segs;
+                    const uint8_t* base = ring() + slot * SLOT_BYTES + (size_t)myseg * g.segw * 2;
+                    for (int u = w; u < units; u += NCW) {
+                        const int rl = u / g.segs;
                         const uint4* wp = reinterpret_cast<const uint4*>(base + (size_t)rl * g.K * 2);
+                        float acc = 0.f;
 #pragma unroll
                         for (int i = 0; i < 4; i++)
-                            if (i < g.cpl) v[k] += dot8(wp[i * 32 + lane()], xr + i * 8);
+                            if (i < g.cpl) acc += dot8(wp[i * 32 + ln], xr + i * 8);
+                        acc = warp_sum(acc);
+                        if (ln == 0) prt[(r - g.r0 + rl) * g.segs + myseg] = acc;
                     }
                 }
-                // transposing butterfly: afterwards lane l holds the total of row k(l)
-                int k_of_lane = 0;
-                float tot;
-                if (R == 4) {
-                    const bool hi16 = lane() & 16;
-                    float keep0 = hi16 ? v[2] : v[0], keep1 = hi16 ? v[3] : v[1];
-                    keep0 += __shfl_xor_sync(0xFFFFFFFFu, hi16 ? v[0] : v[2], 16);
-                    keep1 += __shfl_xor_sync(0xFFFFFFFFu, hi16 ? v[1] : v[3], 16);
-                    const bool hi8 = lane() & 8;
-                    tot = hi8 ? keep1 : keep0;
-                    tot += __shfl_xor_sync(0xFFFFFFFFu, hi8 ? keep0 : keep1, 8);
-                    k_of_lane = (hi16 ? 2 : 0) + (hi8 ? 1 : 0);
-                    tot += __shfl_xor_sync(0xFFFFFFFFu, tot, 4);
-                } else if (R == 2) {
-                    const bool hi16 = lane() & 16;
-                    tot = hi16 ? v[1] : v[0];
-                    tot += __shfl_xor_sync(0xFFFFFFFFu, hi16 ? v[0] : v[1], 16);
-                    k_of_lane = hi16 ? 1 : 0;
-                    tot += __shfl_xor_sync(0xFFFFFFFFu, tot, 8);
-                    tot += __shfl_xor_sync(0xFFFFFFFFu, tot, 4);
-                } else {
-                    tot = v[0];
-                    tot += __shfl_xor_sync(0xFFFFFFFFu, tot, 16);
-                    tot += __shfl_xor_sync(0xFFFFFFFFu, tot, 8);
-                    tot += __shfl_xor_sync(0xFFFFFFFFu, tot, 4);
+                __syncwarp();
+                if (ln == 0 && ok) mbar_arrive(&qw_sm.empty[slot]);
+            }
+        }
+        it = pc;
+    }
+
+    // The Qwen3-0.6B case of gemv_generic, with everything static: 1024-column segments (4 chunks of
+    // 16 bytes per lane) and at most one unit per warp per piece.
+    __device__ __noinline__ void gemv_full_segments(const GemvGeo& gs) {
+        const GemvGeo g = gs;
+        const int w = warp(), ln = lane();
+        const int myseg = w % g.segs, rl = w / g.segs;
+        float xr[32];
+        {
+            const float4* xp = reinterpret_cast<const float4*>(xs() + myseg * 1024 + ln * 8);
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float4 a = xp[i * 64], b = xp[i * 64 + 1];
+                xr[i * 8 + 0] = a.x; xr[i * 8 + 1] = a.y; xr[i * 8 + 2] = a.z; xr[i * 8 + 3] = a.w;
+                xr[i * 8 + 4] = b.x; xr[i * 8 + 5] = b.y; xr[i * 8 + 6] = b.z; xr[i * 8 + 7] = b.w;
+            }
+        }
+        float* const prt = part();
+        const int npieces = (g.r1 - g.r0 + g.rpp - 1) / g.rpp;
+        const size_t woff = ((size_t)rl * g.K + (size_t)myseg * 1024) * 2 + (size_t)ln * 16;
+        uint32_t pc = it;
+        for (int q0 = 0; q0 < npieces; q0 += 4) {
+            const int n = min(4, npieces - q0);
+            bool ok = true;
+            for (int j = 0; j < n; j++)
+                ok = wait_mbar(&qw_sm.full[(pc + j) % NSLOT], ((pc + j) / NSLOT) & 1, DERR_TIMEOUT_FULL) && ok;
+            float v[4] = {0.f, 0.f, 0.f, 0.f};
+            int dst[4] = {-1, -1, -1, -1};
+            if (ok) {
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int r = g.r0 + (q0 + j) * g.rpp;
+                    if (j < n && w < min(g.rpp, g.r1 - r) * g.segs) {
+                        dst[j] = (r - g.r0 + rl) * g.segs + myseg;
+                        const uint4* wp = reinterpret_cast<const uint4*>(ring() + ((pc + j) % NSLOT) * SLOT_BYTES + woff);
+                        uint4 wv[4];
+#pragma unroll
+                        for (int i = 0; i < 4; i++) wv[i] = wp[i * 32];
+#pragma unroll
+                        for (int i = 0; i < 4; i++) v[j] += dot8(wv[i], xr + i * 8);
+                    }
                 }
-                tot += __shfl_xor_sync(0xFFFFFFFFu, tot, 2);
-                tot += __shfl_xor_sync(0xFFFFFFFFu, tot, 1);
-                const int rl = group + k_of_lane * ngroups;
-                if ((lane() & 7) == 0 && k_of_lane < R && rl < nr)
-                    part()[(r - g.r0 + rl) * g.segs + myseg] = tot;
             }
             __syncwarp();
-            if (lane() == 0 && ok) mbar_arrive(&qw_sm.empty[it % NSLOT]);  // a slot is released only after its data landed
-            piece_stamp(it, 3);
-            ++it;
+            if (ln == 0 && ok)  // a slot is released only after its data landed
+                for (int j = 0; j < n; j++) mbar_arrive(&qw_sm.empty[(pc + j) % NSLOT]);
+            pc += n;
+            const bool hi16 = ln & 16, hi8 = ln & 8;
+            float k0 = hi16 ? v[2] : v[0], k1 = hi16 ? v[3] : v[1];
+            k0 += __shfl_xor_sync(0xFFFFFFFFu, hi16 ? v[0] : v[2], 16);
+            k1 += __shfl_xor_sync(0xFFFFFFFFu, hi16 ? v[1] : v[3], 16);
+            float t = hi8 ? k1 : k0;
+            t += __shfl_xor_sync(0xFFFFFFFFu, hi8 ? k0 : k1, 8);
+            t += __shfl_xor_sync(0xFFFFFFFFu, t, 4);
+            t += __shfl_xor_sync(0xFFFFFFFFu, t, 2);
+            t += __shfl_xor_sync(0xFFFFFFFFu, t, 1);
+            const int jj = (hi16 ? 2 : 0) + (hi8 ? 1 : 0);
+            int d = dst[0];
+            if (jj == 1) d = dst[1];
+            if (jj == 2) d = dst[2];
+            if (jj == 3) d = dst[3];
+            if ((ln & 7) == 0 && d >= 0) prt[d] = t;
         }
+        it = pc;
+    }
+
+    __device__ __forceinline__ void gemv_consume(const GemvGeo& g) {
+        if (g.cpl == 4 && g.rpp * g.segs <= NCW) gemv_full_segments(g);
+        else gemv_generic(g);
         named_bar_sync(1, NCT);
     }
 
@@ -533,7 +657,7 @@ public:
     // ------------------------------------------------------------------ attention (phase B)
     // one warp: gather a tagged 128-vector, per-head RMSNorm (q_norm/k_norm), rotate-half RoPE
     // (cpu_inference.rs:134-138, :196-215; the table is the one MetalKVCache builds, :141-154)
-    __device__ float4 gather_head(const u64* src, uint32_t tg) {
+    __device__ __forceinline__ float4 gather_head(const u64* src, uint32_t tg) {
         uint32_t spins = 0;
         uint64_t t0 = 0;
         ulonglong2 a = make_ulonglong2(0, 0), b = make_ulonglong2(0, 0);
@@ -551,10 +675,10 @@ public:
         return make_float4(word_val(a.x), word_val(a.y), word_val(b.x), word_val(b.y));
     }
 
-    __device__ void head_norm_rope(float4 v, const uint16_t* nw, const float2* rrow, float* dst) {
+    __device__ __forceinline__ void head_norm_rope(float4 v, const uint16_t* nw, const float2* rrow, float* dst) {
         float ss = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
         ss = warp_sum(ss);
-        const float s = 1.0f / sqrtf(ss / (float)HD + p.eps);
+        const float s = rsqrtf(ss / (float)HD + p.eps);
         const int d0 = lane() * 4;
         float e[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -570,9 +694,13 @@ public:
         reinterpret_cast<float4*>(dst)[lane()] = make_float4(o[0], o[1], o[2], o[3]);
     }
 
-    // online-softmax update over np positions whose K/V rows (128 f32 each) are in shared memory
-    __device__ void attn_block(const float* Kb, const float* Vb, int np, int buf, const float4* q4,
-                               float& m, float& l, float& acc) {
+    // Online-softmax update over np (<= 32) positions whose K/V rows (128 f32 each) are in shared
+    // memory. Warp w scores positions w, w + 12, ... for the G query heads; then each warp of head h
+    // (thread (h, d) = tid h * 128 + d) turns the np scores into weights P = exp(s - m_new) once per
+    // lane (lane = position), rescales its running (m, l, acc) and adds sum_pp P[pp] * V[pp][d] with
+    // P broadcast by shuffles. Every warp of a head computes the same m and l.
+    __device__ __forceinline__ void attn_block(const float* Kb, const float* Vb, int np, int buf, const float4* q4,
+                                               float& m, float& l, float& acc) {
         for (int pp = warp(); pp < np; pp += NCW) {
             const float4 k4 = reinterpret_cast<const float4*>(Kb + pp * HD)[lane()];
 #pragma unroll
@@ -587,17 +715,19 @@ public:
         named_bar_sync(1, NCT);
         if (tid() < G() * HD) {
             const int h = tid() >> 7, d = tid() & (HD - 1);
-            float mp = -INFINITY;
-            for (int pp = 0; pp < np; pp++) mp = fmaxf(mp, qw_sm.sc[buf][h][pp]);
+            const float sv = lane() < np ? qw_sm.sc[buf][h][lane()] : -INFINITY;
+            float mp = sv;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mp = fmaxf(mp, __shfl_xor_sync(0xFFFFFFFFu, mp, o));
             const float mn = fmaxf(m, mp);
-            const float corr = (m == -INFINITY) ? 0.f : expf(m - mn);
-            l *= corr;
-            acc *= corr;
-            for (int pp = 0; pp < np; pp++) {
-                const float e = expf(qw_sm.sc[buf][h][pp] - mn);
-                l += e;
-                acc = fmaf(e, Vb[pp * HD + d], acc);
-            }
+            const float corr = (m == -INFINITY) ? 0.f : __expf(m - mn);
+            const float pw = lane() < np ? __expf(sv - mn) : 0.f;
+            const float psum = warp_sum(pw);
+            l = l * corr + psum;
+            float a = acc * corr;
+#pragma unroll 4
+            for (int pp = 0; pp < np; pp++) a = fmaf(__shfl_sync(0xFFFFFFFFu, pw, pp), Vb[pp * HD + d], a);
+            acc = a;
             m = mn;
         }
     }
@@ -717,10 +847,12 @@ public:
         if (tid() < G() * HD) {
             const int h = tid() >> 7, d = tid() & (HD - 1);
             float M = -INFINITY;
+            #pragma unroll 1
             for (int s = 0; s < a.S_eff; s++) M = fmaxf(M, qw_sm.ml[s][h][0]);
             float Lt = 0.f, O = 0.f;
+            #pragma unroll 1
             for (int s = 0; s < a.S_eff; s++) {
-                const float w = expf(qw_sm.ml[s][h][0] - M);
+                const float w = __expf(qw_sm.ml[s][h][0] - M);
                 Lt = fmaf(w, qw_sm.ml[s][h][1], Lt);
                 O = fmaf(w, s == 0 ? acc : stage[(s - 1) * (G() * HD) + tid()], O);
             }
@@ -736,6 +868,7 @@ public:
         const int nloc = g.r1 - g.r0;
         float bv = -INFINITY;
         unsigned bi = NONE_IDX;
+        #pragma unroll 1
         for (int i = tid(); i < nloc; i += NCT) {
             const float y = row_value(g, i);
             const unsigned row = (unsigned)(g.r0 + i);
@@ -786,10 +919,12 @@ public:
     }
 
     __device__ __noinline__ void store_rows(u64* dst, const GemvGeo& g, uint32_t tg) {
+        #pragma unroll 1
         for (int i = tid(); i < g.r1 - g.r0; i += NCT) st_relaxed_u64(dst + g.r0 + i, tagged(row_value(g, i), tg));
     }
 
     __device__ __noinline__ void residual_rows(const GemvGeo& g, uint32_t tg) {  // x[r] += y[r] on this CTA's rows
+        #pragma unroll 1
         for (int i = tid(); i < g.r1 - g.r0; i += NCT) {
             const float v = xloc()[i] + row_value(g, i);
             xloc()[i] = v;
@@ -831,9 +966,10 @@ public:
                 gemv_consume(gD());
                 {
                     const uint32_t tg = tag(seq(step, l, 4));
+                    #pragma unroll 1
                     for (int i = tid(); i < (gD().r1 - gD().r0) / 2; i += NCT) {
                         const float gt = row_value(gD(), 2 * i), up = row_value(gD(), 2 * i + 1);
-                        st_relaxed_u64(p.hbuf + gD().r0 / 2 + i, tagged(gt / (1.0f + expf(-gt)) * up, tg));
+                        st_relaxed_u64(p.hbuf + gD().r0 / 2 + i, tagged(gt / (1.0f + __expf(-gt)) * up, tg));
                     }
                 }
                 // E: down_proj + residual
@@ -882,7 +1018,6 @@ public:
                 const uint32_t bytes = (uint32_t)nr * (uint32_t)g.K * 2u;
                 mbar_arrive_expect_tx(&qw_sm.full[slot], bytes);
                 bulk_g2s_evict_first(ring() + slot * SLOT_BYTES, wbase + g.woff + (size_t)r * g.K, bytes, &qw_sm.full[slot], pol);
-                piece_stamp(it, 0);
                 n_issued = it + 1;
             }
             ++it;

@@ -448,8 +448,7 @@ void* qw_model_stream(const qw_model* m) { return m ? static_cast<void*>(m->stre
 
 size_t qw_trace_stride(const qw_model* m) { return m ? (size_t)TRACE_PER_LAYER * m->cfg.layers + 4 : 0; }
 
-// stamps the trace buffer holds: num_ctas * stride phase stamps, then 4 * TRACE_PIECES ring stamps of CTA 0
-static size_t trace_words(const qw_model* m) { return (size_t)m->nctas * qw_trace_stride(m) + 4 * (size_t)TRACE_PIECES; }
+static size_t trace_words(const qw_model* m) { return (size_t)m->nctas * qw_trace_stride(m); }
 
 int qw_set_trace(qw_model* m, int enable) {
     if (!m) return set_err(QW_ERR_ARG, "null handle");

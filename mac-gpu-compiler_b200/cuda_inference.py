@@ -153,15 +153,12 @@ class CudaModel:
         """Record a per-CTA phase timeline of each launch's first step (see include/cuda_inference.h)."""
         _check(lib().qw_set_trace(self._h, 1 if enable else 0))
 
-    TRACE_PIECES = 1024
-
-    def read_trace(self) -> tuple[np.ndarray, np.ndarray]:
-        """([num_ctas, stride] phase stamps, [TRACE_PIECES, 4] CTA-0 ring stamps), globaltimer ns."""
+    def read_trace(self) -> np.ndarray:
+        """[num_ctas, stride] uint64 globaltimer stamps (ns) of the most recent launch's first step."""
         stride = int(lib().qw_trace_stride(self._h))
-        n = self.num_ctas * stride + 4 * self.TRACE_PIECES
-        out = np.zeros(n, np.uint64)
+        out = np.zeros((self.num_ctas, stride), np.uint64)
         _check(lib().qw_read_trace(self._h, out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint64)), out.size))
-        return out[: self.num_ctas * stride].reshape(self.num_ctas, stride), out[self.num_ctas * stride:].reshape(-1, 4)
+        return out
 
     def forward(self, token: int, pos: int, cache: "CudaKVCache") -> np.ndarray:
         out = np.empty(self.config.vocab_size, np.float32)

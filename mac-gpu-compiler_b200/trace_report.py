@@ -35,7 +35,6 @@ def main() -> None:
     ap.add_argument("--geometry", default="qwen3-0.6b", choices=sorted(randmodel.GEOMETRIES))
     ap.add_argument("--pos", type=int, default=130)
     ap.add_argument("--json", action="store_true")
-    ap.add_argument("--dump-pieces", type=int, default=0)
     a = ap.parse_args()
     model = ci.CudaModel.load_model(randmodel.make_model(a.geometry, 0))
     L = model.config.num_hidden_layers
@@ -45,9 +44,7 @@ def main() -> None:
         model.forward(ids[pos], pos, cache)
     model.set_trace(True)
     model.forward(ids[a.pos], a.pos, cache)
-    tr, pieces = model.read_trace()
-    tr = tr.astype(np.int64)
-    pieces = pieces.astype(np.int64)
+    tr = model.read_trace().astype(np.int64)
     model.set_trace(False)
     t0 = tr[:, 0].min()
     rel = tr - t0
@@ -73,16 +70,6 @@ def main() -> None:
         "barrier_us": float(np.median(rel[:, tail + 2] - rel[:, tail + 1])) / 1e3,
         "intervals": rows,
     }
-    used = pieces[:, 1] > 0
-    pc = pieces[used] - t0
-    out["cta0_pieces"] = int(used.sum())
-    if used.any():
-        out["cta0_piece_wait_us_median"] = float(np.median(pc[:, 2] - pc[:, 1])) / 1e3
-        out["cta0_piece_consume_us_median"] = float(np.median(pc[:, 3] - pc[:, 2])) / 1e3
-        out["cta0_piece_issue_to_ready_us_median"] = float(np.median(pc[:, 2] - pc[:, 0])) / 1e3
-    if a.dump_pieces:
-        for i, r in enumerate(pc[: a.dump_pieces]):
-            print(f"piece {i:4d}: issued {r[0]/1e3:9.2f}  wait {r[1]/1e3:9.2f}  ready {r[2]/1e3:9.2f}  done {r[3]/1e3:9.2f} us")
     if a.json:
         print(json.dumps(out))
         return
@@ -91,9 +78,6 @@ def main() -> None:
           f"lm_head {out['lm_head_us']:.1f} us; end barrier {out['barrier_us']:.2f} us")
     for r in rows:
         print(f"  {r['interval']:32s} median {r['median_us']:7.2f} us   max {r['max_us']:7.2f} us")
-    for k in ("cta0_pieces", "cta0_piece_wait_us_median", "cta0_piece_consume_us_median", "cta0_piece_issue_to_ready_us_median"):
-        if k in out:
-            print(f"  {k}: {out[k]}")
 
 
 if __name__ == "__main__":
