@@ -14,7 +14,7 @@ Printed JSON (one line, rank 0):
                token streamed back to the host callback), timed with CUDA events on the model's
                stream around each call
   roofline     the decode kernel against the measured HBM copy bandwidth (MEASURED_PEAKS.json):
-               achieved = the reference's bytes-per-token rule (tests/mbu.rs:151-167: all weights
+               achieved = the reference's bytes-per-token rule (tests/mbu.rs:19-37: all weights
                but the embedding table + one embedding row + f32 K/V of positions 0..pos) summed
                over the 128 positions of a launch / average launch time (CUDA events)
   cpu_baseline the CPU oracle (C++ restatement of cpu_inference.rs, all host threads) on a bounded
@@ -52,7 +52,7 @@ NCU_DRAM_BYTES_PER_TOKEN = None
 
 
 def kv_bytes_at(cfg, pos: int) -> int:
-    """tests/mbu.rs:162-167 — f32 K and V for every cached position (0..=pos) in every layer."""
+    """tests/mbu.rs:32-37 — f32 K and V for every cached position (0..=pos) in every layer."""
     return 2 * cfg.num_hidden_layers * (pos + 1) * cfg.num_key_value_heads * cfg.head_dim * 4
 
 

@@ -68,7 +68,7 @@ void qw_free(qw_model* model);
 /* MetalModel::config (metal_inference.rs:170) */
 int qw_config_get(const qw_model* model, qw_config* out);
 
-/* bytes one decode token reads by the reference's rule (tests/mbu.rs:151-160, bench.rs:107-116):
+/* bytes one decode token reads by the reference's rule (tests/mbu.rs:19-30, bench.rs:107-116):
  * every tensor except the embedding table, plus one bf16 embedding row */
 uint64_t qw_weight_bytes_per_token(const qw_model* model);
 
@@ -122,7 +122,7 @@ int qw_read_trace(qw_model* model, uint64_t* out, size_t capacity);
 /* ---- standalone kernels (the device code of the decode kernel, exposed for microbenchmarks) ---- */
 
 /* y = W x, W bf16 [rows][cols] row-major, x/y f32 — the matvec_bf16 kernel
- * (shaders/inference.metal:143-186, cpu_inference.rs:225-257) as the decode kernel streams it.
+ * (src/shaders/inference.metal:143-186, cpu_inference.rs:225-257) as the decode kernel streams it.
  * cols must split into 1, 2, 3, 4, 6 or 12 segments of 256, 512, 768 or 1024 columns
  * (e.g. 256, 512, 768, 1024, 2048, 3072, 4096, 6144, 12288). */
 int qw_gemv_bf16(int device, const uint16_t* d_w, const float* d_x, float* d_y, size_t rows, size_t cols,

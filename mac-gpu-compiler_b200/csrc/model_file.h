@@ -36,7 +36,7 @@ public:
     // pointer to a tensor's bytes (after validate(), every tensor the engine reads is present)
     const uint8_t* data(const std::string& name) const;
     const TensorView* find(const std::string& name) const;
-    // tests/mbu.rs:151-160: all tensors except the embedding table, plus one bf16 embedding row
+    // tests/mbu.rs:19-30: all tensors except the embedding table, plus one bf16 embedding row
     uint64_t weight_bytes_per_token() const;
     const std::unordered_map<std::string, TensorView>& tensors() const { return tensors_; }
 

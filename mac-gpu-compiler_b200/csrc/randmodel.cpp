@@ -2,7 +2,7 @@
 //
 // Writes a safetensors file with the Hugging Face Qwen3 tensor names and shapes, the same set
 // the reference engine reads (metal_infrence_engine/src/cpu_inference.rs:109-177), so that the
-// reference loader, its bytes-per-token rule (tests/mbu.rs:151-160) and this repo's engine all
+// reference loader, its bytes-per-token rule (tests/mbu.rs:19-30) and this repo's engine all
 // apply unchanged. Values: linear weights and the embedding ~ N(0, 0.02), RMSNorm gains
 // 1 + N(0, 0.01), all rounded to bf16 (round-to-nearest-even). `lm_head.weight` is a byte copy
 // of `model.embed_tokens.weight` (Qwen3-0.6B ties them) stored under its own name.

@@ -137,7 +137,7 @@ class CudaModel:
         return cls(h, device)
 
     def weight_bytes_per_token(self) -> int:
-        """tests/mbu.rs:151-160"""
+        """tests/mbu.rs:19-30"""
         return int(lib().qw_weight_bytes_per_token(self._h))
 
     @property

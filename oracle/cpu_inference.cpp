@@ -351,7 +351,7 @@ void oracle_config(const OracleModel* m, uint64_t* fields, float* eps, float* th
     *eos = c.eos_token_id;
 }
 
-// tests/mbu.rs:151-160: every tensor except the embedding table, plus one bf16 embedding row
+// tests/mbu.rs:19-30: every tensor except the embedding table, plus one bf16 embedding row
 uint64_t oracle_weight_bytes_per_token(const OracleModel* m) {
     uint64_t bytes = 0;
     for (auto& t : m->tensors) {

@@ -128,7 +128,7 @@ class Model:
         return cls(h)
 
     def weight_bytes_per_token(self) -> int:
-        """tests/mbu.rs:151-160"""
+        """tests/mbu.rs:19-30"""
         return int(lib().oracle_weight_bytes_per_token(self._h))
 
     def forward(self, token: int, pos: int, cache: KVCache) -> np.ndarray:

@@ -42,7 +42,7 @@ def test_oracle_matches_transformers_full_geometry(full_model_path):
 
 
 def test_weight_bytes_rule_matches_reference(full_model_path):
-    # tests/mbu.rs:151-160 on the Qwen3-0.6B geometry gives the reference's published
+    # tests/mbu.rs:19-30 on the Qwen3-0.6B geometry gives the reference's published
     # 1,192,101,888 B/token (mlx_baseline/results/engine_metal_m1_ai.json:140)
     m = co.Model.load_model(full_model_path)
     assert m.weight_bytes_per_token() == 1_192_101_888
