@@ -134,6 +134,19 @@ int qw_gemv_bf16(int device, const uint16_t* d_w, const float* d_x, float* d_y, 
 size_t qw_argmax_workspace_size(size_t n);
 int qw_argmax_f32(int device, const float* d_x, size_t n, uint32_t* d_out, void* d_workspace, void* stream);
 
+/* qw_argmax_f32 for callers that cannot allocate device memory — for example code running inside
+ * a CUDA stream capture, or a host that owns the device allocator and forbids cudaMalloc on its
+ * serving path. This entry point has no counterpart in the reference. Instead of a caller
+ * workspace it uses one file-scope device array of 8,448 bytes that every GPU loading this
+ * library holds until the process exits; it calls no cudaMalloc, cudaFree or other allocating
+ * routine. The first call on a device looks up that array's device address (do it before any
+ * stream capture). n must be in [1, QW_ARGMAX_NOALLOC_MAX_N]; larger n returns QW_ERR_ARG. All
+ * calls on a device share the array, which keeps the last call's contents (the call clears what
+ * must start at zero itself): two calls that overlap on the GPU — on different streams, or from
+ * different threads — race and give wrong results; keep them ordered on one stream. */
+#define QW_ARGMAX_NOALLOC_MAX_N 4294967295ull
+int qw_argmax_f32_noalloc(int device, const float* d_x, size_t n, uint32_t* d_out, void* stream);
+
 /* Streaming-read probe (tests/read_bandwidth.rs:16-54): sums n_floats floats (n_floats % 4 == 0,
  * d_src 16-byte aligned) into per-CTA partials d_partials[0 .. n_partials). Returns the number
  * of partials written through *n_written. */

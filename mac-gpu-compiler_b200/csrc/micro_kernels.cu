@@ -7,7 +7,9 @@
 
 #include <algorithm>
 #include <cmath>
+#include <mutex>
 #include <string>
+#include <vector>
 
 #include "../../include/cuda_inference.h"
 #include "decode_kernel.cuh"
@@ -139,6 +141,33 @@ __global__ void __launch_bounds__(RP_THREADS) read_probe_kernel(const float4* __
     }
 }
 
+// Scratch of qw_argmax_f32_noalloc: the same layout as the caller workspace of qw_argmax_f32
+// (a 4-byte ticket in the first 256 bytes, then up to 1024 block maxima and 1024 block indices).
+// It is one file-scope device array: every GPU that loads this library holds these 8,448 bytes
+// until the process exits, and all calls on a device share them.
+constexpr size_t NOALLOC_ARGMAX_SCRATCH = 256 + 2 * 4 * 1024;
+static __device__ __align__(256) uint8_t g_argmax_scratch[NOALLOC_ARGMAX_SCRATCH];
+
+// Device address of g_argmax_scratch on `device`, looked up once per device with that device
+// current (in host code the array's name is only a host-side stand-in, not a device address).
+void* argmax_scratch_address(int device, std::string& err) {
+    static std::mutex mu;
+    static std::vector<void*> addr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (device < 0) { err = "bad device index"; return nullptr; }
+    if ((int)addr.size() <= device) addr.resize(device + 1, nullptr);
+    if (!addr[device]) {
+        void* ptr = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&ptr, g_argmax_scratch);
+        if (e != cudaSuccess || !ptr) {
+            err = std::string("cudaGetSymbolAddress(g_argmax_scratch) failed: ") + cudaGetErrorString(e);
+            return nullptr;
+        }
+        addr[device] = ptr;
+    }
+    return addr[device];
+}
+
 int sm_count(int device) {
     int n = 0;
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
@@ -198,6 +227,26 @@ int qw_argmax_f32(int device, const float* d_x, size_t n, uint32_t* d_out, void*
     unsigned* idxs = reinterpret_cast<unsigned*>(ws + 256 + 4 * 1024);
     if (cudaMemsetAsync(ticket, 0, 4, s) != cudaSuccess) return set_error(QW_ERR_CUDA, "workspace reset failed");
     argmax_kernel<<<blocks, AM_THREADS, 0, s>>>(d_x, n, d_out, vals, idxs, ticket);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_error(QW_ERR_CUDA, cudaGetErrorString(e));
+    return QW_OK;
+}
+
+int qw_argmax_f32_noalloc(int device, const float* d_x, size_t n, uint32_t* d_out, void* stream) {
+    if (!d_x || !d_out) return set_error(QW_ERR_ARG, "qw_argmax_f32_noalloc: null pointer");
+    if (n == 0 || n > QW_ARGMAX_NOALLOC_MAX_N)
+        return set_error(QW_ERR_ARG, "qw_argmax_f32_noalloc: n must be in [1, QW_ARGMAX_NOALLOC_MAX_N]");
+    if (cudaSetDevice(device) != cudaSuccess) return set_error(QW_ERR_CUDA, "cudaSetDevice failed");
+    std::string err;
+    uint8_t* ws = static_cast<uint8_t*>(argmax_scratch_address(device, err));
+    if (!ws) return set_error(QW_ERR_CUDA, err.c_str());
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int blocks = (int)std::min<size_t>(std::min<size_t>(1024, (size_t)sm_count(device) * 4), (n + AM_THREADS - 1) / AM_THREADS);
+    unsigned* ticket = reinterpret_cast<unsigned*>(ws);
+    // the ticket must start at zero; the partials are always written before they are read
+    if (cudaMemsetAsync(ticket, 0, 4, s) != cudaSuccess) return set_error(QW_ERR_CUDA, "scratch reset failed");
+    argmax_kernel<<<blocks, AM_THREADS, 0, s>>>(d_x, n, d_out, reinterpret_cast<float*>(ws + 256),
+                                                reinterpret_cast<unsigned*>(ws + 256 + 4 * 1024), ticket);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(QW_ERR_CUDA, cudaGetErrorString(e));
     return QW_OK;

@@ -98,6 +98,7 @@ def lib() -> ctypes.CDLL:
             "qw_gemv_bf16": (i32, [i32, vp, vp, vp, sz, sz, vp]),
             "qw_argmax_workspace_size": (sz, [sz]),
             "qw_argmax_f32": (i32, [i32, vp, sz, vp, vp, vp]),
+            "qw_argmax_f32_noalloc": (i32, [i32, vp, sz, vp, vp]),
             "qw_read_probe": (i32, [i32, vp, sz, vp, sz, ctypes.POINTER(sz), vp]),
         }
         for name, (res, args) in sig.items():
@@ -236,6 +237,11 @@ def argmax_workspace_size(n: int) -> int:
 
 def argmax_f32(device: int, d_x: int, n: int, d_out: int, d_workspace: int, stream: int = 0) -> None:
     _check(lib().qw_argmax_f32(device, d_x, n, d_out, d_workspace, stream or None))
+
+
+def argmax_f32_noalloc(device: int, d_x: int, n: int, d_out: int, stream: int = 0) -> None:
+    """argmax_f32 without a caller workspace (see qw_argmax_f32_noalloc in the header)."""
+    _check(lib().qw_argmax_f32_noalloc(device, d_x, n, d_out, stream or None))
 
 
 def read_probe(device: int, d_src: int, n_floats: int, d_partials: int, n_partials: int, stream: int = 0) -> int:
