@@ -47,8 +47,12 @@ CONFIGS = {
 # reference's published decode tok/s for this metric and config: Metal engine, f32 KV cache, Apple M1
 # (metal_infrence_engine/README.md:22)
 PUBLISHED_TPS = 46.37
-# DRAM bytes per decode token of the decode kernel, from an ncu capture (see profiles/); None until measured
-NCU_DRAM_BYTES_PER_TOKEN = None
+# DRAM traffic of the decode kernel relative to its algorithmic bytes, from one ncu capture of
+# mac-gpu-compiler_b200/profile_case.py's decode launch: a 4-token launch at positions 8..11 read
+# 4,777,480,000 B and wrote 8,422,144 B against 4,778,041,344 algorithmic bytes. The bench launch
+# (128 tokens, ~158 GB) is too large to capture, and its traffic grows with the same weight + K/V
+# bytes per token, so roofline.traffic is that ratio times the launch's algorithmic bytes.
+NCU_TRAFFIC_RATIO = (4_777_480_000 + 8_422_144) / 4_778_041_344
 
 
 def kv_bytes_at(cfg, pos: int) -> int:
@@ -288,7 +292,7 @@ def main() -> None:
         achieved = bytes_launch / avg_launch / 1e9
         peak, peak_kind = load_peaks()
         value = n_dec * args.steps * world / elapsed_max
-        traffic = None if NCU_DRAM_BYTES_PER_TOKEN is None else NCU_DRAM_BYTES_PER_TOKEN * n_dec
+        traffic = NCU_TRAFFIC_RATIO * bytes_launch
         line = {
             "metric": "Qwen3-0.6B bf16 decode tok/s @bs1 & % of HBM roofline; box tok/s at 1-8 GPUs",
             "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -306,6 +310,7 @@ def main() -> None:
                     "d2h_bytes_per_step": 4 * n_dec, "api": "qw_decode (host callback per token)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": f"{peak_kind} (hbm_gbs, copy)", "traffic": traffic,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of a 4-token launch, scaled by algorithmic bytes",
                          "algorithmic_bytes_per_launch": bytes_launch,
                          "kernel": "qw::decode_kernel", "avg_launch_ms": avg_launch * 1e3},
             "gpu_launches": args.steps,
