@@ -58,6 +58,7 @@ constexpr int MAX_S = 18;                     // attention chunks per KV head
 constexpr int MIN_CHUNK = 32;                 // fewest positions per attention chunk
 constexpr uint32_t LM_PREFETCH_BYTES = 256u * 1024;  // lm_head bytes per CTA warmed into L2 ahead of use
 constexpr int APART_STRIDE = HD + 4;          // words per attention partial: acc[128], m, l, pad
+constexpr int ATT_WST = HD + 4;               // floats per (warp, head) softmax state staged in part: acc[128], m, l, pad
 constexpr int GP = 4;                         // tagged word pairs a consumer thread polls at once
 constexpr uint32_t NONE_IDX = 0xFFFFFFFFu;
 // Math: the softmax / SiLU exponentials use __expf and the RMSNorm scales rsqrtf (hardware
@@ -92,8 +93,8 @@ struct DecodeParams {
     // tagged activation words {f32 value | tag << 32}
     u64* x;                      // [H] residual stream
     u64* qkv;                    // [QD + 2*KVD] raw projections
-    u64* att;                    // [QD] attention output
     u64* hbuf;                   // [I] SiLU(gate)*up
+    u64* att;                    // [QD] attention output
     u64* apart;                  // [KVH][S][G][APART_STRIDE] attention partials
     // argmax partials and the per-token barrier
     float* am_val;               // [grid]
@@ -182,19 +183,28 @@ __device__ inline AttnItem attn_item(const DecodeParams& p, int cta, int pos) {
     return a;
 }
 
+struct LoopState {
+    int step;        // token of the launch being decoded
+    int l;           // layer
+    unsigned token;  // input token of the current step (consumers)
+};
+
 struct Smem {
     // qs / ks / vs are accessed as float4: keep them 16-byte aligned
     __align__(16) float qs[MAX_G][HD];
     __align__(16) float ks[HD];
     __align__(16) float vs[HD];
     GemvGeo geo[5];              // this CTA's rows of phases A (q|k|v), C (o), D (gate|up), E (down), F (lm_head)
-    float sc[2][MAX_G][ATT_P];
     float ml[MAX_S][MAX_G][2];   // attention partials' (m, l) gathered by the merging CTA
     float red[64];
     float redv[NCW];
     unsigned redi[NCW];
     uint64_t full[NSLOT];
     uint64_t empty[NSLOT];
+    DecodeParams prm;              // the launch's parameters (read by every phase routine)
+    uint32_t ring_it[NCW + 1];     // per warp: ring pieces consumed (consumers) or walked (producer)
+    uint32_t n_issued;             // producer: pieces whose copies were issued
+    LoopState loop[NCW + 1];       // per warp: token/layer loop state (see Decoder::ls)
     uint32_t progress;   // tokens whose end-of-token barrier this CTA's consumers have passed
     int abort;           // set once any wait expired
     unsigned token;
@@ -237,17 +247,14 @@ __device__ __forceinline__ u64 tagged(float v, uint32_t tag) { return ((u64)tag 
 __shared__ Smem qw_sm;
 extern __shared__ __align__(128) uint8_t qw_dyn[];
 
-// Per-thread state is kept to the two ring counters: everything else is re-derived from special
-// registers, the (constant-bank) kernel parameters and fixed shared-memory addresses, which keeps
-// the whole kernel within the 128 registers a 13-warp CTA can have per thread.
+// The decoder has no per-thread object state: the launch parameters (copied into shared memory at
+// launch), the ring counters and the phase geometry live at fixed shared-memory addresses, and
+// everything else is re-derived from special registers. With no object whose address the
+// out-of-line phase routines need, nothing sits in local memory, which on this kernel is backed
+// by an L1 of only ~24 KB (shared memory takes the rest) and would miss to L2 on the critical
+// path. It also keeps the kernel within the 128 registers a 13-warp CTA can have per thread.
 class Decoder {
 public:
-    const DecodeParams& p;
-    uint32_t it = 0;       // ring pieces consumed (consumer) or walked (producer)
-    uint32_t n_issued = 0; // producer: pieces whose copies were issued (all before any abort)
-
-    __device__ explicit Decoder(const DecodeParams& p_) : p(p_) {}
-
     __device__ __forceinline__ static int tid() { return (int)threadIdx.x; }
     __device__ __forceinline__ static int warp() { return (int)(threadIdx.x >> 5); }
     __device__ __forceinline__ static int lane() { return (int)(threadIdx.x & 31); }
@@ -255,12 +262,14 @@ public:
     __device__ __forceinline__ static int nctas() { return (int)gridDim.x; }
     __device__ __forceinline__ static uint8_t* ring() { return qw_dyn; }
     __device__ __forceinline__ static float* xs() { return reinterpret_cast<float*>(qw_dyn + NSLOT * SLOT_BYTES); }
-    __device__ __forceinline__ float* part() const { return xs() + p.xs_cap; }
-    __device__ __forceinline__ float* xloc() const { return part() + p.part_cap; }
-    __device__ __forceinline__ int QD() const { return p.NQ * HD; }
-    __device__ __forceinline__ int KVD() const { return p.NKV * HD; }
-    __device__ __forceinline__ int G() const { return p.NQ / p.NKV; }
-    __device__ __forceinline__ int QKVR() const { return QD() + 2 * KVD(); }
+    // ring pieces this warp has consumed (consumer warps) or walked (the producer)
+    __device__ __forceinline__ static uint32_t& ring_pos() { return qw_sm.ring_it[threadIdx.x >> 5]; }
+    __device__ __forceinline__ static float* part() { return xs() + qw_sm.prm.xs_cap; }
+    __device__ __forceinline__ static float* xloc() { return part() + qw_sm.prm.part_cap; }
+    __device__ __forceinline__ static int QD() { return qw_sm.prm.NQ * HD; }
+    __device__ __forceinline__ static int KVD() { return qw_sm.prm.NKV * HD; }
+    __device__ __forceinline__ static int G() { return qw_sm.prm.NQ / qw_sm.prm.NKV; }
+    __device__ __forceinline__ static int QKVR() { return QD() + 2 * KVD(); }
     // this CTA's static row partition of phases A (q|k|v), C (o), D (gate|up), E (down), F (lm_head)
     __device__ __forceinline__ static const GemvGeo& gA() { return qw_sm.geo[0]; }
     __device__ __forceinline__ static const GemvGeo& gC() { return qw_sm.geo[1]; }
@@ -283,21 +292,27 @@ public:
     }
 
     // phase sequence numbers within the launch -> tags (12 bits of epoch, 20 bits of sequence)
-    __device__ uint32_t seq(int step, int l, int ph) const {  // ph: 1 A, 2 B, 3 C, 4 D, 5 E
+    __device__ static uint32_t seq(int step, int l, int ph) {  // ph: 1 A, 2 B, 3 C, 4 D, 5 E
+        const volatile DecodeParams& p = qw_sm.prm;
         return (uint32_t)step * (uint32_t)(5 * p.L + 1) + (uint32_t)(5 * l + ph);
     }
-    __device__ uint32_t tag(uint32_t sq) const { return ((p.epoch & 0xFFFu) << 20) | (sq & 0xFFFFFu); }
+    __device__ static uint32_t tag(uint32_t sq) {
+        const volatile DecodeParams& p = qw_sm.prm;
+        return ((p.epoch & 0xFFFu) << 20) | (sq & 0xFFFFFu);
+    }
 
-    __device__ __forceinline__ void stamp(int step, int idx) const {
+    __device__ __forceinline__ static void stamp(int step, int idx) {
+        const volatile DecodeParams& p = qw_sm.prm;
         if (p.trace != nullptr && step == 0 && tid() == 0)
             p.trace[(size_t)cta() * (TRACE_PER_LAYER * p.L + 4) + idx] = globaltimer_ns();
     }
 
 
     // ------------------------------------------------------------------ errors and waits
-    __device__ bool aborted() const { return *reinterpret_cast<volatile const int*>(&qw_sm.abort) != 0; }
+    __device__ static bool aborted() { return *reinterpret_cast<volatile const int*>(&qw_sm.abort) != 0; }
 
-    __device__ __noinline__ void fail(int code, int where) {
+    __device__ __noinline__ static void fail(int code, int where) {
+        const DecodeParams& p = qw_sm.prm;
         *reinterpret_cast<volatile int*>(&qw_sm.abort) = 1;
         if (atomicCAS(&p.err[0], 0, code) == 0) {
             p.err[1] = cta();
@@ -311,14 +326,15 @@ public:
     // CTA's abort flag and (after 50 us) the global error word. Arguments pass by value: an
     // out-of-line call per polling round, or references to the loop counters, would move the
     // polling state through the stack on every round.
-    __device__ __forceinline__ bool wait_expired(uint32_t& spins, uint64_t& t0, int code, int where) {
+    __device__ __forceinline__ static bool wait_expired(uint32_t& spins, uint64_t& t0, int code, int where) {
         if ((++spins & 31) != 0) return false;
         t0 = wait_check(spins, t0, code, where);
         return t0 == ~0ull;
     }
 
     // returns the (possibly started) wait start time, or ~0 when the wait must end
-    __device__ __noinline__ uint64_t wait_check(uint32_t spins, uint64_t t0, int code, int where) {
+    __device__ __noinline__ static uint64_t wait_check(uint32_t spins, uint64_t t0, int code, int where) {
+        const DecodeParams& p = qw_sm.prm;
         if (aborted()) return ~0ull;
         const uint64_t now = globaltimer_ns();
         if (spins == 32) return now;
@@ -334,12 +350,13 @@ public:
         return t0;
     }
 
-    __device__ __forceinline__ bool wait_mbar(uint64_t* bar, uint32_t parity, int code) {
+    __device__ __forceinline__ static bool wait_mbar(uint64_t* bar, uint32_t parity, int code) {
         if (mbar_try_wait(bar, parity)) return true;  // fast path: the phase already completed
         return wait_mbar_slow(bar, parity, code);
     }
 
-    __device__ __noinline__ bool wait_mbar_slow(uint64_t* bar, uint32_t parity, int code) {
+    __device__ __noinline__ static bool wait_mbar_slow(uint64_t* bar, uint32_t parity, int code) {
+        uint32_t& it = ring_pos();
         if (aborted()) return false;
         uint32_t spins = 0;
         uint64_t t0 = 0;
@@ -348,8 +365,21 @@ public:
         return true;
     }
 
+    // Waits for ring pieces pc .. pc+n-1 (n <= 32) with lane j waiting on piece pc + j, so the
+    // mbarrier probes of a group run side by side instead of one after another. Returns (to every
+    // lane) whether all of them landed; the __syncwarp orders the lanes' later reads of every
+    // piece after the probe that saw it land.
+    __device__ __forceinline__ static bool wait_pieces(uint32_t pc, int n) {
+        bool mine = true;
+        if (lane() < n) mine = wait_mbar(&qw_sm.full[(pc + lane()) % NSLOT], ((pc + lane()) / NSLOT) & 1, DERR_TIMEOUT_FULL);
+        const bool ok = __all_sync(0xFFFFFFFFu, mine);
+        __syncwarp();
+        return ok;
+    }
+
     // xs[0..K) <- values of the tagged words src[0..K) once each carries `tg` (K even, src 16-byte aligned)
-    __device__ __noinline__ void gather(const u64* src, int K, uint32_t tg) {
+    __device__ __noinline__ static void gather(const u64* src, int K, uint32_t tg) {
+        const DecodeParams& p = qw_sm.prm;
         const int npairs = K >> 1;
         for (int base = 0; base < npairs; base += NCT * GP) {
             unsigned pending = 0;
@@ -382,7 +412,8 @@ public:
     }
 
     // one end-of-token grid barrier: every CTA has published `done` finished tokens
-    __device__ __noinline__ void token_barrier(uint32_t done) {
+    __device__ __noinline__ static void token_barrier(uint32_t done) {
+        const DecodeParams& p = qw_sm.prm;
         named_bar_sync(1, NCT);
         const u64 target = ((u64)p.epoch << 32) | done;
         if (tid() == 0) {
@@ -415,7 +446,7 @@ public:
     }
 
     // ------------------------------------------------------------------ consumer helpers
-    __device__ float block_sum(float v) {
+    __device__ static float block_sum(float v) {
         v = warp_sum(v);
         if (lane() == 0) qw_sm.red[warp()] = v;
         named_bar_sync(1, NCT);
@@ -431,7 +462,8 @@ public:
     // xs <- rmsnorm(src) * w  (cpu_inference.rs:189-194). src is the tagged residual stream, or
     // (from_embed) the embedding row of `token`, in which case the CTA also initialises its own
     // residual rows xloc from that row.
-    __device__ __noinline__ void norm_prologue(const uint16_t* w, bool from_embed, unsigned token, uint32_t tg) {
+    __device__ __noinline__ static void norm_prologue(const uint16_t* w, bool from_embed, unsigned token, uint32_t tg) {
+        const DecodeParams& p = qw_sm.prm;
         const int H = p.H;
         // the gains do not depend on the token: fetch them before waiting for the input
         constexpr int MAXK = 8;  // H <= 8 * 384 keeps them in registers
@@ -484,7 +516,8 @@ public:
     // butterfly (6 shuffles for 4 rows). A layer phase (2-4 pieces, resident in shared memory by
     // the time its input arrives) is then one group: its cost is the shared-memory traffic, not a
     // per-piece chain of load, FMA and shuffle latencies.
-    __device__ __noinline__ void gemv_generic(const GemvGeo& gs) {
+    __device__ __noinline__ static void gemv_generic(const GemvGeo& gs) {
+        uint32_t& it = ring_pos();
         const GemvGeo g = gs;  // loop-invariant: keep the phase geometry in registers
         const int w = warp(), ln = lane();
         const int myseg = w % g.segs;
@@ -575,11 +608,13 @@ public:
             }
         }
         it = pc;
+        named_bar_sync(1, NCT);
     }
 
     // The Qwen3-0.6B case of gemv_generic, with everything static: 1024-column segments (4 chunks of
     // 16 bytes per lane) and at most one unit per warp per piece.
-    __device__ __noinline__ void gemv_full_segments(const GemvGeo& gs) {
+    __device__ __noinline__ static void gemv_full_segments(const GemvGeo& gs) {
+        uint32_t& it = ring_pos();
         const GemvGeo g = gs;
         const int w = warp(), ln = lane();
         const int myseg = w % g.segs, rl = w / g.segs;
@@ -597,11 +632,12 @@ public:
         const int npieces = (g.r1 - g.r0 + g.rpp - 1) / g.rpp;
         const size_t woff = ((size_t)rl * g.K + (size_t)myseg * 1024) * 2 + (size_t)ln * 16;
         uint32_t pc = it;
+        // a phase whose pieces all fit in the ring releases them once, after the phase's closing
+        // barrier below; a longer one (lm_head) releases each group as soon as it is read
+        const bool release_here = npieces > NSLOT;
         for (int q0 = 0; q0 < npieces; q0 += 4) {
             const int n = min(4, npieces - q0);
-            bool ok = true;
-            for (int j = 0; j < n; j++)
-                ok = wait_mbar(&qw_sm.full[(pc + j) % NSLOT], ((pc + j) / NSLOT) & 1, DERR_TIMEOUT_FULL) && ok;
+            const bool ok = wait_pieces(pc, n);
             float v[4] = {0.f, 0.f, 0.f, 0.f};
             int dst[4] = {-1, -1, -1, -1};
             if (ok) {
@@ -619,9 +655,11 @@ public:
                     }
                 }
             }
-            __syncwarp();
-            if (ln == 0 && ok)  // a slot is released only after its data landed
-                for (int j = 0; j < n; j++) mbar_arrive(&qw_sm.empty[(pc + j) % NSLOT]);
+            if (release_here) {
+                __syncwarp();
+                if (ln == 0 && ok)  // a slot is released only after its data landed
+                    for (int j = 0; j < n; j++) mbar_arrive(&qw_sm.empty[(pc + j) % NSLOT]);
+            }
             pc += n;
             const bool hi16 = ln & 16, hi8 = ln & 8;
             float k0 = hi16 ? v[2] : v[0], k1 = hi16 ? v[3] : v[1];
@@ -640,15 +678,19 @@ public:
             if ((ln & 7) == 0 && d >= 0) prt[d] = t;
         }
         it = pc;
+        named_bar_sync(1, NCT);
+        // every warp has read the phase's pieces: one lane per slot releases it for all 12 warps
+        if (!release_here && warp() == 0 && lane() < npieces && !aborted())
+            mbar_arrive_cnt(&qw_sm.empty[(pc - npieces + lane()) % NSLOT], NCW);
     }
 
-    __device__ __forceinline__ void gemv_consume(const GemvGeo& g) {
+    // one GEMV phase of the CTA; returns after a CTA-wide barrier (part() then holds every row's sums)
+    __device__ __forceinline__ static void gemv_consume(const GemvGeo& g) {
         if (g.cpl == 4 && g.rpp * g.segs <= NCW) gemv_full_segments(g);
         else gemv_generic(g);
-        named_bar_sync(1, NCT);
     }
 
-    __device__ __forceinline__ float row_value(const GemvGeo& g, int rl) const {
+    __device__ __forceinline__ static float row_value(const GemvGeo& g, int rl) {
         float y = 0.f;
         for (int sgi = 0; sgi < g.segs; sgi++) y += part()[rl * g.segs + sgi];
         return y;
@@ -657,7 +699,8 @@ public:
     // ------------------------------------------------------------------ attention (phase B)
     // one warp: gather a tagged 128-vector, per-head RMSNorm (q_norm/k_norm), rotate-half RoPE
     // (cpu_inference.rs:134-138, :196-215; the table is the one MetalKVCache builds, :141-154)
-    __device__ __forceinline__ float4 gather_head(const u64* src, uint32_t tg) {
+    __device__ __forceinline__ static float4 gather_head(const u64* src, uint32_t tg) {
+        const DecodeParams& p = qw_sm.prm;
         uint32_t spins = 0;
         uint64_t t0 = 0;
         ulonglong2 a = make_ulonglong2(0, 0), b = make_ulonglong2(0, 0);
@@ -675,7 +718,8 @@ public:
         return make_float4(word_val(a.x), word_val(a.y), word_val(b.x), word_val(b.y));
     }
 
-    __device__ __forceinline__ void head_norm_rope(float4 v, const uint16_t* nw, const float2* rrow, float* dst) {
+    __device__ __forceinline__ static void head_norm_rope(float4 v, const uint16_t* nw, const float2* rrow, float* dst) {
+        const DecodeParams& p = qw_sm.prm;
         float ss = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
         ss = warp_sum(ss);
         const float s = rsqrtf(ss / (float)HD + p.eps);
@@ -694,45 +738,63 @@ public:
         reinterpret_cast<float4*>(dst)[lane()] = make_float4(o[0], o[1], o[2], o[3]);
     }
 
-    // Online-softmax update over np (<= 32) positions whose K/V rows (128 f32 each) are in shared
-    // memory. Warp w scores positions w, w + 12, ... for the G query heads; then each warp of head h
-    // (thread (h, d) = tid h * 128 + d) turns the np scores into weights P = exp(s - m_new) once per
-    // lane (lane = position), rescales its running (m, l, acc) and adds sum_pp P[pp] * V[pp][d] with
-    // P broadcast by shuffles. Every warp of a head computes the same m and l.
-    __device__ __forceinline__ void attn_block(const float* Kb, const float* Vb, int np, int buf, const float4* q4,
-                                               float& m, float& l, float& acc) {
-        for (int pp = warp(); pp < np; pp += NCW) {
-            const float4 k4 = reinterpret_cast<const float4*>(Kb + pp * HD)[lane()];
+    // Running softmax state of one warp for up to MAX_G query heads: every lane holds the same
+    // (m, l) per head and its own 4 of the 128 accumulator dimensions.
+    struct WarpSoftmax {
+        float m[MAX_G], l[MAX_G];
+        float4 acc[MAX_G];
+    };
+
+    // Up to two cached positions (K and V rows of 128 f32 in shared memory; the second may be
+    // absent) into a warp's running softmax (cpu_inference.rs:144-161: scores q.k / sqrt(128),
+    // softmax, sum of p * v). The warp scores both positions against its Gh query heads with
+    // butterfly sums, so every lane holds every score; the 2 x Gh sums are independent, so their
+    // shuffle chains overlap. Then each head's state is rescaled once for the pair.
+    __device__ __forceinline__ static void attn_pair(const float* K0, const float* V0, const float* K1, const float* V1,
+                                                     bool has1, const float4* q4, WarpSoftmax& ws, int Gh, float scale) {
+        const float4 k0 = reinterpret_cast<const float4*>(K0)[lane()];
+        const float4 v0 = reinterpret_cast<const float4*>(V0)[lane()];
+        float4 k1 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = k1;
+        if (has1) {
+            k1 = reinterpret_cast<const float4*>(K1)[lane()];
+            v1 = reinterpret_cast<const float4*>(V1)[lane()];
+        }
+        float s0[MAX_G], s1[MAX_G];
+#pragma unroll
+        for (int h = 0; h < MAX_G; h++) {
+            s0[h] = q4[h].x * k0.x + q4[h].y * k0.y + q4[h].z * k0.z + q4[h].w * k0.w;
+            s1[h] = q4[h].x * k1.x + q4[h].y * k1.y + q4[h].z * k1.z + q4[h].w * k1.w;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
 #pragma unroll
             for (int h = 0; h < MAX_G; h++) {
-                if (h < G()) {
-                    float d = q4[h].x * k4.x + q4[h].y * k4.y + q4[h].z * k4.z + q4[h].w * k4.w;
-                    d = warp_sum(d);
-                    if (lane() == 0) qw_sm.sc[buf][h][pp] = d * p.scale;
+                if (h < Gh) {
+                    s0[h] += __shfl_xor_sync(0xFFFFFFFFu, s0[h], o);
+                    s1[h] += __shfl_xor_sync(0xFFFFFFFFu, s1[h], o);
                 }
             }
         }
-        named_bar_sync(1, NCT);
-        if (tid() < G() * HD) {
-            const int h = tid() >> 7, d = tid() & (HD - 1);
-            const float sv = lane() < np ? qw_sm.sc[buf][h][lane()] : -INFINITY;
-            float mp = sv;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) mp = fmaxf(mp, __shfl_xor_sync(0xFFFFFFFFu, mp, o));
-            const float mn = fmaxf(m, mp);
-            const float corr = (m == -INFINITY) ? 0.f : __expf(m - mn);
-            const float pw = lane() < np ? __expf(sv - mn) : 0.f;
-            const float psum = warp_sum(pw);
-            l = l * corr + psum;
-            float a = acc * corr;
-#pragma unroll 4
-            for (int pp = 0; pp < np; pp++) a = fmaf(__shfl_sync(0xFFFFFFFFu, pw, pp), Vb[pp * HD + d], a);
-            acc = a;
-            m = mn;
+        for (int h = 0; h < MAX_G; h++) {
+            if (h < Gh) {
+                const float a0 = s0[h] * scale, a1 = has1 ? s1[h] * scale : -INFINITY;
+                const float mn = fmaxf(ws.m[h], fmaxf(a0, a1));
+                const float corr = __expf(ws.m[h] - mn);  // 0 while m is still -inf
+                const float p0 = __expf(a0 - mn), p1 = __expf(a1 - mn);  // p1 = 0 without a second position
+                ws.l[h] = fmaf(ws.l[h], corr, p0 + p1);
+                ws.acc[h].x = fmaf(ws.acc[h].x, corr, fmaf(p0, v0.x, p1 * v1.x));
+                ws.acc[h].y = fmaf(ws.acc[h].y, corr, fmaf(p0, v0.y, p1 * v1.y));
+                ws.acc[h].z = fmaf(ws.acc[h].z, corr, fmaf(p0, v0.z, p1 * v1.z));
+                ws.acc[h].w = fmaf(ws.acc[h].w, corr, fmaf(p0, v0.w, p1 * v1.w));
+                ws.m[h] = mn;
+            }
         }
     }
 
-    __device__ __noinline__ void attention_consume(int step, int l, int pos) {
+    __device__ __noinline__ static void attention_consume(int step, int l, int pos) {
+        const DecodeParams& p = qw_sm.prm;
+        uint32_t& it = ring_pos();
         const AttnItem a = attn_item(p, cta(), pos);
         if (!a.active) return;   // uniform over the CTA
         const uint16_t* nrm = p.layer_n + (size_t)l * p.norm_stride;
@@ -758,26 +820,69 @@ public:
 #pragma unroll
         for (int h = 0; h < MAX_G; h++)
             q4[h] = h < G() ? reinterpret_cast<const float4*>(qw_sm.qs[h])[lane()] : make_float4(0, 0, 0, 0);
-        float m = -INFINITY, lsum = 0.f, acc = 0.f;
-        int buf = 0;
+        // Each warp takes the chunk's positions j = warp, warp + 12, ... (j counted from t0), two per
+        // call, and keeps its own running softmax: no CTA-wide barrier per ring piece. A piece holds
+        // ATT_P = 24 = 2 x 12 positions, so position pp of a piece is chunk position j with
+        // j % 12 == pp % 12.
+        WarpSoftmax ws;
+        const int Gh = G();
+        const float scale = p.scale;
+#pragma unroll
+        for (int h = 0; h < MAX_G; h++) {
+            ws.m[h] = -INFINITY;
+            ws.l[h] = 0.f;
+            ws.acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
         const int tc1 = a.has_cur ? pos : a.t1;  // cached positions [t0, tc1)
-        for (int t = a.t0; t < tc1; t += ATT_P) {
-            const int np = min(ATT_P, tc1 - t);
-            const int slot = it % NSLOT;
-            const uint32_t par = (it / NSLOT) & 1;
-            const bool ok = wait_mbar(&qw_sm.full[slot], par, DERR_TIMEOUT_FULL);
-            const float* Kb = reinterpret_cast<const float*>(ring() + slot * SLOT_BYTES);
-            const float* Vb = Kb + ATT_P * HD;
-            attn_block(Kb, Vb, np, buf, q4, m, lsum, acc);
+        const int npieces = tc1 > a.t0 ? (tc1 - a.t0 + ATT_P - 1) / ATT_P : 0;
+        for (int q0 = 0; q0 < npieces; q0 += 4) {  // up to four pieces waited for side by side
+            const int n = min(4, npieces - q0);
+            const uint32_t pc = it;
+            const bool ok = wait_pieces(pc, n);
+            for (int j = 0; j < n; j++) {
+                const int np = min(ATT_P, tc1 - (a.t0 + (q0 + j) * ATT_P));
+                const float* Kb = reinterpret_cast<const float*>(ring() + ((pc + j) % NSLOT) * SLOT_BYTES);
+                const float* Vb = Kb + ATT_P * HD;
+                if (ok)
+                    for (int pp = warp(); pp < np; pp += 2 * NCW)
+                        attn_pair(Kb + pp * HD, Vb + pp * HD, Kb + (pp + NCW) * HD, Vb + (pp + NCW) * HD, pp + NCW < np, q4,
+                                  ws, Gh, scale);
+            }
             __syncwarp();
-            if (lane() == 0 && ok) mbar_arrive(&qw_sm.empty[slot]);
-            ++it;
-            buf ^= 1;
+            if (lane() == 0 && ok)
+                for (int j = 0; j < n; j++) mbar_arrive(&qw_sm.empty[(pc + j) % NSLOT]);
+            it = pc + n;
         }
-        if (a.has_cur) {
-            attn_block(qw_sm.ks, qw_sm.vs, 1, buf, q4, m, lsum, acc);
-            buf ^= 1;
+        if (a.has_cur && warp() == (tc1 - a.t0) % NCW) attn_pair(qw_sm.ks, qw_sm.vs, nullptr, nullptr, false, q4, ws, Gh, scale);
+        // combine the 12 warps' states in warp order (deterministic): stage [warp][h < G][acc 128 | m | l | pad]
+        float* const wst = part();
+        constexpr int WST = ATT_WST;
+#pragma unroll
+        for (int h = 0; h < MAX_G; h++) {
+            if (h < G()) {
+                float* d = wst + (warp() * G() + h) * WST;
+                reinterpret_cast<float4*>(d)[lane()] = ws.acc[h];
+                if (lane() == 0) {
+                    d[HD] = ws.m[h];
+                    d[HD + 1] = ws.l[h];
+                }
+            }
         }
+        named_bar_sync(1, NCT);
+        float m = -INFINITY, lsum = 0.f, acc = 0.f;
+        if (tid() < G() * HD) {
+            const int h = tid() >> 7, d = tid() & (HD - 1);
+#pragma unroll
+            for (int w = 0; w < NCW; w++) m = fmaxf(m, wst[(w * G() + h) * WST + HD]);
+#pragma unroll
+            for (int w = 0; w < NCW; w++) {
+                const float* src = wst + (w * G() + h) * WST;
+                const float e = src[HD] == -INFINITY ? 0.f : __expf(src[HD] - m);  // a warp without positions adds nothing
+                lsum = fmaf(e, src[HD + 1], lsum);
+                acc = fmaf(e, src[d], acc);
+            }
+        }
+        named_bar_sync(1, NCT);  // the warp states in part are dead: the merge below may reuse part
         stamp(step, l * TRACE_PER_LAYER + 4);
         const size_t head_base = (size_t)a.g * p.S * G();  // partial (s, h) at apart[((head_base + s*G + h) * APART_STRIDE]
         if (a.s != 0) {
@@ -863,7 +968,8 @@ public:
     }
 
     // ------------------------------------------------------------------ lm_head + argmax
-    __device__ __noinline__ void lm_epilogue() {
+    __device__ __noinline__ static void lm_epilogue() {
+        const DecodeParams& p = qw_sm.prm;
         const GemvGeo& g = gF();
         const int nloc = g.r1 - g.r0;
         float bv = -INFINITY;
@@ -893,7 +999,8 @@ public:
     }
 
     // after the end-of-token barrier: every CTA reduces the partials to the same next token
-    __device__ __noinline__ unsigned argmax_combine() {
+    __device__ __noinline__ static unsigned argmax_combine() {
+        const DecodeParams& p = qw_sm.prm;
         if (warp() == 0) {
             float bv = -INFINITY;
             unsigned bi = NONE_IDX;
@@ -918,14 +1025,15 @@ public:
         return qw_sm.token;
     }
 
-    __device__ __noinline__ void store_rows(u64* dst, const GemvGeo& g, uint32_t tg) {
+    __device__ __noinline__ static void store_rows(u64* dst, const GemvGeo& g, uint32_t tg) {
         #pragma unroll 1
         for (int i = tid(); i < g.r1 - g.r0; i += NCT) st_relaxed_u64(dst + g.r0 + i, tagged(row_value(g, i), tg));
     }
 
-    __device__ __noinline__ void residual_rows(const GemvGeo& g, uint32_t tg) {  // x[r] += y[r] on this CTA's rows
+    __device__ __noinline__ static void residual_rows(const GemvGeo& g, uint32_t tg) {  // x[r] += y[r] on this CTA's rows
         #pragma unroll 1
         for (int i = tid(); i < g.r1 - g.r0; i += NCT) {
+        const DecodeParams& p = qw_sm.prm;
             const float v = xloc()[i] + row_value(g, i);
             xloc()[i] = v;
             st_relaxed_u64(p.x + g.r0 + i, tagged(v, tg));
@@ -933,84 +1041,120 @@ public:
     }
 
     // ------------------------------------------------------------------ consumer main loop
-    __device__ void consume() {
-        unsigned token = __ldcg(p.tok_in);
-        if (token >= (unsigned)p.V) {
-            if (tid() == 0) fail(DERR_BAD_TOKEN, (int)token);
-            token = 0;
+    // Loop state of the token/layer loops, per warp in shared memory. The loops call out-of-line
+    // phase routines that may use every register; a loop counter held in a register across such a
+    // call would be spilled to local memory. Reading the state back from shared memory after each
+    // call (volatile: the compiler may not keep a copy) leaves no value that has to survive a call.
+    // (%tid.x is read with a volatile asm so that the compiler re-reads it instead of keeping the
+    // derived address live across the calls)
+    __device__ __forceinline__ static volatile LoopState& ls() {
+        uint32_t t;
+        asm volatile("mov.u32 %0, %%tid.x;" : "=r"(t));
+        return qw_sm.loop[t >> 5];
+    }
+    __device__ __forceinline__ static const volatile DecodeParams& vprm() { return qw_sm.prm; }
+    __device__ __forceinline__ static int cur_step() { return ls().step; }
+    __device__ __forceinline__ static int cur_layer() { return ls().l; }
+    __device__ __forceinline__ static const uint16_t* layer_norms() {
+        return vprm().layer_n + (size_t)cur_layer() * vprm().norm_stride;
+    }
+    __device__ __forceinline__ static uint32_t ltag(int ph) { return tag(seq(cur_step(), cur_layer(), ph)); }
+    __device__ __forceinline__ static void lstamp(int k) { stamp(cur_step(), cur_layer() * TRACE_PER_LAYER + k); }
+    __device__ __forceinline__ static void tstamp(int k) { stamp(cur_step(), vprm().L * TRACE_PER_LAYER + k); }
+
+    // h[r] = silu(gate_r) * up_r on this CTA's interleaved gate/up rows (cpu_inference.rs:166-170, :187)
+    __device__ __noinline__ static void silu_rows(uint32_t tg) {
+        const GemvGeo& g = gD();
+        u64* const h = qw_sm.prm.hbuf;
+        #pragma unroll 1
+        for (int i = tid(); i < (g.r1 - g.r0) / 2; i += NCT) {
+            const float gt = row_value(g, 2 * i), up = row_value(g, 2 * i + 1);
+            st_relaxed_u64(h + g.r0 / 2 + i, tagged(gt / (1.0f + __expf(-gt)) * up, tg));
         }
-        for (int step = 0; step < p.steps; step++) {
-            const int pos = p.start_pos + step;
-            for (int l = 0; l < p.L; l++) {
-                const uint16_t* nrm = p.layer_n + (size_t)l * p.norm_stride;
-                // A: rmsnorm(x) -> q|k|v rows
-                const int tb = l * TRACE_PER_LAYER;
-                stamp(step, tb + 0);
-                norm_prologue(nrm, l == 0, token, l == 0 ? 0u : tag(seq(step, l - 1, 5)));
-                stamp(step, tb + 1);
-                gemv_consume(gA());
-                store_rows(p.qkv, gA(), tag(seq(step, l, 1)));
-                stamp(step, tb + 2);
-                // B: q/k norm + rope, KV append, attention (partials, then the chunk-0 merge)
-                attention_consume(step, l, pos);
-                stamp(step, tb + 5);
-                // C: o_proj + residual
-                gather(p.att, QD(), tag(seq(step, l, 2)));
-                stamp(step, tb + 6);
-                gemv_consume(gC());
-                residual_rows(gC(), tag(seq(step, l, 3)));
-                stamp(step, tb + 7);
-                // D: rmsnorm(x) -> gate|up -> silu(gate) * up
-                norm_prologue(nrm + p.H, false, 0, tag(seq(step, l, 3)));
-                stamp(step, tb + 8);
-                gemv_consume(gD());
-                {
-                    const uint32_t tg = tag(seq(step, l, 4));
-                    #pragma unroll 1
-                    for (int i = tid(); i < (gD().r1 - gD().r0) / 2; i += NCT) {
-                        const float gt = row_value(gD(), 2 * i), up = row_value(gD(), 2 * i + 1);
-                        st_relaxed_u64(p.hbuf + gD().r0 / 2 + i, tagged(gt / (1.0f + __expf(-gt)) * up, tg));
-                    }
-                }
-                // E: down_proj + residual
-                stamp(step, tb + 9);
-                gather(p.hbuf, p.I, tag(seq(step, l, 4)));
-                stamp(step, tb + 10);
-                gemv_consume(gE());
-                residual_rows(gE(), tag(seq(step, l, 5)));
-                stamp(step, tb + 11);
-            }
-            // F: final rmsnorm -> lm_head -> argmax partials -> end-of-token barrier -> next token
-            const int tt = p.L * TRACE_PER_LAYER;
-            norm_prologue(p.final_norm, false, 0, tag(seq(step, p.L - 1, 5)));
-            stamp(step, tt + 0);
-            gemv_consume(gF());
-            lm_epilogue();
-            stamp(step, tt + 1);
-            token_barrier((uint32_t)step + 1);
-            stamp(step, tt + 2);
-            token = argmax_combine();
-            stamp(step, tt + 3);
-            if (cta() == 0 && tid() == 0 && !aborted()) {
-                if (p.tok_out) p.tok_out[step + 1] = token;
-                if (p.host_tok) {
-                    volatile uint32_t* ht = p.host_tok;
-                    ht[step + 1] = token;
-                    __threadfence_system();
-                    *reinterpret_cast<volatile unsigned*>(p.host_count) = (unsigned)(step + 1);
-                }
+    }
+
+    // CTA 0 hands step `step`'s token to the device ring and the mapped host mirror
+    __device__ __noinline__ static void publish_token(int step, unsigned token) {
+        const DecodeParams& p = qw_sm.prm;
+        if (cta() == 0 && tid() == 0 && !aborted()) {
+            if (p.tok_out) p.tok_out[step + 1] = token;
+            if (p.host_tok) {
+                volatile uint32_t* ht = p.host_tok;
+                ht[step + 1] = token;
+                __threadfence_system();
+                *reinterpret_cast<volatile unsigned*>(p.host_count) = (unsigned)(step + 1);
             }
         }
     }
 
+    // one layer: A rmsnorm + q|k|v, B attention, C o + residual, D rmsnorm + gate|up + SiLU, E down + residual
+    __device__ __forceinline__ static void consume_layer() {
+        lstamp(0);
+        norm_prologue(layer_norms(), cur_layer() == 0, ls().token, cur_layer() == 0 ? 0u : tag(seq(cur_step(), cur_layer() - 1, 5)));
+        lstamp(1);
+        gemv_consume(gA());
+        store_rows(vprm().qkv, gA(), ltag(1));
+        lstamp(2);
+        attention_consume(cur_step(), cur_layer(), vprm().start_pos + cur_step());
+        lstamp(5);
+        gather(vprm().att, QD(), ltag(2));
+        lstamp(6);
+        gemv_consume(gC());
+        residual_rows(gC(), ltag(3));
+        lstamp(7);
+        norm_prologue(layer_norms() + vprm().H, false, 0, ltag(3));
+        lstamp(8);
+        gemv_consume(gD());
+        silu_rows(ltag(4));
+        lstamp(9);
+        gather(vprm().hbuf, vprm().I, ltag(4));
+        lstamp(10);
+        gemv_consume(gE());
+        residual_rows(gE(), ltag(5));
+        lstamp(11);
+    }
+
+    __device__ static void consume() {
+        {
+            const DecodeParams& p = qw_sm.prm;
+            unsigned token = __ldcg(p.tok_in);
+            if (token >= (unsigned)p.V) {
+                if (tid() == 0) fail(DERR_BAD_TOKEN, (int)token);
+                token = 0;
+            }
+            ls().token = token;
+        }
+        for (ls().step = 0; cur_step() < vprm().steps; ls().step = cur_step() + 1) {
+            for (ls().l = 0; cur_layer() < vprm().L; ls().l = cur_layer() + 1) consume_layer();
+            // F: final rmsnorm -> lm_head -> argmax partials -> end-of-token barrier -> next token
+            norm_prologue(vprm().final_norm, false, 0, tag(seq(cur_step(), vprm().L - 1, 5)));
+            tstamp(0);
+            gemv_consume(gF());
+            lm_epilogue();
+            tstamp(1);
+            token_barrier((uint32_t)cur_step() + 1);
+            tstamp(2);
+            ls().token = argmax_combine();
+            tstamp(3);
+            publish_token(cur_step(), ls().token);
+        }
+    }
+
     // ------------------------------------------------------------------ producer
-    __device__ bool slot_acquire(uint32_t& slot) {
+    __device__ static bool slot_acquire(uint32_t& slot) {
+        uint32_t& it = ring_pos();
         slot = it % NSLOT;
         const uint32_t par = ((it / NSLOT) & 1) ^ 1;
         return wait_mbar(&qw_sm.empty[slot], par, DERR_TIMEOUT_EMPTY);
     }
 
-    __device__ __noinline__ void gemv_produce(const GemvGeo& g, const uint16_t* wbase, uint64_t pol) {
+    __device__ __forceinline__ static const uint16_t* layer_weights(int l) {
+        return vprm().layer_w + (size_t)l * vprm().layer_stride;
+    }
+
+    __device__ __noinline__ static void gemv_produce(const GemvGeo& g, const uint16_t* wbase) {
+        const uint64_t pol = policy_evict_first();
+        uint32_t& it = ring_pos();
         for (int r = g.r0; r < g.r1; r += g.rpp) {
             const int nr = min(g.rpp, g.r1 - r);
             uint32_t slot;
@@ -1018,13 +1162,15 @@ public:
                 const uint32_t bytes = (uint32_t)nr * (uint32_t)g.K * 2u;
                 mbar_arrive_expect_tx(&qw_sm.full[slot], bytes);
                 bulk_g2s_evict_first(ring() + slot * SLOT_BYTES, wbase + g.woff + (size_t)r * g.K, bytes, &qw_sm.full[slot], pol);
-                n_issued = it + 1;
+                qw_sm.n_issued = it + 1;
             }
             ++it;
         }
     }
 
-    __device__ __noinline__ void attn_produce(int step, int l, int pos) {
+    __device__ __noinline__ static void attn_produce(int step, int l, int pos) {
+        const DecodeParams& p = qw_sm.prm;
+        uint32_t& it = ring_pos();
         const AttnItem a = attn_item(p, cta(), pos);
         if (!a.active) return;
         const int tc1 = a.has_cur ? pos : a.t1;
@@ -1051,7 +1197,7 @@ public:
                 uint8_t* dst = ring() + slot * SLOT_BYTES;
                 bulk_g2s(dst, p.kc + (head + t) * HD, bytes, &qw_sm.full[slot]);
                 bulk_g2s(dst + ATT_P * HD * 4, p.vc + (head + t) * HD, bytes, &qw_sm.full[slot]);
-                n_issued = it + 1;
+                qw_sm.n_issued = it + 1;
             }
             ++it;
         }
@@ -1060,7 +1206,7 @@ public:
     // warm L2 with this CTA's rows of one layer (A, C, D, E), so the ring's bulk copies of that
     // layer hit L2: the ring holds less than a layer, and without this the next layer's first
     // pieces would be fetched from HBM only once the current layer's last pieces are released
-    __device__ __noinline__ void prefetch_layer(const uint16_t* W) const {
+    __device__ __noinline__ static void prefetch_layer(const uint16_t* W) {
         const GemvGeo* gs[4] = {&gA(), &gC(), &gD(), &gE()};
         for (int k = 0; k < 4; k++) {
             const GemvGeo& g = *gs[k];
@@ -1069,30 +1215,28 @@ public:
         }
     }
 
-    __device__ void prefetch_lm_head() const {
+    __device__ static void prefetch_lm_head() {
+        const DecodeParams& p = qw_sm.prm;
         const GemvGeo& g = gF();
         const uint32_t all = (uint32_t)(g.r1 - g.r0) * (uint32_t)g.K * 2u;
         const uint32_t bytes = all < LM_PREFETCH_BYTES ? all : LM_PREFETCH_BYTES;
         if (bytes) bulk_prefetch_l2(p.lm_head + (size_t)g.r0 * g.K, bytes);
     }
 
-    __device__ void produce() {
-        const uint64_t pol = policy_evict_first();
-        prefetch_layer(p.layer_w);
-        for (int step = 0; step < p.steps; step++) {
-            const int pos = p.start_pos + step;
-            for (int l = 0; l < p.L; l++) {
-                const uint16_t* W = p.layer_w + (size_t)l * p.layer_stride;
-                if (l + 1 < p.L) prefetch_layer(W + p.layer_stride);
+    __device__ static void produce() {
+        prefetch_layer(vprm().layer_w);
+        for (ls().step = 0; cur_step() < vprm().steps; ls().step = cur_step() + 1) {
+            for (ls().l = 0; cur_layer() < vprm().L; ls().l = cur_layer() + 1) {
+                if (cur_layer() + 1 < vprm().L) prefetch_layer(layer_weights(cur_layer() + 1));
                 else prefetch_lm_head();
-                gemv_produce(gA(), W, pol);
-                attn_produce(step, l, pos);
-                gemv_produce(gC(), W, pol);
-                gemv_produce(gD(), W, pol);
-                gemv_produce(gE(), W, pol);
+                gemv_produce(gA(), layer_weights(cur_layer()));
+                attn_produce(cur_step(), cur_layer(), vprm().start_pos + cur_step());
+                gemv_produce(gC(), layer_weights(cur_layer()));
+                gemv_produce(gD(), layer_weights(cur_layer()));
+                gemv_produce(gE(), layer_weights(cur_layer()));
             }
-            if (step + 1 < p.steps) prefetch_layer(p.layer_w);
-            gemv_produce(gF(), p.lm_head, pol);
+            if (cur_step() + 1 < vprm().steps) prefetch_layer(vprm().layer_w);
+            gemv_produce(gF(), vprm().lm_head);
         }
         drain();
     }
@@ -1101,10 +1245,11 @@ public:
     // abort, wait (bounded) for the copies still in flight before the CTA may exit. Consumers stop
     // releasing slots once they abort, so only the last NSLOT issued pieces can be outstanding,
     // one per slot.
-    __device__ __noinline__ void drain() {
+    __device__ __noinline__ static void drain() {
+        const DecodeParams& p = qw_sm.prm;
         if (aborted()) {
-            const uint32_t first = n_issued > NSLOT ? n_issued - NSLOT : 0;
-            for (uint32_t j = first; j < n_issued; j++) {
+            const uint32_t first = qw_sm.n_issued > NSLOT ? qw_sm.n_issued - NSLOT : 0;
+            for (uint32_t j = first; j < qw_sm.n_issued; j++) {
                 const int slot = j % NSLOT;
                 const uint32_t par = (j / NSLOT) & 1;
                 const uint64_t t0 = globaltimer_ns();

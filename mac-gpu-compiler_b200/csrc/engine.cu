@@ -101,16 +101,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
         qw_sm.progress = 0;
         qw_sm.abort = 0;
         qw_sm.token = 0;
+        qw_sm.prm = p;
+        for (int w = 0; w <= NCW; w++) qw_sm.ring_it[w] = 0;
+        qw_sm.n_issued = 0;
         Decoder::init_geometry(p);
         fence_mbar_init();
     }
     __syncthreads();
-    Decoder d(p);
     if (Decoder::warp() == NCW) {
-        if (Decoder::lane() == 0) d.produce();
+        if (Decoder::lane() == 0) Decoder::produce();
         return;
     }
-    d.consume();
+    Decoder::consume();
 }
 
 }  // namespace qw
@@ -204,8 +206,8 @@ int launch_decode(qw_model* m, qw_cache* c, const uint32_t* tok_in, uint32_t* to
     p.rope = c->d_rope;
     p.x = m->d_x;
     p.qkv = m->d_qkv;
-    p.att = m->d_att;
     p.hbuf = m->d_h;
+    p.att = m->d_att;
     p.apart = m->d_apart;
     p.am_val = m->d_am_val;
     p.am_idx = m->d_am_idx;
@@ -381,7 +383,8 @@ int qw_load(const char* path, int device, qw_model** out) {
     auto phase_cap = [&](uint64_t rows, uint64_t K) { return (uint64_t)seg_count((int)K) * (ceil_div(rows, nctas) + 2); };
     uint64_t pc = std::max({phase_cap(QKVR, H), phase_cap(H, QD), phase_cap(2 * I, H) + 2, phase_cap(H, I), phase_cap(c.vocab, H)});
     // part also stages the attention merge's partials: (S - 1) chunks x G heads x 128
-    m->part_cap = (int)align_up(std::max<uint64_t>(pc, (uint64_t)(m->S - 1) * G * HD), 4);
+    // and the 12 consumer warps' attention softmax states: NCW x G x ATT_WST
+    m->part_cap = (int)align_up(std::max<uint64_t>({pc, (uint64_t)(m->S - 1) * G * HD, (uint64_t)NCW * G * ATT_WST}), 4);
     m->xs_cap = (int)align_up(std::max({H, QD, I}), 4);
     m->xloc_cap = (int)align_up(ceil_div(H, nctas) + 2, 4);
     m->dyn_smem = (size_t)NSLOT * SLOT_BYTES + ((size_t)m->part_cap + m->xs_cap + m->xloc_cap) * 4;

@@ -33,23 +33,25 @@ gemv_kernel(const __grid_constant__ DecodeParams p, const uint16_t* w, const flo
         }
         qw_sm.progress = 0;
         qw_sm.abort = 0;
+        qw_sm.prm = p;
+        for (int k = 0; k <= NCW; k++) qw_sm.ring_it[k] = 0;
+        qw_sm.n_issued = 0;
         qw_sm.geo[0] = make_geo(rows, cols, blockIdx.x, gridDim.x, 0, 0);
         fence_mbar_init();
     }
     __syncthreads();
-    Decoder d(p);
     const GemvGeo& g = qw_sm.geo[0];
     if (Decoder::warp() == NCW) {
         if (Decoder::lane() == 0) {
-            d.gemv_produce(g, w, policy_evict_first());
-            d.drain();
+            Decoder::gemv_produce(g, w);
+            Decoder::drain();
         }
         return;
     }
     for (int i = Decoder::tid(); i < cols; i += NCT) Decoder::xs()[i] = x[i];
     named_bar_sync(1, NCT);
-    d.gemv_consume(g);
-    for (int i = Decoder::tid(); i < g.r1 - g.r0; i += NCT) y[g.r0 + i] = d.row_value(g, i);
+    Decoder::gemv_consume(g);
+    for (int i = Decoder::tid(); i < g.r1 - g.r0; i += NCT) y[g.r0 + i] = Decoder::row_value(g, i);
 }
 
 // argmax with the reference CPU rule, in two levels inside one launch (last-block reduction)
