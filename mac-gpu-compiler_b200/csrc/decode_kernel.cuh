@@ -143,6 +143,22 @@ __host__ __device__ inline int seg_count(int K) {
     return (K % 1024 == 0 && 12 % (K / 1024) == 0) ? K / 1024 : 0;
 }
 
+// Shared-memory layout of a GEMV input vector: within each block of 256 columns, lane l's two
+// float4 of columns 8l .. 8l+3 and 8l+4 .. 8l+7 are stored at float4 slots l and 32 + l, so the
+// warp-wide float4 loads of a 1024-column segment are contiguous 512-byte accesses (no bank
+// conflicts). Consecutive even/odd columns stay adjacent.
+__host__ __device__ inline int xperm(int c) {
+    return (c & ~255) | ((c & 4) << 5) | (((c >> 3) & 31) << 2) | (c & 3);
+}
+
+// per consumer warp, per GEMV phase: what the warp does in each ring piece
+struct WarpGeo {
+    int npieces;      // ring pieces of the phase
+    int myseg;        // the column segment this warp holds in registers
+    int rl;           // the row of each piece this warp works on
+    int wbyte;        // byte offset of that row's segment within a piece
+};
+
 __device__ inline GemvGeo make_geo(long long rows, int K, int cta, int n, long long woff, int pair) {
     GemvGeo g;
     if (pair) {  // gate/up: partition pairs so each CTA owns whole (gate_i, up_i) row pairs
@@ -160,6 +176,15 @@ __device__ inline GemvGeo make_geo(long long rows, int K, int cta, int n, long l
     g.cpl = g.segw / 256;
     g.woff = woff;
     return g;
+}
+
+__device__ inline WarpGeo make_warp_geo(const GemvGeo& g, int w) {
+    WarpGeo wg;
+    wg.npieces = (g.r1 - g.r0 + g.rpp - 1) / g.rpp;
+    wg.myseg = g.segs ? w % g.segs : 0;
+    wg.rl = g.segs ? w / g.segs : 0;
+    wg.wbyte = (wg.rl * g.K + wg.myseg * g.segw) * 2;
+    return wg;
 }
 
 // attention work item of a CTA at a given position (same answer in producer and consumers)
@@ -195,6 +220,7 @@ struct Smem {
     __align__(16) float ks[HD];
     __align__(16) float vs[HD];
     GemvGeo geo[5];              // this CTA's rows of phases A (q|k|v), C (o), D (gate|up), E (down), F (lm_head)
+    WarpGeo wgeo[5][NCW];        // per phase and consumer warp (see WarpGeo)
     float ml[MAX_S][MAX_G][2];   // attention partials' (m, l) gathered by the merging CTA
     float red[64];
     float redv[NCW];
@@ -289,6 +315,8 @@ public:
         qw_sm.geo[2] = make_geo(2LL * p.I, p.H, c, nc, offD, 1);
         qw_sm.geo[3] = make_geo(p.H, p.I, c, nc, offE, 0);
         qw_sm.geo[4] = make_geo(p.V, p.H, c, nc, 0, 0);
+        for (int k = 0; k < 5; k++)
+            for (int w = 0; w < NCW; w++) qw_sm.wgeo[k][w] = make_warp_geo(qw_sm.geo[k], w);
     }
 
     // phase sequence numbers within the launch -> tags (12 bits of epoch, 20 bits of sequence)
@@ -397,8 +425,7 @@ public:
                 for (int j = 0; j < GP; j++) {
                     if ((pending & (1u << j)) && word_tag(w[j].x) == tg && word_tag(w[j].y) == tg) {
                         const int i = 2 * (base + tid() + j * NCT);
-                        xs()[i] = word_val(w[j].x);
-                        xs()[i + 1] = word_val(w[j].y);
+                        *reinterpret_cast<float2*>(xs() + xperm(i)) = make_float2(word_val(w[j].x), word_val(w[j].y));
                         pending &= ~(1u << j);
                     }
                 }
@@ -478,7 +505,7 @@ public:
             #pragma unroll 1
             for (int i = tid(); i < H; i += NCT) {
                 const float v = bf16_to_f32(__ldg(erow + i));
-                xs()[i] = v;
+                xs()[xperm(i)] = v;
                 if (i >= gC().r0 && i < gC().r1) xloc()[i - gC().r0] = v;
             }
             named_bar_sync(1, NCT);
@@ -489,19 +516,19 @@ public:
 #pragma unroll
         for (int k = 0; k < MAXK; k++) {
             const int i = tid() + k * NCT;
-            if (i < H) ss = fmaf(xs()[i], xs()[i], ss);
+            if (i < H) ss = fmaf(xs()[xperm(i)], xs()[xperm(i)], ss);
         }
         #pragma unroll 1
-        for (int i = tid() + MAXK * NCT; i < H; i += NCT) ss = fmaf(xs()[i], xs()[i], ss);
+        for (int i = tid() + MAXK * NCT; i < H; i += NCT) ss = fmaf(xs()[xperm(i)], xs()[xperm(i)], ss);
         const float tot = block_sum(ss);
         const float sc = rsqrtf(tot / (float)H + p.eps);
 #pragma unroll
         for (int k = 0; k < MAXK; k++) {
             const int i = tid() + k * NCT;
-            if (i < H) xs()[i] = xs()[i] * sc * wg[k];
+            if (i < H) xs()[xperm(i)] = xs()[xperm(i)] * sc * wg[k];
         }
         #pragma unroll 1
-        for (int i = tid() + MAXK * NCT; i < H; i += NCT) xs()[i] = xs()[i] * sc * bf16_to_f32(__ldg(w + i));
+        for (int i = tid() + MAXK * NCT; i < H; i += NCT) xs()[xperm(i)] = xs()[xperm(i)] * sc * bf16_to_f32(__ldg(w + i));
         named_bar_sync(1, NCT);
     }
 
@@ -525,8 +552,8 @@ public:
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             if (i < g.cpl) {
-                const float4* xp = reinterpret_cast<const float4*>(xs() + myseg * g.segw + (i * 32 + ln) * 8);
-                float4 a = xp[0], b = xp[1];
+                const float4* xp = reinterpret_cast<const float4*>(xs() + myseg * g.segw) + i * 64 + ln;
+                float4 a = xp[0], b = xp[32];
                 xr[i * 8 + 0] = a.x; xr[i * 8 + 1] = a.y; xr[i * 8 + 2] = a.z; xr[i * 8 + 3] = a.w;
                 xr[i * 8 + 4] = b.x; xr[i * 8 + 5] = b.y; xr[i * 8 + 6] = b.z; xr[i * 8 + 7] = b.w;
             } else {
@@ -617,20 +644,21 @@ public:
         uint32_t& it = ring_pos();
         const GemvGeo g = gs;
         const int w = warp(), ln = lane();
-        const int myseg = w % g.segs, rl = w / g.segs;
+        const WarpGeo wgo = qw_sm.wgeo[&gs - qw_sm.geo][w];
+        const int myseg = wgo.myseg, rl = wgo.rl;
         float xr[32];
         {
-            const float4* xp = reinterpret_cast<const float4*>(xs() + myseg * 1024 + ln * 8);
+            const float4* xp = reinterpret_cast<const float4*>(xs() + myseg * 1024) + ln;
 #pragma unroll
             for (int i = 0; i < 4; i++) {
-                const float4 a = xp[i * 64], b = xp[i * 64 + 1];
+                const float4 a = xp[i * 64], b = xp[i * 64 + 32];
                 xr[i * 8 + 0] = a.x; xr[i * 8 + 1] = a.y; xr[i * 8 + 2] = a.z; xr[i * 8 + 3] = a.w;
                 xr[i * 8 + 4] = b.x; xr[i * 8 + 5] = b.y; xr[i * 8 + 6] = b.z; xr[i * 8 + 7] = b.w;
             }
         }
         float* const prt = part();
-        const int npieces = (g.r1 - g.r0 + g.rpp - 1) / g.rpp;
-        const size_t woff = ((size_t)rl * g.K + (size_t)myseg * 1024) * 2 + (size_t)ln * 16;
+        const int npieces = wgo.npieces;
+        const int woff = wgo.wbyte + ln * 16;
         uint32_t pc = it;
         // a phase whose pieces all fit in the ring releases them once, after the phase's closing
         // barrier below; a longer one (lm_head) releases each group as soon as it is read

@@ -37,6 +37,7 @@ gemv_kernel(const __grid_constant__ DecodeParams p, const uint16_t* w, const flo
         for (int k = 0; k <= NCW; k++) qw_sm.ring_it[k] = 0;
         qw_sm.n_issued = 0;
         qw_sm.geo[0] = make_geo(rows, cols, blockIdx.x, gridDim.x, 0, 0);
+        for (int w = 0; w < NCW; w++) qw_sm.wgeo[0][w] = make_warp_geo(qw_sm.geo[0], w);
         fence_mbar_init();
     }
     __syncthreads();
@@ -48,7 +49,7 @@ gemv_kernel(const __grid_constant__ DecodeParams p, const uint16_t* w, const flo
         }
         return;
     }
-    for (int i = Decoder::tid(); i < cols; i += NCT) Decoder::xs()[i] = x[i];
+    for (int i = Decoder::tid(); i < cols; i += NCT) Decoder::xs()[xperm(i)] = x[i];
     named_bar_sync(1, NCT);
     Decoder::gemv_consume(g);
     for (int i = Decoder::tid(); i < g.r1 - g.r0; i += NCT) y[g.r0 + i] = Decoder::row_value(g, i);
