@@ -223,6 +223,7 @@ struct Smem {
     WarpGeo wgeo[5][NCW];        // per phase and consumer warp (see WarpGeo)
     float ml[MAX_S][MAX_G][2];   // attention partials' (m, l) gathered by the merging CTA
     float red[64];
+    float ssq[NCW];              // per consumer warp: sum of squares of the last RMSNorm input
     float redv[NCW];
     unsigned redi[NCW];
     uint64_t full[NSLOT];
@@ -406,14 +407,28 @@ public:
     }
 
     // xs[0..K) <- values of the tagged words src[0..K) once each carries `tg` (K even, src 16-byte aligned)
-    __device__ __noinline__ static void gather(const u64* src, int K, uint32_t tg) {
+    //
+    // With `gain` (an RMSNorm input): xs holds x * gain, and each warp's sum of x^2 goes to
+    // ssq[warp]; the GEMV that follows applies the scale rsqrt(mean(x^2) + eps) to its row outputs
+    // (norm_scale), which is the same product regrouped. The gains of a thread's pairs are fetched
+    // before it starts polling, and the squares are summed in a fixed order (arrival order varies).
+    __device__ __noinline__ static void gather(const u64* src, int K, uint32_t tg, const uint16_t* gain = nullptr) {
         const DecodeParams& p = qw_sm.prm;
         const int npairs = K >> 1;
+        float ss = 0.f;
         for (int base = 0; base < npairs; base += NCT * GP) {
             unsigned pending = 0;
+            uint32_t g2[GP];
+            float sq[GP];
 #pragma unroll
-            for (int j = 0; j < GP; j++)
-                if (base + tid() + j * NCT < npairs) pending |= 1u << j;
+            for (int j = 0; j < GP; j++) {
+                sq[j] = 0.f;
+                g2[j] = 0x3F803F80u;  // (1.0, 1.0) in bf16
+                if (base + tid() + j * NCT < npairs) {
+                    pending |= 1u << j;
+                    if (gain) g2[j] = __ldg(reinterpret_cast<const uint32_t*>(gain) + base + tid() + j * NCT);
+                }
+            }
             uint32_t spins = 0;
             uint64_t t0 = 0;
             while (pending && !aborted()) {
@@ -425,7 +440,9 @@ public:
                 for (int j = 0; j < GP; j++) {
                     if ((pending & (1u << j)) && word_tag(w[j].x) == tg && word_tag(w[j].y) == tg) {
                         const int i = 2 * (base + tid() + j * NCT);
-                        *reinterpret_cast<float2*>(xs() + xperm(i)) = make_float2(word_val(w[j].x), word_val(w[j].y));
+                        const float a = word_val(w[j].x), b = word_val(w[j].y);
+                        sq[j] = fmaf(a, a, b * b);
+                        *reinterpret_cast<float2*>(xs() + xperm(i)) = make_float2(a * bf16_lo(g2[j]), b * bf16_hi(g2[j]));
                         pending &= ~(1u << j);
                     }
                 }
@@ -434,6 +451,12 @@ public:
                     if (p.poll_ns) __nanosleep(p.poll_ns);
                 }
             }
+#pragma unroll
+            for (int j = 0; j < GP; j++) ss += sq[j];
+        }
+        if (gain) {
+            ss = warp_sum(ss);
+            if (lane() == 0) qw_sm.ssq[warp()] = ss;
         }
         named_bar_sync(1, NCT);
     }
@@ -473,63 +496,37 @@ public:
     }
 
     // ------------------------------------------------------------------ consumer helpers
-    __device__ static float block_sum(float v) {
-        v = warp_sum(v);
-        if (lane() == 0) qw_sm.red[warp()] = v;
-        named_bar_sync(1, NCT);
-        if (warp() == 0) {
-            float t = lane() < NCW ? qw_sm.red[lane()] : 0.f;
-            t = warp_sum(t);
-            if (lane() == 0) qw_sm.red[32] = t;
-        }
-        named_bar_sync(1, NCT);
-        return qw_sm.red[32];
-    }
-
-    // xs <- rmsnorm(src) * w  (cpu_inference.rs:189-194). src is the tagged residual stream, or
-    // (from_embed) the embedding row of `token`, in which case the CTA also initialises its own
-    // residual rows xloc from that row.
+    // RMSNorm input of a GEMV phase (cpu_inference.rs:189-194): xs <- x * w and ssq <- the warps'
+    // sums of x^2; the phase's epilogue multiplies its row outputs by norm_scale(). x is the tagged
+    // residual stream, or (from_embed) the embedding row of `token`, in which case the CTA also
+    // initialises its own residual rows xloc from that row.
     __device__ __noinline__ static void norm_prologue(const uint16_t* w, bool from_embed, unsigned token, uint32_t tg) {
         const DecodeParams& p = qw_sm.prm;
+        if (!from_embed) {
+            gather(p.x, p.H, tg, w);
+            return;
+        }
         const int H = p.H;
-        // the gains do not depend on the token: fetch them before waiting for the input
-        constexpr int MAXK = 8;  // H <= 8 * 384 keeps them in registers
-        float wg[MAXK];
-#pragma unroll
-        for (int k = 0; k < MAXK; k++) {
-            const int i = tid() + k * NCT;
-            wg[k] = i < H ? bf16_to_f32(__ldg(w + i)) : 0.f;
-        }
-        if (from_embed) {
-            const uint16_t* erow = p.embed + (size_t)token * H;
-            #pragma unroll 1
-            for (int i = tid(); i < H; i += NCT) {
-                const float v = bf16_to_f32(__ldg(erow + i));
-                xs()[xperm(i)] = v;
-                if (i >= gC().r0 && i < gC().r1) xloc()[i - gC().r0] = v;
-            }
-            named_bar_sync(1, NCT);
-        } else {
-            gather(p.x, H, tg);
-        }
+        const uint16_t* erow = p.embed + (size_t)token * H;
         float ss = 0.f;
-#pragma unroll
-        for (int k = 0; k < MAXK; k++) {
-            const int i = tid() + k * NCT;
-            if (i < H) ss = fmaf(xs()[xperm(i)], xs()[xperm(i)], ss);
-        }
         #pragma unroll 1
-        for (int i = tid() + MAXK * NCT; i < H; i += NCT) ss = fmaf(xs()[xperm(i)], xs()[xperm(i)], ss);
-        const float tot = block_sum(ss);
-        const float sc = rsqrtf(tot / (float)H + p.eps);
-#pragma unroll
-        for (int k = 0; k < MAXK; k++) {
-            const int i = tid() + k * NCT;
-            if (i < H) xs()[xperm(i)] = xs()[xperm(i)] * sc * wg[k];
+        for (int i = tid(); i < H; i += NCT) {
+            const float v = bf16_to_f32(__ldg(erow + i));
+            ss = fmaf(v, v, ss);
+            xs()[xperm(i)] = v * bf16_to_f32(__ldg(w + i));
+            if (i >= gC().r0 && i < gC().r1) xloc()[i - gC().r0] = v;
         }
-        #pragma unroll 1
-        for (int i = tid() + MAXK * NCT; i < H; i += NCT) xs()[xperm(i)] = xs()[xperm(i)] * sc * bf16_to_f32(__ldg(w + i));
+        ss = warp_sum(ss);
+        if (lane() == 0) qw_sm.ssq[warp()] = ss;
         named_bar_sync(1, NCT);
+    }
+
+    // 1 / sqrt(mean(x^2) + eps) of the last RMSNorm input (valid after the barrier closing its gather)
+    __device__ __forceinline__ static float norm_scale() {
+        float t = 0.f;
+#pragma unroll
+        for (int w = 0; w < NCW; w++) t += qw_sm.ssq[w];
+        return rsqrtf(t / (float)qw_sm.prm.H + qw_sm.prm.eps);
     }
 
     // All ring pieces of one GEMV phase: part[(row - r0) * segs + seg] = partial dot product.
@@ -998,13 +995,14 @@ public:
     // ------------------------------------------------------------------ lm_head + argmax
     __device__ __noinline__ static void lm_epilogue() {
         const DecodeParams& p = qw_sm.prm;
+        const float sc = norm_scale();
         const GemvGeo& g = gF();
         const int nloc = g.r1 - g.r0;
         float bv = -INFINITY;
         unsigned bi = NONE_IDX;
         #pragma unroll 1
         for (int i = tid(); i < nloc; i += NCT) {
-            const float y = row_value(g, i);
+            const float y = row_value(g, i) * sc;
             const unsigned row = (unsigned)(g.r0 + i);
             if (p.logits) __stcg(p.logits + row, y);
             if (!isnan(y) && am_better(y, row, bv, bi)) { bv = y; bi = row; }
@@ -1053,9 +1051,11 @@ public:
         return qw_sm.token;
     }
 
+    // q|k|v rows (phase A), with the RMSNorm scale of the phase's input
     __device__ __noinline__ static void store_rows(u64* dst, const GemvGeo& g, uint32_t tg) {
+        const float sc = norm_scale();
         #pragma unroll 1
-        for (int i = tid(); i < g.r1 - g.r0; i += NCT) st_relaxed_u64(dst + g.r0 + i, tagged(row_value(g, i), tg));
+        for (int i = tid(); i < g.r1 - g.r0; i += NCT) st_relaxed_u64(dst + g.r0 + i, tagged(row_value(g, i) * sc, tg));
     }
 
     __device__ __noinline__ static void residual_rows(const GemvGeo& g, uint32_t tg) {  // x[r] += y[r] on this CTA's rows
@@ -1094,9 +1094,10 @@ public:
     __device__ __noinline__ static void silu_rows(uint32_t tg) {
         const GemvGeo& g = gD();
         u64* const h = qw_sm.prm.hbuf;
+        const float sc = norm_scale();
         #pragma unroll 1
         for (int i = tid(); i < (g.r1 - g.r0) / 2; i += NCT) {
-            const float gt = row_value(g, 2 * i), up = row_value(g, 2 * i + 1);
+            const float gt = row_value(g, 2 * i) * sc, up = row_value(g, 2 * i + 1) * sc;
             st_relaxed_u64(h + g.r0 / 2 + i, tagged(gt / (1.0f + __expf(-gt)) * up, tg));
         }
     }
