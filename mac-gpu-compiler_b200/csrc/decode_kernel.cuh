@@ -775,8 +775,9 @@ public:
     // softmax, sum of p * v). The warp scores both positions against its Gh query heads with
     // butterfly sums, so every lane holds every score; the 2 x Gh sums are independent, so their
     // shuffle chains overlap. Then each head's state is rescaled once for the pair.
+    template <int GQ>
     __device__ __forceinline__ static void attn_pair(const float* K0, const float* V0, const float* K1, const float* V1,
-                                                     bool has1, const float4* q4, WarpSoftmax& ws, int Gh, float scale) {
+                                                     bool has1, const float4* q4, WarpSoftmax& ws, float scale) {
         const float4 k0 = reinterpret_cast<const float4*>(K0)[lane()];
         const float4 v0 = reinterpret_cast<const float4*>(V0)[lane()];
         float4 k1 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = k1;
@@ -786,23 +787,23 @@ public:
         }
         float s0[MAX_G], s1[MAX_G];
 #pragma unroll
-        for (int h = 0; h < MAX_G; h++) {
+        for (int h = 0; h < GQ; h++) {
             s0[h] = q4[h].x * k0.x + q4[h].y * k0.y + q4[h].z * k0.z + q4[h].w * k0.w;
             s1[h] = q4[h].x * k1.x + q4[h].y * k1.y + q4[h].z * k1.z + q4[h].w * k1.w;
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
 #pragma unroll
-            for (int h = 0; h < MAX_G; h++) {
-                if (h < Gh) {
+            for (int h = 0; h < GQ; h++) {
+                {
                     s0[h] += __shfl_xor_sync(0xFFFFFFFFu, s0[h], o);
                     s1[h] += __shfl_xor_sync(0xFFFFFFFFu, s1[h], o);
                 }
             }
         }
 #pragma unroll
-        for (int h = 0; h < MAX_G; h++) {
-            if (h < Gh) {
+        for (int h = 0; h < GQ; h++) {
+            {
                 const float a0 = s0[h] * scale, a1 = has1 ? s1[h] * scale : -INFINITY;
                 const float mn = fmaxf(ws.m[h], fmaxf(a0, a1));
                 const float corr = __expf(ws.m[h] - mn);  // 0 while m is still -inf
@@ -817,7 +818,10 @@ public:
         }
     }
 
-    __device__ __noinline__ static void attention_consume(int step, int l, int pos) {
+    // phase B for GQ query heads per KV head (a compile-time count: with a runtime count the
+    // per-position code roughly doubles in length)
+    template <int GQ>
+    __device__ __noinline__ static void attention_g(int step, int l, int pos) {
         const DecodeParams& p = qw_sm.prm;
         uint32_t& it = ring_pos();
         const AttnItem a = attn_item(p, cta(), pos);
@@ -828,10 +832,10 @@ public:
         const float2* rrow = p.rope + (size_t)pos * (HD / 2);
         const uint32_t tgA = tag(seq(step, l, 1)), tgB = tag(seq(step, l, 2));
         // q heads g*G .. g*G+G-1, and (last chunk) this position's k and v
-        if (warp() < G()) head_norm_rope(gather_head(p.qkv + (size_t)(a.g * G() + warp()) * HD, tgA), qn, rrow, qw_sm.qs[warp()]);
+        if (warp() < GQ) head_norm_rope(gather_head(p.qkv + (size_t)(a.g * GQ + warp()) * HD, tgA), qn, rrow, qw_sm.qs[warp()]);
         if (a.has_cur) {
-            if (warp() == G()) head_norm_rope(gather_head(p.qkv + QD() + (size_t)a.g * HD, tgA), kn, rrow, qw_sm.ks);
-            if (warp() == G() + 1)
+            if (warp() == GQ) head_norm_rope(gather_head(p.qkv + QD() + (size_t)a.g * HD, tgA), kn, rrow, qw_sm.ks);
+            if (warp() == GQ + 1)
                 reinterpret_cast<float4*>(qw_sm.vs)[lane()] = gather_head(p.qkv + QD() + KVD() + (size_t)a.g * HD, tgA);
         }
         named_bar_sync(1, NCT);
@@ -841,19 +845,18 @@ public:
             if (tid() < HD) p.kc[off + tid()] = qw_sm.ks[tid()];
             else p.vc[off + tid() - HD] = qw_sm.vs[tid() - HD];
         }
-        float4 q4[MAX_G];
+        float4 q4[GQ];
 #pragma unroll
-        for (int h = 0; h < MAX_G; h++)
-            q4[h] = h < G() ? reinterpret_cast<const float4*>(qw_sm.qs[h])[lane()] : make_float4(0, 0, 0, 0);
+        for (int h = 0; h < GQ; h++)
+            q4[h] = reinterpret_cast<const float4*>(qw_sm.qs[h])[lane()];
         // Each warp takes the chunk's positions j = warp, warp + 12, ... (j counted from t0), two per
         // call, and keeps its own running softmax: no CTA-wide barrier per ring piece. A piece holds
         // ATT_P = 24 = 2 x 12 positions, so position pp of a piece is chunk position j with
         // j % 12 == pp % 12.
         WarpSoftmax ws;
-        const int Gh = G();
         const float scale = p.scale;
 #pragma unroll
-        for (int h = 0; h < MAX_G; h++) {
+        for (int h = 0; h < GQ; h++) {
             ws.m[h] = -INFINITY;
             ws.l[h] = 0.f;
             ws.acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -870,22 +873,22 @@ public:
                 const float* Vb = Kb + ATT_P * HD;
                 if (ok)
                     for (int pp = warp(); pp < np; pp += 2 * NCW)
-                        attn_pair(Kb + pp * HD, Vb + pp * HD, Kb + (pp + NCW) * HD, Vb + (pp + NCW) * HD, pp + NCW < np, q4,
-                                  ws, Gh, scale);
+                        attn_pair<GQ>(Kb + pp * HD, Vb + pp * HD, Kb + (pp + NCW) * HD, Vb + (pp + NCW) * HD, pp + NCW < np, q4,
+                                  ws, scale);
             }
             __syncwarp();
             if (lane() == 0 && ok)
                 for (int j = 0; j < n; j++) mbar_arrive(&qw_sm.empty[(pc + j) % NSLOT]);
             it = pc + n;
         }
-        if (a.has_cur && warp() == (tc1 - a.t0) % NCW) attn_pair(qw_sm.ks, qw_sm.vs, nullptr, nullptr, false, q4, ws, Gh, scale);
+        if (a.has_cur && warp() == (tc1 - a.t0) % NCW) attn_pair<GQ>(qw_sm.ks, qw_sm.vs, nullptr, nullptr, false, q4, ws, scale);
         // combine the 12 warps' states in warp order (deterministic): stage [warp][h < G][acc 128 | m | l | pad]
         float* const wst = part();
         constexpr int WST = ATT_WST;
 #pragma unroll
-        for (int h = 0; h < MAX_G; h++) {
-            if (h < G()) {
-                float* d = wst + (warp() * G() + h) * WST;
+        for (int h = 0; h < GQ; h++) {
+            if (h < GQ) {
+                float* d = wst + (warp() * GQ + h) * WST;
                 reinterpret_cast<float4*>(d)[lane()] = ws.acc[h];
                 if (lane() == 0) {
                     d[HD] = ws.m[h];
@@ -895,13 +898,13 @@ public:
         }
         named_bar_sync(1, NCT);
         float m = -INFINITY, lsum = 0.f, acc = 0.f;
-        if (tid() < G() * HD) {
+        if (tid() < GQ * HD) {
             const int h = tid() >> 7, d = tid() & (HD - 1);
 #pragma unroll
-            for (int w = 0; w < NCW; w++) m = fmaxf(m, wst[(w * G() + h) * WST + HD]);
+            for (int w = 0; w < NCW; w++) m = fmaxf(m, wst[(w * GQ + h) * WST + HD]);
 #pragma unroll
             for (int w = 0; w < NCW; w++) {
-                const float* src = wst + (w * G() + h) * WST;
+                const float* src = wst + (w * GQ + h) * WST;
                 const float e = src[HD] == -INFINITY ? 0.f : __expf(src[HD] - m);  // a warp without positions adds nothing
                 lsum = fmaf(e, src[HD + 1], lsum);
                 acc = fmaf(e, src[d], acc);
@@ -909,12 +912,12 @@ public:
         }
         named_bar_sync(1, NCT);  // the warp states in part are dead: the merge below may reuse part
         stamp(step, l * TRACE_PER_LAYER + 4);
-        const size_t head_base = (size_t)a.g * p.S * G();  // partial (s, h) at apart[((head_base + s*G + h) * APART_STRIDE]
+        const size_t head_base = (size_t)a.g * p.S * GQ;  // partial (s, h) at apart[((head_base + s*G + h) * APART_STRIDE]
         if (a.s != 0) {
             // publish this chunk's partial as tagged words for the chunk-0 CTA of this KV head
-            if (tid() < G() * HD) {
+            if (tid() < GQ * HD) {
                 const int h = tid() >> 7, d = tid() & (HD - 1);
-                u64* dst = p.apart + (head_base + (size_t)a.s * G() + h) * APART_STRIDE;
+                u64* dst = p.apart + (head_base + (size_t)a.s * GQ + h) * APART_STRIDE;
                 st_relaxed_u64(dst + d, tagged(acc, tgB));
                 if (d == 0) {
                     st_relaxed_u64(dst + HD, tagged(m, tgB));
@@ -926,7 +929,7 @@ public:
         // chunk 0 merges the partials of chunks 0..S_eff-1 in chunk order: an accumulator thread
         // (h, d) polls word d of chunks 1.. (four chunks in flight per round) into the shared stage,
         // and the first (S_eff-1)*G*2 threads also poll one (m or l) word each.
-        if (tid() < G() * HD && (tid() & (HD - 1)) == 0) {
+        if (tid() < GQ * HD && (tid() & (HD - 1)) == 0) {
             qw_sm.ml[0][tid() >> 7][0] = m;
             qw_sm.ml[0][tid() >> 7][1] = lsum;
         }
@@ -935,9 +938,9 @@ public:
             const int h = tid() >> 7, d = tid() & (HD - 1);
             const u64* mlsrc = nullptr;
             float* mldst = nullptr;
-            if (tid() < (a.S_eff - 1) * G() * 2) {  // the first (S_eff-1)*G*2 threads also fetch one (m or l) word
-                const int s = 1 + tid() / (2 * G()), hh = (tid() >> 1) % G(), which = tid() & 1;
-                mlsrc = p.apart + (head_base + (size_t)s * G() + hh) * APART_STRIDE + HD + which;
+            if (tid() < (a.S_eff - 1) * GQ * 2) {  // the first (S_eff-1)*G*2 threads also fetch one (m or l) word
+                const int s = 1 + tid() / (2 * GQ), hh = (tid() >> 1) % GQ, which = tid() & 1;
+                mlsrc = p.apart + (head_base + (size_t)s * GQ + hh) * APART_STRIDE + HD + which;
                 mldst = &qw_sm.ml[s][hh][which];
             }
             // up to four chunks' words (bits 0-3) and the (m, l) word (bit 4) in flight per round
@@ -945,19 +948,19 @@ public:
                 uint32_t pending = mlsrc ? 16u : 0u;  // the (m, l) word is polled in the first round only
 #pragma unroll
                 for (int j = 0; j < 4; j++)
-                    if (tid() < G() * HD && s0 + j < a.S_eff) pending |= 1u << j;
+                    if (tid() < GQ * HD && s0 + j < a.S_eff) pending |= 1u << j;
                 uint32_t spins = 0;
                 uint64_t t0 = 0;
                 while (pending && !aborted()) {
                     u64 w[5];
 #pragma unroll
                     for (int j = 0; j < 4; j++)
-                        if (pending & (1u << j)) w[j] = ld_relaxed_u64(p.apart + (head_base + (size_t)(s0 + j) * G() + h) * APART_STRIDE + d);
+                        if (pending & (1u << j)) w[j] = ld_relaxed_u64(p.apart + (head_base + (size_t)(s0 + j) * GQ + h) * APART_STRIDE + d);
                     if (pending & 16u) w[4] = ld_relaxed_u64(mlsrc);
 #pragma unroll
                     for (int j = 0; j < 4; j++)
                         if ((pending & (1u << j)) && word_tag(w[j]) == tgB) {
-                            stage[(s0 + j - 1) * (G() * HD) + tid()] = word_val(w[j]);
+                            stage[(s0 + j - 1) * (GQ * HD) + tid()] = word_val(w[j]);
                             pending &= ~(1u << j);
                         }
                     if ((pending & 16u) && word_tag(w[4]) == tgB) {
@@ -974,7 +977,7 @@ public:
         }
         stamp(step, l * TRACE_PER_LAYER + 12);
         named_bar_sync(1, NCT);
-        if (tid() < G() * HD) {
+        if (tid() < GQ * HD) {
             const int h = tid() >> 7, d = tid() & (HD - 1);
             float M = -INFINITY;
             #pragma unroll 1
@@ -984,12 +987,20 @@ public:
             for (int s = 0; s < a.S_eff; s++) {
                 const float w = __expf(qw_sm.ml[s][h][0] - M);
                 Lt = fmaf(w, qw_sm.ml[s][h][1], Lt);
-                O = fmaf(w, s == 0 ? acc : stage[(s - 1) * (G() * HD) + tid()], O);
+                O = fmaf(w, s == 0 ? acc : stage[(s - 1) * (GQ * HD) + tid()], O);
             }
-            st_relaxed_u64(p.att + (size_t)(a.g * G() + h) * HD + d, tagged(O / Lt, tgB));
+            st_relaxed_u64(p.att + (size_t)(a.g * GQ + h) * HD + d, tagged(O / Lt, tgB));
         }
         stamp(step, l * TRACE_PER_LAYER + 13);
         named_bar_sync(1, NCT);  // the stage lives in part, which the next phase's GEMV overwrites
+    }
+
+    __device__ __noinline__ static void attention_consume(int step, int l, int pos) {
+        switch (G()) {
+            case 1: attention_g<1>(step, l, pos); break;
+            case 2: attention_g<2>(step, l, pos); break;
+            default: attention_g<3>(step, l, pos); break;
+        }
     }
 
     // ------------------------------------------------------------------ lm_head + argmax
