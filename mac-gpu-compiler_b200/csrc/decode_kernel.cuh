@@ -59,7 +59,8 @@ constexpr int MIN_CHUNK = 32;                 // fewest positions per attention 
 constexpr uint32_t LM_PREFETCH_BYTES = 256u * 1024;  // lm_head bytes per CTA warmed into L2 ahead of use
 constexpr int APART_STRIDE = HD + 4;          // words per attention partial: acc[128], m, l, pad
 constexpr int ATT_WST = HD + 4;               // floats per (warp, head) softmax state staged in part: acc[128], m, l, pad
-constexpr int GP = 4;                         // tagged word pairs a consumer thread polls at once
+constexpr int GP = 4;
+enum : int { EPI_PART = 0, EPI_STORE = 1, EPI_SILU = 2 };  // GEMV epilogues (see gemv_full_segments)                         // tagged word pairs a consumer thread polls at once
 constexpr uint32_t NONE_IDX = 0xFFFFFFFFu;
 // Math: the softmax / SiLU exponentials use __expf and the RMSNorm scales rsqrtf (hardware
 // approximations, ~1e-6 relative error): the inline IEEE expansions of expf and 1/sqrtf would
@@ -637,12 +638,21 @@ public:
 
     // The Qwen3-0.6B case of gemv_generic, with everything static: 1024-column segments (4 chunks of
     // 16 bytes per lane) and at most one unit per warp per piece.
-    __device__ __noinline__ static void gemv_full_segments(const GemvGeo& gs) {
+    //
+    // Epilogue EPI: EPI_PART leaves the row sums in part() for a later pass; EPI_STORE (segs == 1)
+    // has the lane holding a row's total store it at once, times the RMSNorm scale, as a tagged
+    // word out[row]; EPI_SILU (segs == 1, 12 rows per piece, interleaved gate/up rows) gives each
+    // warp whole (gate, up) row pairs - warp w takes pair w % 6 of pieces w / 6 and w / 6 + 2 of a
+    // group - and stores silu(gate) * up as out[row / 2]. The fused epilogues write their results
+    // before the phase's closing barrier, so the hand-off to other CTAs starts earlier.
+    template <int EPI>
+    __device__ __noinline__ static void gemv_full_segments(const GemvGeo& gs, u64* out, uint32_t tg) {
         uint32_t& it = ring_pos();
         const GemvGeo g = gs;
         const int w = warp(), ln = lane();
         const WarpGeo wgo = qw_sm.wgeo[&gs - qw_sm.geo][w];
         const int myseg = wgo.myseg, rl = wgo.rl;
+        const float sc = EPI == EPI_PART ? 1.f : norm_scale();
         float xr[32];
         {
             const float4* xp = reinterpret_cast<const float4*>(xs() + myseg * 1024) + ln;
@@ -668,10 +678,16 @@ public:
             if (ok) {
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
-                    const int r = g.r0 + (q0 + j) * g.rpp;
-                    if (j < n && w < min(g.rpp, g.r1 - r) * g.segs) {
-                        dst[j] = (r - g.r0 + rl) * g.segs + myseg;
-                        const uint4* wp = reinterpret_cast<const uint4*>(ring() + ((pc + j) % NSLOT) * SLOT_BYTES + woff);
+                    // unit j of this warp: EPI_SILU -> row 2 * (w % 6) + (j & 1) of piece w / 6 + (j & 2);
+                    // otherwise -> row rl of piece j
+                    const int pj = EPI == EPI_SILU ? w / 6 + (j & 2) : j;
+                    const int r = g.r0 + (q0 + pj) * g.rpp;
+                    const int rr = EPI == EPI_SILU ? 2 * (w % 6) + (j & 1) : rl;
+                    const bool have = EPI == EPI_SILU ? (pj < n && rr < g.r1 - r) : (j < n && w < min(g.rpp, g.r1 - r) * g.segs);
+                    if (have) {
+                        dst[j] = (r - g.r0 + rr) * g.segs + myseg;
+                        const uint4* wp = reinterpret_cast<const uint4*>(
+                            ring() + ((pc + pj) % NSLOT) * SLOT_BYTES + (EPI == EPI_SILU ? rr * 2048 + ln * 16 : woff));
                         uint4 wv[4];
 #pragma unroll
                         for (int i = 0; i < 4; i++) wv[i] = wp[i * 32];
@@ -700,7 +716,18 @@ public:
             if (jj == 1) d = dst[1];
             if (jj == 2) d = dst[2];
             if (jj == 3) d = dst[3];
-            if ((ln & 7) == 0 && d >= 0) prt[d] = t;
+            if (EPI == EPI_PART) {
+                if ((ln & 7) == 0 && d >= 0) prt[d] = t;
+            } else if (EPI == EPI_STORE) {
+                if ((ln & 7) == 0 && d >= 0) st_relaxed_u64(out + g.r0 + d, tagged(t * sc, tg));
+            } else {
+                // lanes 0 and 16 hold a gate row total, lanes 8 and 24 the matching up row total
+                const float up = __shfl_down_sync(0xFFFFFFFFu, t, 8);
+                if ((ln & 15) == 0 && d >= 0) {
+                    const float gt = t * sc, u = up * sc;
+                    st_relaxed_u64(out + (g.r0 + d) / 2, tagged(gt / (1.0f + __expf(-gt)) * u, tg));
+                }
+            }
         }
         it = pc;
         named_bar_sync(1, NCT);
@@ -710,9 +737,18 @@ public:
     }
 
     // one GEMV phase of the CTA; returns after a CTA-wide barrier (part() then holds every row's sums)
-    __device__ __forceinline__ static void gemv_consume(const GemvGeo& g) {
-        if (g.cpl == 4 && g.rpp * g.segs <= NCW) gemv_full_segments(g);
-        else gemv_generic(g);
+    // EPI_STORE and EPI_SILU write their outputs (out, tagged tg) themselves; EPI_PART leaves the
+    // row sums in part() for residual_rows / lm_epilogue
+    template <int EPI>
+    __device__ __forceinline__ static void gemv_consume(const GemvGeo& g, u64* out = nullptr, uint32_t tg = 0) {
+        const bool full = g.cpl == 4 && g.rpp * g.segs <= NCW && (EPI == EPI_PART || (g.segs == 1 && g.rpp == 12));
+        if (full) {
+            gemv_full_segments<EPI>(g, out, tg);
+        } else {
+            gemv_generic(g);
+            if (EPI == EPI_STORE) store_rows(out, g, tg);
+            if (EPI == EPI_SILU) silu_rows(tg);
+        }
     }
 
     __device__ __forceinline__ static float row_value(const GemvGeo& g, int rl) {
@@ -979,15 +1015,16 @@ public:
         named_bar_sync(1, NCT);
         if (tid() < GQ * HD) {
             const int h = tid() >> 7, d = tid() & (HD - 1);
-            float M = -INFINITY;
-            #pragma unroll 1
-            for (int s = 0; s < a.S_eff; s++) M = fmaxf(M, qw_sm.ml[s][h][0]);
-            float Lt = 0.f, O = 0.f;
-            #pragma unroll 1
-            for (int s = 0; s < a.S_eff; s++) {
+            float M = qw_sm.ml[0][h][0];
+#pragma unroll 4
+            for (int s = 1; s < a.S_eff; s++) M = fmaxf(M, qw_sm.ml[s][h][0]);
+            const float w0 = __expf(qw_sm.ml[0][h][0] - M);
+            float Lt = w0 * qw_sm.ml[0][h][1], O = w0 * acc;
+#pragma unroll 4
+            for (int s = 1; s < a.S_eff; s++) {
                 const float w = __expf(qw_sm.ml[s][h][0] - M);
                 Lt = fmaf(w, qw_sm.ml[s][h][1], Lt);
-                O = fmaf(w, s == 0 ? acc : stage[(s - 1) * (GQ * HD) + tid()], O);
+                O = fmaf(w, stage[(s - 1) * (GQ * HD) + tid()], O);
             }
             st_relaxed_u64(p.att + (size_t)(a.g * GQ + h) * HD + d, tagged(O / Lt, tgB));
         }
@@ -1132,24 +1169,22 @@ public:
         lstamp(0);
         norm_prologue(layer_norms(), cur_layer() == 0, ls().token, cur_layer() == 0 ? 0u : tag(seq(cur_step(), cur_layer() - 1, 5)));
         lstamp(1);
-        gemv_consume(gA());
-        store_rows(vprm().qkv, gA(), ltag(1));
+        gemv_consume<EPI_STORE>(gA(), vprm().qkv, ltag(1));
         lstamp(2);
         attention_consume(cur_step(), cur_layer(), vprm().start_pos + cur_step());
         lstamp(5);
         gather(vprm().att, QD(), ltag(2));
         lstamp(6);
-        gemv_consume(gC());
+        gemv_consume<EPI_PART>(gC());
         residual_rows(gC(), ltag(3));
         lstamp(7);
         norm_prologue(layer_norms() + vprm().H, false, 0, ltag(3));
         lstamp(8);
-        gemv_consume(gD());
-        silu_rows(ltag(4));
+        gemv_consume<EPI_SILU>(gD(), vprm().hbuf, ltag(4));
         lstamp(9);
         gather(vprm().hbuf, vprm().I, ltag(4));
         lstamp(10);
-        gemv_consume(gE());
+        gemv_consume<EPI_PART>(gE());
         residual_rows(gE(), ltag(5));
         lstamp(11);
     }
@@ -1169,7 +1204,7 @@ public:
             // F: final rmsnorm -> lm_head -> argmax partials -> end-of-token barrier -> next token
             norm_prologue(vprm().final_norm, false, 0, tag(seq(cur_step(), vprm().L - 1, 5)));
             tstamp(0);
-            gemv_consume(gF());
+            gemv_consume<EPI_PART>(gF());
             lm_epilogue();
             tstamp(1);
             token_barrier((uint32_t)cur_step() + 1);

@@ -51,7 +51,7 @@ gemv_kernel(const __grid_constant__ DecodeParams p, const uint16_t* w, const flo
     }
     for (int i = Decoder::tid(); i < cols; i += NCT) Decoder::xs()[xperm(i)] = x[i];
     named_bar_sync(1, NCT);
-    Decoder::gemv_consume(g);
+    Decoder::gemv_consume<EPI_PART>(g);
     for (int i = Decoder::tid(); i < g.r1 - g.r0; i += NCT) y[g.r0 + i] = Decoder::row_value(g, i);
 }
 
