@@ -19,8 +19,10 @@ Printed JSON (one line, rank 0):
                over the 128 positions of a launch / average launch time (CUDA events)
   cpu_baseline the CPU oracle (C++ restatement of cpu_inference.rs, all host threads) on a bounded
                sample of the same decode positions
-Multi-GPU (torchrun): every rank holds a weight replica and decodes its own independent sequence
-(prompt seed 1 + rank); no collective touches the decode path (weak scaling).
+Multi-GPU (torchrun): every rank holds a weight replica and decodes its own independent sequences
+(replicas.shard: one per rank for configs[0]/[1], prompt seed 1 + rank; `--config box` shards
+configs[4]'s 64 sequences); no collective touches the decode path (weak scaling), and `value` is
+all ranks' tokens over the slowest rank's device time.
 `--impl reference` times the reference's CPU engine (its C++ restatement; the Rust original cannot
 be built here) on the same config, rank 0 only.
 """
@@ -39,10 +41,13 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "mac-gpu-compiler_b200"))
 
 import randmodel  # noqa: E402
+import replicas  # noqa: E402
 
 CONFIGS = {
     "ai130": dict(prompt=130, decode=128, label="configs[0]: 130-id prompt token-by-token, then 128 greedy decode steps (pos 130..257)"),
     "long": dict(prompt=2048, decode=512, label="configs[1]: 2048-id prompt token-by-token, then 512 greedy decode steps (pos 2048..2559)"),
+    "box": dict(prompt=130, decode=128, sequences=64,
+                label="configs[4]: 64 independent sequences (130-id prompt + 128 greedy steps each) sharded over the GPUs"),
 }
 # reference's published decode tok/s for this metric and config: Metal engine, f32 KV cache, Apple M1
 # (metal_infrence_engine/README.md:22)
@@ -224,23 +229,31 @@ def main() -> None:
     path = randmodel.make_model("qwen3-0.6b", 0)
     model = ci.CudaModel.load_model(path, device=local)
     cfg = model.config
-    cache = ci.CudaKVCache(model, n_prompt + n_dec + 1)
-    ids = randmodel.prompt_ids(n_prompt, cfg.vocab_size, seed=1 + rank)
-    logits = None
-    for pos, tok in enumerate(ids):              # token-by-token prefill (untimed)
-        logits = model.forward(tok, pos, cache)
-    first = int(np.argmax(logits))
+    # this rank's independent sequences: one per rank (its own prompt seed), or a share of configs[4]'s 64
+    seqs = replicas.shard(c.get("sequences", world), world, rank)
+    caches, toks_dev, firsts = [], [], []
+    for sq in seqs:
+        cache = ci.CudaKVCache(model, n_prompt + n_dec + 1)
+        ids = randmodel.prompt_ids(n_prompt, cfg.vocab_size, seed=replicas.prompt_seed(sq))
+        logits = None
+        for pos, tok in enumerate(ids):              # token-by-token prefill (untimed)
+            logits = model.forward(tok, pos, cache)
+        first = int(np.argmax(logits))
+        t = torch.zeros(n_dec + 1, dtype=torch.int32, device=f"cuda:{local}")
+        t[0] = first
+        caches.append(cache)
+        toks_dev.append(t)
+        firsts.append(first)
     stream = torch.cuda.ExternalStream(model.stream)
-    toks = torch.zeros(n_dec + 1, dtype=torch.int32, device=f"cuda:{local}")
-    toks[0] = first
     torch.cuda.synchronize()
 
     def barrier():
         if pg is not None:
             pg.barrier()
 
-    def step():
-        model.decode_device(cache, toks.data_ptr(), n_prompt, n_dec, stream=model.stream)
+    def step():  # one greedy decode of n_dec tokens per sequence of this rank, one launch each
+        for cache, t in zip(caches, toks_dev):
+            model.decode_device(cache, t.data_ptr(), n_prompt, n_dec, stream=model.stream)
 
     for _ in range(args.warmup):
         step()
@@ -259,31 +272,33 @@ def main() -> None:
         torch.cuda.synchronize()
     model.sync()
     elapsed = t_start.elapsed_time(t_end) / 1e3
-    launch_ms = [a.elapsed_time(b) for a, b in evs]
+    launch_ms = [a.elapsed_time(b) / max(1, len(seqs)) for a, b in evs]
     barrier()
-    # max over ranks
-    el = torch.tensor([elapsed], dtype=torch.float64, device=f"cuda:{local}")
-    if pg is not None:
-        pg.all_reduce(el, op=pg.ReduceOp.MAX)
-    elapsed_max = float(el.item())
+    # every rank's (tokens, device seconds): whole-box tok/s = all tokens / the slowest rank's time
+    timings = replicas.reduce_timings(replicas.RankTiming(n_dec * args.steps * len(seqs), elapsed),
+                                      group=pg.group.WORLD if pg is not None else None)
+    box = replicas.aggregate(timings)
+    elapsed_max = box["seconds"]
 
-    # decode tokens must match the prefix invariant: the first decoded token is deterministic
-    out_tokens = toks.cpu().tolist()
+    out_tokens = toks_dev[0].cpu().tolist() if seqs else []
 
-    # e2e through the public host API (qw_decode: host first token in, tokens streamed to host)
-    e2e_times = []
-    for i in range(max(2, min(args.steps, 5)) + 1):
+    # e2e through the public host API (qw_decode: host first token in, every token streamed to the
+    # host callback), each sequence of this rank once per round, timed with events on the model stream
+    rounds = max(2, min(args.steps, 5))
+    e2e_sec = 0.0
+    for i in range(rounds + 1):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        got = model.decode(first, n_prompt, n_dec, cache)
+        for k, cache in enumerate(caches):
+            got = model.decode(firsts[k], n_prompt, n_dec, cache)
+            if k == 0:
+                assert got == out_tokens[1:], "host-API decode disagrees with the device-resident decode"
         b.record(stream)
         torch.cuda.synchronize()
         if i > 0:
-            e2e_times.append(a.elapsed_time(b) / 1e3)
-        assert got == out_tokens[1:], "host-API decode disagrees with the device-resident decode"
-    e2e_t = torch.tensor([statistics.mean(e2e_times)], dtype=torch.float64, device=f"cuda:{local}")
-    if pg is not None:
-        pg.all_reduce(e2e_t, op=pg.ReduceOp.MAX)
+            e2e_sec += a.elapsed_time(b) / 1e3
+    e2e_box = replicas.aggregate(replicas.reduce_timings(replicas.RankTiming(n_dec * rounds * len(seqs), e2e_sec),
+                                                         group=pg.group.WORLD if pg is not None else None))
 
     if rank == 0:
         W = model.weight_bytes_per_token()
@@ -291,29 +306,31 @@ def main() -> None:
         avg_launch = statistics.mean(launch_ms) / 1e3
         achieved = bytes_launch / avg_launch / 1e9
         peak, peak_kind = load_peaks()
-        value = n_dec * args.steps * world / elapsed_max
+        value = box["tok_per_s"]
         traffic = NCU_TRAFFIC_RATIO * bytes_launch
         line = {
             "metric": "Qwen3-0.6B bf16 decode tok/s @bs1 & % of HBM roofline; box tok/s at 1-8 GPUs",
             "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": elapsed_max / args.steps * 1e3, "ms_per_token": elapsed_max / args.steps / n_dec * 1e3,
+            "ms_per_step": elapsed_max / args.steps * 1e3,
+            "ms_per_token": elapsed_max / args.steps / n_dec / max(1, len(seqs)) * 1e3,
             "higher_is_better": True, "scaling": "weak",
             "vs_baseline": value / PUBLISHED_TPS if args.config == "ai130" else None,
             "vs_baseline_ref": "reference Metal engine, f32 KV, Apple M1: 46.37 tok/s (README.md:22)",
             "dtype": "bf16", "accumulate": "f32", "data": "synthetic",
             "config": {"workload": c["label"], "model": "Qwen3-0.6B geometry, random-init bf16 (seed 0)",
-                       "global_batch": world, "seq_len": n_prompt + n_dec,
-                       "parallelism": f"replicas x{world}, one independent sequence per GPU, no collective",
+                       "global_batch": box["tokens"] // (n_dec * args.steps), "seq_len": n_prompt + n_dec,
+                       "parallelism": f"replicas x{world}, independent sequences sharded over the GPUs "
+                                      f"({len(seqs)} on rank 0), no collective",
                        "l2": "inputs larger than L2: 1.19 GB of weights streamed per token",
-                       "step": f"one {n_dec}-token greedy decode = one decode-kernel launch"},
-            "e2e": {"value": n_dec * world / float(e2e_t.item()), "unit": "tok/s", "h2d_bytes_per_step": 4,
-                    "d2h_bytes_per_step": 4 * n_dec, "api": "qw_decode (host callback per token)"},
+                       "step": f"one {n_dec}-token greedy decode per sequence = one decode-kernel launch each"},
+            "e2e": {"value": e2e_box["tok_per_s"], "unit": "tok/s", "h2d_bytes_per_step": 4 * len(seqs),
+                    "d2h_bytes_per_step": 4 * n_dec * len(seqs), "api": "qw_decode (host callback per token)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": f"{peak_kind} (hbm_gbs, copy)", "traffic": traffic,
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of a 4-token launch, scaled by algorithmic bytes",
                          "algorithmic_bytes_per_launch": bytes_launch,
                          "kernel": "qw::decode_kernel", "avg_launch_ms": avg_launch * 1e3},
-            "gpu_launches": args.steps,
+            "gpu_launches": args.steps * len(seqs),
             "clocks": clocks.summary(),
             "first_tokens": out_tokens[1:9],
         }

@@ -1106,10 +1106,11 @@ public:
         for (int i = tid(); i < g.r1 - g.r0; i += NCT) st_relaxed_u64(dst + g.r0 + i, tagged(row_value(g, i) * sc, tg));
     }
 
-    __device__ __noinline__ static void residual_rows(const GemvGeo& g, uint32_t tg) {  // x[r] += y[r] on this CTA's rows
+    // x[r] += y[r] on this CTA's rows (cpu_inference.rs:163-164, :171-172)
+    __device__ __noinline__ static void residual_rows(const GemvGeo& g, uint32_t tg) {
+        const DecodeParams& p = qw_sm.prm;
         #pragma unroll 1
         for (int i = tid(); i < g.r1 - g.r0; i += NCT) {
-        const DecodeParams& p = qw_sm.prm;
             const float v = xloc()[i] + row_value(g, i);
             xloc()[i] = v;
             st_relaxed_u64(p.x + g.r0 + i, tagged(v, tg));
