@@ -297,19 +297,20 @@ uint64_t ModelFile::weight_bytes_per_token() const {
 }
 
 int check_supported(const ModelConfig& c, std::string& msg) {
-    // a GEMV width is supported when some segment width in {256, 512, 768, 1024} divides it into a
-    // number of segments that divides the decode kernel's 12 consumer warps
+    // a GEMV width K is supported when it is a multiple of 256 and at most 1024 (one segment), or a
+    // multiple of 1024 whose 1024-column segment count divides the decode kernel's 12 consumer
+    // warps (seg_count in decode_kernel.cuh)
     auto seg_ok = [](uint64_t K) {
-        for (uint64_t segw = 256; segw <= 1024; segw += 256)
-            if (K % segw == 0 && 12 % (K / segw) == 0) return true;
-        return false;
+        if (K == 0 || K % 256 != 0) return false;
+        if (K <= 1024) return true;
+        return K % 1024 == 0 && 12 % (K / 1024) == 0;
     };
     if (c.layers == 0 || c.vocab == 0 || c.heads == 0 || c.kv_heads == 0) { msg = "config: zero-sized dimension"; return QW_ERR_FORMAT; }
     if (c.head_dim != 128) { msg = "unsupported head_dim (the kernels fix it at 128, like inference.metal's attention)"; return QW_ERR_UNSUPPORTED; }
     if (c.heads % c.kv_heads != 0) { msg = "num_attention_heads must be a multiple of num_key_value_heads"; return QW_ERR_UNSUPPORTED; }
     if (c.heads / c.kv_heads > 3) { msg = "more than 3 query heads per KV head is not supported"; return QW_ERR_UNSUPPORTED; }
     if (!seg_ok(c.hidden) || !seg_ok(c.inter) || !seg_ok(c.heads * c.head_dim)) {
-        msg = "hidden_size, intermediate_size and heads*head_dim must split into 1, 2, 3, 4, 6 or 12 segments of 256-1024 columns";
+        msg = "hidden_size, intermediate_size and heads*head_dim must be multiples of 256 up to 1024, or split into 1, 2, 3, 4, 6 or 12 segments of 1024 columns";
         return QW_ERR_UNSUPPORTED;
     }
     if (c.vocab >= (1ull << 31)) { msg = "vocab_size too large"; return QW_ERR_UNSUPPORTED; }

@@ -118,3 +118,21 @@ def test_standalone_kernels_reject_bad_arguments():
     with pytest.raises(ci.QwError):
         ci.argmax_f32(0, 0, 10, 0, 0)
     assert ci.argmax_workspace_size(151936) >= 256
+
+
+def test_inspect_rejects_widths_the_kernel_cannot_segment(tmp_path):
+    # intermediate 1536 is a multiple of 256 but neither <= 1024 nor a whole number of 1024-column
+    # segments: the GEMV segmentation cannot split it, so the loader must refuse it up front
+    import randmodel
+    d = tmp_path / "odd"
+    d.mkdir()
+    st = d / "model.safetensors"
+    g = dict(randmodel.GEOMETRIES["tiny"], intermediate_size=1536, num_hidden_layers=1)
+    rc = randmodel._lib().rm_write_model(str(st).encode(), g["hidden_size"], g["intermediate_size"],
+                                         g["num_hidden_layers"], g["num_attention_heads"],
+                                         g["num_key_value_heads"], g["head_dim"], g["vocab_size"], 0, 0)
+    assert rc == 0
+    cfg = randmodel.config_dict("tiny")
+    cfg.update(intermediate_size=1536, num_hidden_layers=1)
+    (d / "config.json").write_text(json.dumps(cfg))
+    assert _code(st) == ci.QW_ERR_UNSUPPORTED
