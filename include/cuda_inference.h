@@ -147,6 +147,14 @@ int qw_argmax_f32(int device, const float* d_x, size_t n, uint32_t* d_out, void*
 #define QW_ARGMAX_NOALLOC_MAX_N 4294967295ull
 int qw_argmax_f32_noalloc(int device, const float* d_x, size_t n, uint32_t* d_out, void* stream);
 
+/* The batched prefill's tensor-core GEMM (tcgen05, TMA tiles): d_y[M][N] (f32) =
+ * (d_a_hi + d_a_lo)[M][K] . d_b[N][K]^T, where d_a_hi / d_a_lo are the bf16 high and low halves of
+ * f32 activations and d_b a bf16 weight matrix [out][in] as stored (matvec_bf16's operand,
+ * src/shaders/inference.metal:143-186, for many tokens at once). K must be a multiple of 64 and
+ * every pointer 16-byte aligned. Synchronous: returns after the product is in d_y. */
+int qw_gemm_bf16x2(int device, const uint16_t* d_a_hi, const uint16_t* d_a_lo, const uint16_t* d_b, float* d_y, size_t M,
+                   size_t N, size_t K, void* stream);
+
 /* Streaming-read probe (tests/read_bandwidth.rs:16-54): sums n_floats floats (n_floats % 4 == 0,
  * d_src 16-byte aligned) into per-CTA partials d_partials[0 .. n_partials). Returns the number
  * of partials written through *n_written. */

@@ -34,7 +34,7 @@ def _stale(out: Path, deps: list[Path]) -> bool:
 
 def build_engine(force: bool = False, verbose: bool = False) -> Path:
     out = HERE / "libcuda_inference.so"
-    srcs = [CSRC / "engine.cu", CSRC / "micro_kernels.cu", CSRC / "model_file.cpp"]
+    srcs = [CSRC / "engine.cu", CSRC / "micro_kernels.cu", CSRC / "prefill.cu", CSRC / "model_file.cpp"]
     deps = srcs + list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + [ROOT / "include" / "cuda_inference.h"]
     if not force and not _stale(out, deps):
         return out

@@ -1,0 +1,237 @@
+// tcgen05 tensor-core GEMM for the batched prefill (sm_100a):
+//
+//   Y[M x N] (f32) = (A_hi + A_lo)[M x K] . B[N x K]^T
+//
+// A holds f32 activations split into two bf16 halves (A_hi = bf16(a), A_lo = bf16(a - A_hi)), so
+// that the product keeps ~16 bits of each activation's mantissa against bf16 weights: the two
+// halves accumulate into the same f32 accumulator. B is a weight matrix as stored ([out][in],
+// row-major, bf16). Both operands are K-major, which is the nn.Linear layout.
+//
+// One CTA computes one BM x BN tile (BM = 128 rows, BN = 128 columns) with 4 warps:
+//   * warp 0, one lane: TMA producer. Per K block of 64 it loads the A_hi, A_lo and B tiles with
+//     2-D tiled bulk tensor copies (cp.async.bulk.tensor, 128-byte swizzle, no multicast) into a
+//     STAGES-deep shared-memory ring, signalling a full mbarrier with the byte count;
+//   * warp 1, one lane: MMA issuer. Per K block it issues 4 K-steps x 2 halves of
+//     tcgen05.mma.cta_group::1.kind::f16 (M=128, N=128, K=16, bf16 x bf16 -> f32) accumulating in
+//     tensor memory, then tcgen05.commit to the stage's empty mbarrier so the producer may refill
+//     it; after the last block a final commit signals the epilogue;
+//   * all 4 warps: epilogue. Warp w reads TMEM lanes 32w..32w+31 (its 32 rows) with
+//     tcgen05.ld.32x32b and stores the f32 rows.
+// TMEM: 128 columns (the accumulator) allocated by warp 1 and freed by it at the end.
+//
+// Every wait is bounded: a wait that runs out sets `err` (the kernel's error word) and the CTA
+// skips the remaining work, still waiting (bounded) for the copies and MMAs it issued and freeing
+// its tensor memory before it exits.
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "ptx.cuh"
+
+namespace qw {
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BN = 128;
+constexpr int BK = 64;                       // bf16 elements per 128-byte swizzle row
+constexpr int STAGES = 4;
+constexpr int TILE_A = BM * BK * 2;          // bytes of one A half tile (16 KB)
+constexpr int TILE_B = BN * BK * 2;          // bytes of one B tile (16 KB)
+constexpr int STAGE_BYTES = 2 * TILE_A + TILE_B;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack for the 1024-byte swizzle atoms
+constexpr int THREADS = 128;
+constexpr int TMEM_COLS = BN;                // f32 accumulator columns
+constexpr long long WAIT_LIMIT_NS = 2000000000ll;
+
+// UMMA shared-memory descriptor of a K-major operand tile written by TMA with 128-byte swizzle:
+// rows of 128 bytes, 8-row groups 1024 bytes apart (stride byte offset), version 1 (sm_100),
+// layout type 2 (SWIZZLE_128B). Addresses and offsets are in 16-byte units.
+__device__ __forceinline__ uint64_t smem_desc_k128(uint32_t smem_addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);         // start address
+    d |= (uint64_t)1u << 16;                              // leading byte offset (unused for swizzled K-major)
+    d |= (uint64_t)(1024u >> 4) << 32;                    // stride byte offset: next 8-row group
+    d |= (uint64_t)1u << 46;                              // descriptor version (sm_100)
+    d |= (uint64_t)2u << 61;                              // SWIZZLE_128B
+    return d;
+}
+
+// instruction descriptor of kind::f16 with bf16 A and B, f32 accumulate, both K-major, M x N
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
+    return (1u << 4)                   // D format: f32
+         | (1u << 7)                   // A format: bf16
+         | (1u << 10)                  // B format: bf16
+         | ((uint32_t)(n >> 3) << 17)  // N / 8
+         | ((uint32_t)(m >> 4) << 24); // M / 16
+}
+
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int c0, int c1, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+        ::"r"(smem_u32(smem_dst)), "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        ::"r"(tmem_d), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// bounded wait on an mbarrier phase; false when it ran out (or another thread gave up)
+__device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t spins = 0;
+    while (!mbar_try_wait(bar, parity)) {
+        if ((++spins & 63) == 0) {
+            if (*abort_flag) return false;
+            if (globaltimer_ns() - t0 > (uint64_t)WAIT_LIMIT_NS) {
+                *abort_flag = 1;
+                return false;
+            }
+        }
+    }
+    return true;
+}
+
+struct GemmArgs {
+    float* y;          // [M][ldy] f32 output
+    int M, N, K;
+    int ldy;
+    int* err;          // kernel error word (nonzero: a wait ran out)
+};
+
+__global__ void __launch_bounds__(THREADS, 1)
+gemm_bf16x2_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
+                   const __grid_constant__ CUtensorMap map_b, const GemmArgs args) {
+    extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
+    __shared__ uint64_t full[STAGES], empty[STAGES], done;
+    __shared__ uint32_t tmem_base;
+    __shared__ volatile int abort_flag;
+    // 1024-byte aligned ring (the 128-byte swizzle atom spans 8 rows x 128 bytes)
+    uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int nkb = args.K / BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&done, 1);
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {  // one warp allocates the accumulator's tensor-memory columns
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32(&tmem_base)), "r"((uint32_t)TMEM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_base;
+    const uint32_t idesc = idesc_bf16_f32(BM, BN);
+    int issued_kb = 0;   // producer: K blocks whose copies were issued
+
+    if (warp == 0 && lane == 0) {
+        for (int kb = 0; kb < nkb; kb++) {
+            const int s = kb % STAGES;
+            if (kb >= STAGES && !bounded_wait(&empty[s], ((kb / STAGES) - 1) & 1, &abort_flag)) break;
+            uint8_t* st = ring + s * STAGE_BYTES;
+            mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+            tma_load_2d(st, &map_ahi, kb * BK, m0, &full[s]);
+            tma_load_2d(st + TILE_A, &map_alo, kb * BK, m0, &full[s]);
+            tma_load_2d(st + 2 * TILE_A, &map_b, kb * BK, n0, &full[s]);
+            issued_kb = kb + 1;
+        }
+    } else if (warp == 1 && lane == 0) {
+        for (int kb = 0; kb < nkb; kb++) {
+            const int s = kb % STAGES;
+            if (!bounded_wait(&full[s], (kb / STAGES) & 1, &abort_flag)) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t st = smem_u32(ring + s * STAGE_BYTES);
+            const uint64_t dhi = smem_desc_k128(st), dlo = smem_desc_k128(st + TILE_A), db = smem_desc_k128(st + 2 * TILE_A);
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; kk++) {
+                // a K step of 16 bf16 is 32 bytes along the swizzled row: +2 in 16-byte units
+                mma_bf16(tmem, dhi + 2 * kk, db + 2 * kk, idesc, (kb | kk) != 0);
+                mma_bf16(tmem, dlo + 2 * kk, db + 2 * kk, idesc, 1u);
+            }
+            mma_commit(&empty[s]);  // the stage may be refilled once these MMAs have read it
+        }
+        mma_commit(&done);          // arrives when every MMA issued above has completed
+    }
+    __syncwarp();
+    // epilogue: wait for the accumulator (bounded), then TMEM -> registers -> global
+    const bool ok = bounded_wait(&done, 0, &abort_flag) && !abort_flag;
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (ok) {
+        const int row = m0 + warp * 32 + lane;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+            uint32_t r[32];
+            tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, r);
+            if (row < args.M && n0 + c < args.N) {
+                float* dst = args.y + (size_t)row * args.ldy + n0 + c;
+                const int nv = args.N - (n0 + c) < 32 ? args.N - (n0 + c) : 32;
+                if (nv == 32) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4)
+                        *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
+                                                                          __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+                } else {
+                    for (int j = 0; j < nv; j++) dst[j] = __uint_as_float(r[j]);
+                }
+            }
+        }
+    }
+    if (!ok && threadIdx.x == 0) atomicExch(args.err, 1);
+    // after an abort, the TMA copies still in flight must land before the CTA exits
+    if (!ok && warp == 0 && lane == 0) {
+        for (int kb = issued_kb - STAGES > 0 ? issued_kb - STAGES : 0; kb < issued_kb; kb++) {
+            const uint64_t t0 = globaltimer_ns();
+            while (!mbar_try_wait(&full[kb % STAGES], (kb / STAGES) & 1))
+                if (globaltimer_ns() - t0 > (uint64_t)WAIT_LIMIT_NS) break;
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        // the MMAs issued before an abort must finish before their accumulator columns are freed:
+        // the final commit arrives on `done` once they have (bounded wait, whatever abort_flag says)
+        if (!ok && lane == 0) {
+            const uint64_t t0 = globaltimer_ns();
+            while (!mbar_try_wait(&done, 0))
+                if (globaltimer_ns() - t0 > (uint64_t)WAIT_LIMIT_NS) break;
+        }
+        __syncwarp();
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)TMEM_COLS) : "memory");
+    }
+}
+
+}  // namespace tc
+}  // namespace qw

@@ -100,6 +100,7 @@ def lib() -> ctypes.CDLL:
             "qw_argmax_f32": (i32, [i32, vp, sz, vp, vp, vp]),
             "qw_argmax_f32_noalloc": (i32, [i32, vp, sz, vp, vp]),
             "qw_read_probe": (i32, [i32, vp, sz, vp, sz, ctypes.POINTER(sz), vp]),
+            "qw_gemm_bf16x2": (i32, [i32, vp, vp, vp, vp, sz, sz, sz, vp]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -242,6 +243,12 @@ def argmax_f32(device: int, d_x: int, n: int, d_out: int, d_workspace: int, stre
 def argmax_f32_noalloc(device: int, d_x: int, n: int, d_out: int, stream: int = 0) -> None:
     """argmax_f32 without a caller workspace (see qw_argmax_f32_noalloc in the header)."""
     _check(lib().qw_argmax_f32_noalloc(device, d_x, n, d_out, stream or None))
+
+
+def gemm_bf16x2(device: int, d_a_hi: int, d_a_lo: int, d_b: int, d_y: int, M: int, N: int, K: int,
+                stream: int = 0) -> None:
+    """d_y[M][N] = (a_hi + a_lo)[M][K] . b[N][K]^T on the tensor cores (see qw_gemm_bf16x2)."""
+    _check(lib().qw_gemm_bf16x2(device, d_a_hi, d_a_lo, d_b, d_y, M, N, K, stream or None))
 
 
 def read_probe(device: int, d_src: int, n_floats: int, d_partials: int, n_partials: int, stream: int = 0) -> int:
