@@ -82,6 +82,14 @@ size_t qw_cache_max_seq(const qw_cache* cache); /* MetalKVCache::max_seq (metal_
  * cache, copy vocab_size f32 logits to `logits_out` (host). Synchronous. */
 int qw_forward(qw_model* model, qw_cache* cache, uint32_t token, size_t pos, float* logits_out);
 
+/* Batched prefill (the reference feeds a prompt token by token through
+ * forward, metal_inference.rs:286-291, src/bin/bench.rs:166-191): one pass over ids[0..n) at
+ * positions start_pos .. start_pos+n-1 whose projections run as tcgen05 tensor-core GEMMs over all
+ * n tokens. Writes their K/V into the cache exactly where n forward calls would; with logits_out
+ * (host, n * vocab_size floats, row t = position start_pos + t) also every position's logits.
+ * Synchronous. */
+int qw_prefill(qw_model* model, qw_cache* cache, const uint32_t* ids, size_t n, size_t start_pos, float* logits_out);
+
 /* MetalModel::decode (metal_inference.rs:297-316): greedy decode; `first` goes in at `start_pos`,
  * each step's argmax feeds the next, and on_token(user, t) is called with each step's output
  * token as soon as the GPU produces it (steps calls). The whole run is one kernel launch. */

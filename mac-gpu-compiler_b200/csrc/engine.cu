@@ -22,6 +22,7 @@
 #include "../../include/cuda_inference.h"
 #include "decode_kernel.cuh"
 #include "model_file.h"
+#include "prefill.h"
 
 using namespace qw;
 
@@ -145,6 +146,11 @@ struct qw_model {
     size_t h_cap = 0;
     uint32_t* h_stage = nullptr; // pinned, 1 token
     float* h_logits = nullptr;   // pinned [vocab]
+    // batched prefill: scratch for up to pf.cap tokens, their ids and (when asked for) logits
+    qw::pf::Scratch pf;
+    uint32_t* d_pf_ids = nullptr;
+    float* d_pf_logits = nullptr;
+    size_t pf_logits_cap = 0;    // tokens d_pf_logits holds
     unsigned epoch = 0;
     int S = 0, part_cap = 0, xs_cap = 0, xloc_cap = 0;
     u64* d_trace = nullptr;      // phase timeline of the most recent launch's first step, if enabled
@@ -429,6 +435,14 @@ void qw_free(qw_model* m) {
     cudaFree(m->d_scratch);
     cudaFree(m->d_tok);
     cudaFree(m->d_trace);
+    cudaFree(m->pf.X);
+    cudaFree(m->pf.Y);
+    cudaFree(m->pf.Q);
+    cudaFree(m->pf.att);
+    cudaFree(m->pf.ahi);
+    cudaFree(m->pf.alo);
+    cudaFree(m->d_pf_ids);
+    cudaFree(m->d_pf_logits);
     if (m->h_tok) cudaFreeHost(m->h_tok);
     if (m->h_stage) cudaFreeHost(m->h_stage);
     if (m->h_logits) cudaFreeHost(m->h_logits);
@@ -530,6 +544,72 @@ void qw_cache_free(qw_cache* c) {
 }
 
 size_t qw_cache_max_seq(const qw_cache* c) { return c ? c->max_seq : 0; }
+
+namespace {
+
+// grow the prefill scratch to hold n tokens (and, with logits, n rows of logits)
+int ensure_prefill(qw_model* m, size_t n, bool logits) {
+    const ModelConfig& c = m->cfg;
+    const size_t H = c.hidden, I = c.inter, QD = c.heads * c.head_dim, KVD = c.kv_heads * c.head_dim;
+    const size_t QKVR = QD + 2 * KVD;
+    if ((int)n > m->pf.cap) {
+        const size_t cap = std::max<size_t>(n, 2 * (size_t)m->pf.cap);
+        qw::pf::Scratch sc;
+        const size_t ycols = std::max({QKVR, 2 * I, H}), acols = std::max({H, QD, I});
+        bool ok = cudaMalloc(&sc.X, cap * H * 4) == cudaSuccess && cudaMalloc(&sc.Y, cap * ycols * 4) == cudaSuccess &&
+                  cudaMalloc(&sc.Q, cap * QD * 4) == cudaSuccess && cudaMalloc(&sc.att, cap * QD * 4) == cudaSuccess &&
+                  cudaMalloc(&sc.ahi, cap * acols * 2) == cudaSuccess && cudaMalloc(&sc.alo, cap * acols * 2) == cudaSuccess;
+        uint32_t* ids = nullptr;
+        ok = ok && cudaMalloc(&ids, cap * 4) == cudaSuccess;
+        if (!ok) {
+            cudaFree(sc.X); cudaFree(sc.Y); cudaFree(sc.Q); cudaFree(sc.att); cudaFree(sc.ahi); cudaFree(sc.alo); cudaFree(ids);
+            return set_err(QW_ERR_NOMEM, "prefill scratch allocation failed");
+        }
+        cudaFree(m->pf.X); cudaFree(m->pf.Y); cudaFree(m->pf.Q); cudaFree(m->pf.att); cudaFree(m->pf.ahi); cudaFree(m->pf.alo);
+        cudaFree(m->d_pf_ids);
+        sc.cap = (int)cap;
+        m->pf = sc;
+        m->d_pf_ids = ids;
+    }
+    if (logits && n > m->pf_logits_cap) {
+        float* d = nullptr;
+        if (cudaMalloc(&d, n * c.vocab * 4) != cudaSuccess) return set_err(QW_ERR_NOMEM, "prefill logits allocation failed");
+        cudaFree(m->d_pf_logits);
+        m->d_pf_logits = d;
+        m->pf_logits_cap = n;
+    }
+    return QW_OK;
+}
+
+}  // namespace
+
+int qw_prefill(qw_model* m, qw_cache* c, const uint32_t* ids, size_t n, size_t start_pos, float* logits_out) {
+    if (!m || !c || !ids || c->m != m || c->model_id != m->id) return set_err(QW_ERR_ARG, "null or mismatched handle");
+    if (n == 0) return QW_OK;
+    if (n > (1u << 20) || start_pos + n > c->max_seq) return set_err(QW_ERR_ARG, "start_pos + n exceeds the KV cache size");
+    for (size_t i = 0; i < n; i++)
+        if (ids[i] >= m->cfg.vocab) return set_err(QW_ERR_ARG, "token id >= vocab_size");
+    QW_CUDA(cudaSetDevice(m->device));
+    if (int e = ensure_prefill(m, n, logits_out != nullptr)) return e;
+    int* ew = qw::device_err_word_for(m->device);
+    if (!ew) return set_err(QW_ERR_NOMEM, "error word allocation failed");
+    QW_CUDA(cudaMemsetAsync(ew, 0, sizeof(int), m->stream));
+    QW_CUDA(cudaMemcpyAsync(m->d_pf_ids, ids, n * 4, cudaMemcpyHostToDevice, m->stream));
+    const ModelConfig& cf = m->cfg;
+    qw::pf::Weights w{m->d_layer_w, m->d_layer_n, m->d_final_norm, m->d_embed, m->d_lm_head, m->layer_stride, m->norm_stride,
+                      (int)cf.hidden, (int)cf.inter, (int)cf.layers, (int)cf.heads, (int)cf.kv_heads, (int)cf.vocab, cf.eps};
+    qw::pf::CacheView cv{c->d_k, c->d_v, c->d_rope, (int)c->max_seq};
+    std::string err;
+    if (int e = qw::pf::run(w, cv, m->d_pf_ids, (int)n, (int)start_pos, logits_out ? m->d_pf_logits : nullptr, m->pf, ew,
+                            m->stream, err))
+        return set_err(e, err);
+    if (logits_out) QW_CUDA(cudaMemcpyAsync(logits_out, m->d_pf_logits, n * cf.vocab * 4, cudaMemcpyDeviceToHost, m->stream));
+    int h = 0;
+    QW_CUDA(cudaMemcpyAsync(&h, ew, sizeof(int), cudaMemcpyDeviceToHost, m->stream));
+    QW_CUDA(cudaStreamSynchronize(m->stream));
+    if (h) return set_err(QW_ERR_DEVICE_TIMEOUT, "prefill: a GEMM pipeline wait expired on the device");
+    return QW_OK;
+}
 
 int qw_forward(qw_model* m, qw_cache* c, uint32_t token, size_t pos, float* logits_out) {
     if (!m || !c || !logits_out || c->m != m || c->model_id != m->id) return set_err(QW_ERR_ARG, "null or mismatched handle");

@@ -1,13 +1,16 @@
 // Batched prefill: the tcgen05 GEMM's host side (tensor maps, launch) and
 // the standalone entry point qw_gemm_bf16x2 (see tc_gemm.cuh for the kernel).
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <string>
 
 #include "../../include/cuda_inference.h"
+#include "prefill.h"
 #include "tc_gemm.cuh"
 
 namespace qw {
@@ -96,6 +99,234 @@ int gemm(const uint16_t* a_hi, const uint16_t* a_lo, int lda, const uint16_t* b,
 }
 
 }  // namespace tc
+
+// ---------------------------------------------------------------------------------------------
+// The prefill pipeline: one forward pass over n prompt tokens at positions start .. start+n-1
+// (the reference feeds them one at a time, cpu_inference.rs:100-179; here every projection is
+// one tensor-core GEMM over all n tokens). Residual stream X [n][H] f32; GEMM inputs are the
+// bf16 hi/lo halves of f32 activations (see tc_gemm.cuh).
+namespace pf {
+
+constexpr int ROW_THREADS = 256;
+
+__device__ __forceinline__ float bf16f(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+
+__device__ __forceinline__ void split_store(float v, uint16_t* hi, uint16_t* lo, size_t i) {
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    hi[i] = __bfloat16_as_ushort(h);
+    lo[i] = __bfloat16_as_ushort(__float2bfloat16_rn(v - __bfloat162float(h)));
+}
+
+// X[t] = f32(embed[ids[t]]) (cpu_inference.rs:109-111)
+__global__ void embed_rows(const uint32_t* ids, int H, const uint16_t* embed, float* X) {
+    const int t = blockIdx.x;
+    const uint16_t* e = embed + (size_t)ids[t] * H;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) X[(size_t)t * H + i] = bf16f(e[i]);
+}
+
+__device__ float block_sum256(float v, float* red) {
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = 0.f;
+    for (int w = 0; w < ROW_THREADS / 32; w++) t += red[w];
+    __syncthreads();
+    return t;
+}
+
+// A_hi/A_lo[t] = split(rmsnorm(X[t]) * gain) (cpu_inference.rs:189-194)
+__global__ void __launch_bounds__(ROW_THREADS) norm_split(const float* X, int H, const uint16_t* gain, float eps, uint16_t* hi,
+                                                          uint16_t* lo) {
+    __shared__ float red[ROW_THREADS / 32];
+    const int t = blockIdx.x;
+    const float* x = X + (size_t)t * H;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < H; i += ROW_THREADS) ss = fmaf(x[i], x[i], ss);
+    const float sc = rsqrtf(block_sum256(ss, red) / (float)H + eps);
+    for (int i = threadIdx.x; i < H; i += ROW_THREADS) split_store(x[i] * sc * bf16f(gain[i]), hi, lo, (size_t)t * H + i);
+}
+
+// A_hi/A_lo = split(src) over n rows of K
+__global__ void split_rows(const float* src, size_t total, uint16_t* hi, uint16_t* lo) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x)
+        split_store(src[i], hi, lo, i);
+}
+
+// X += Y (cpu_inference.rs:163-164, :171-172)
+__global__ void residual_add(float* X, const float* Y, size_t total) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x)
+        X[i] += Y[i];
+}
+
+// h[t][i] = silu(gate) * up from the interleaved gate/up outputs Y[t][2i], Y[t][2i+1], split for
+// the down GEMM (cpu_inference.rs:166-170, :187)
+__global__ void silu_split(const float* Y, size_t n_inter, uint16_t* hi, uint16_t* lo) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_inter; i += (size_t)gridDim.x * blockDim.x) {
+        const float g = Y[2 * i], u = Y[2 * i + 1];
+        split_store(g / (1.0f + __expf(-g)) * u, hi, lo, i);
+    }
+}
+
+// Per token and head of the q|k|v outputs Y[t][QKVR]: q heads get q_norm + RoPE into Q[t][NQ*128];
+// k heads k_norm + RoPE and v heads as they are go into the cache at position start + t
+// (cpu_inference.rs:134-141, :196-215; the RoPE table is the decode path's). One warp per head.
+__global__ void qkv_post(const float* Y, int n, int start, int NQ, int NKV, const uint16_t* qn, const uint16_t* kn, float eps,
+                         const float2* rope, float* Q, float* Kc, float* Vc, size_t head_stride_l, int max_seq) {
+    const int warps = blockDim.x >> 5;
+    const int item = blockIdx.x * warps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    const int per_tok = NQ + 2 * NKV;
+    if (item >= n * per_tok) return;
+    const int t = item / per_tok, hh = item - t * per_tok, pos = start + t;
+    const int QKVR = per_tok * 128;
+    const float4 v = reinterpret_cast<const float4*>(Y + (size_t)t * QKVR + (size_t)hh * 128)[lane];
+    if (hh >= NQ + NKV) {  // v head: straight into the cache
+        const int g = hh - NQ - NKV;
+        reinterpret_cast<float4*>(Vc + head_stride_l + ((size_t)g * max_seq + pos) * 128)[lane] = v;
+        return;
+    }
+    const uint16_t* gw = hh < NQ ? qn : kn;
+    float ss = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    const float s = rsqrtf(ss / 128.0f + eps);
+    const int d0 = lane * 4;
+    float e[4] = {v.x, v.y, v.z, v.w}, o4[4];
+    for (int j = 0; j < 4; j++) e[j] = e[j] * s * bf16f(gw[d0 + j]);
+    const float2* rr = rope + (size_t)pos * 64;
+    for (int j = 0; j < 4; j++) {
+        const float other = __shfl_xor_sync(0xFFFFFFFFu, e[j], 16);  // element d +- 64
+        const float2 cs = rr[(d0 + j) & 63];
+        o4[j] = lane < 16 ? e[j] * cs.x - other * cs.y : e[j] * cs.x + other * cs.y;
+    }
+    const float4 out = make_float4(o4[0], o4[1], o4[2], o4[3]);
+    if (hh < NQ) reinterpret_cast<float4*>(Q + (size_t)t * NQ * 128 + (size_t)hh * 128)[lane] = out;
+    else reinterpret_cast<float4*>(Kc + head_stride_l + ((size_t)(hh - NQ) * max_seq + pos) * 128)[lane] = out;
+}
+
+constexpr int ATT_TOK = 8;    // tokens per attention CTA (one warp each)
+constexpr int ATT_CHUNK = 32; // cached positions staged in shared memory at a time
+
+// Causal GQA attention for the prefill: CTA (token tile, kv head g), warp w = token t0 + w with its
+// G query heads; every warp runs the same online softmax as the decode kernel over positions
+// 0 .. start + t, reading the K/V rows the CTA stages in shared memory (cpu_inference.rs:143-161).
+template <int G>
+__global__ void __launch_bounds__(ATT_TOK * 32) attention(const float* Q, float* att, const float* Kc, const float* Vc, int n,
+                                                          int start, int NQ, size_t head_stride_l, int max_seq, float scale) {
+    __shared__ __align__(16) float Ks[ATT_CHUNK][128];
+    __shared__ __align__(16) float Vs[ATT_CHUNK][128];
+    const int g = blockIdx.y, t0 = blockIdx.x * ATT_TOK;
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = t0 + w;
+    const bool valid = t < n;
+    const int pos = start + t;
+    const int last = start + min(n, t0 + ATT_TOK) - 1;
+    float4 q4[G];
+    float m[G], l[G];
+    float4 acc[G];
+    for (int h = 0; h < G; h++) {
+        q4[h] = valid ? reinterpret_cast<const float4*>(Q + (size_t)t * NQ * 128 + (size_t)(g * G + h) * 128)[lane]
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+        m[h] = -INFINITY;
+        l[h] = 0.f;
+        acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    const float* kb = Kc + head_stride_l + (size_t)g * max_seq * 128;
+    const float* vb = Vc + head_stride_l + (size_t)g * max_seq * 128;
+    for (int p0 = 0; p0 <= last; p0 += ATT_CHUNK) {
+        const int np = min(ATT_CHUNK, last + 1 - p0);
+        __syncthreads();
+        for (int i = threadIdx.x; i < np * 32; i += blockDim.x) {
+            const int r = i >> 5, c = i & 31;
+            reinterpret_cast<float4*>(Ks[r])[c] = reinterpret_cast<const float4*>(kb + (size_t)(p0 + r) * 128)[c];
+            reinterpret_cast<float4*>(Vs[r])[c] = reinterpret_cast<const float4*>(vb + (size_t)(p0 + r) * 128)[c];
+        }
+        __syncthreads();
+        if (!valid) continue;
+        const int myn = min(np, pos + 1 - p0);  // positions of this chunk this token attends to
+        for (int pp = 0; pp < myn; pp++) {
+            const float4 k4 = reinterpret_cast<const float4*>(Ks[pp])[lane];
+            const float4 v4 = reinterpret_cast<const float4*>(Vs[pp])[lane];
+            float sc[G];
+#pragma unroll
+            for (int h = 0; h < G; h++) sc[h] = q4[h].x * k4.x + q4[h].y * k4.y + q4[h].z * k4.z + q4[h].w * k4.w;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (int h = 0; h < G; h++) sc[h] += __shfl_xor_sync(0xFFFFFFFFu, sc[h], o);
+#pragma unroll
+            for (int h = 0; h < G; h++) {
+                const float a = sc[h] * scale;
+                const float mn = fmaxf(m[h], a);
+                const float corr = __expf(m[h] - mn), pw = __expf(a - mn);
+                l[h] = fmaf(l[h], corr, pw);
+                acc[h].x = fmaf(acc[h].x, corr, pw * v4.x);
+                acc[h].y = fmaf(acc[h].y, corr, pw * v4.y);
+                acc[h].z = fmaf(acc[h].z, corr, pw * v4.z);
+                acc[h].w = fmaf(acc[h].w, corr, pw * v4.w);
+                m[h] = mn;
+            }
+        }
+    }
+    if (!valid) return;
+    for (int h = 0; h < G; h++) {
+        const float inv = 1.0f / l[h];
+        reinterpret_cast<float4*>(att + (size_t)t * NQ * 128 + (size_t)(g * G + h) * 128)[lane] =
+            make_float4(acc[h].x * inv, acc[h].y * inv, acc[h].z * inv, acc[h].w * inv);
+    }
+}
+
+int grid_for(size_t total) { return (int)std::min<size_t>((total + 255) / 256, 148 * 8); }
+
+int run(const Weights& w, const CacheView& c, const uint32_t* d_ids, int n, int start, float* d_logits, Scratch& sc,
+        int* err_word, cudaStream_t s, std::string& err) {
+    const int H = w.H, I = w.I, NQ = w.NQ, NKV = w.NKV, QD = NQ * 128, KVD = NKV * 128, QKVR = QD + 2 * KVD;
+    const size_t nH = (size_t)n * H;
+    embed_rows<<<n, 256, 0, s>>>(d_ids, H, w.embed, sc.X);
+    const int G = NQ / NKV;
+    const float scale = 1.0f / sqrtf(128.0f);
+    for (int l = 0; l < w.L; l++) {
+        const uint16_t* W = w.layer_w + (size_t)l * w.layer_stride;
+        const uint16_t* nrm = w.layer_n + (size_t)l * w.norm_stride;
+        const size_t hsl = (size_t)l * NKV * c.max_seq * 128;
+        int rc;
+        // A: rmsnorm -> q|k|v
+        norm_split<<<n, ROW_THREADS, 0, s>>>(sc.X, H, nrm, w.eps, sc.ahi, sc.alo);
+        if ((rc = tc::gemm(sc.ahi, sc.alo, H, W, H, sc.Y, QKVR, n, QKVR, H, err_word, s, err))) return rc;
+        // B: q/k norm + RoPE, K/V into the cache, causal attention
+        const int items = n * (NQ + 2 * NKV);
+        qkv_post<<<(items + 7) / 8, 256, 0, s>>>(sc.Y, n, start, NQ, NKV, nrm + 2 * H, nrm + 2 * H + 128, w.eps, c.rope, sc.Q,
+                                                 c.k, c.v, hsl, c.max_seq);
+        dim3 ag((n + ATT_TOK - 1) / ATT_TOK, NKV);
+        if (G == 1) attention<1><<<ag, ATT_TOK * 32, 0, s>>>(sc.Q, sc.att, c.k, c.v, n, start, NQ, hsl, c.max_seq, scale);
+        else if (G == 2) attention<2><<<ag, ATT_TOK * 32, 0, s>>>(sc.Q, sc.att, c.k, c.v, n, start, NQ, hsl, c.max_seq, scale);
+        else attention<3><<<ag, ATT_TOK * 32, 0, s>>>(sc.Q, sc.att, c.k, c.v, n, start, NQ, hsl, c.max_seq, scale);
+        // C: o_proj + residual
+        split_rows<<<grid_for((size_t)n * QD), 256, 0, s>>>(sc.att, (size_t)n * QD, sc.ahi, sc.alo);
+        if ((rc = tc::gemm(sc.ahi, sc.alo, QD, W + (size_t)QKVR * H, QD, sc.Y, H, n, H, QD, err_word, s, err))) return rc;
+        residual_add<<<grid_for(nH), 256, 0, s>>>(sc.X, sc.Y, nH);
+        // D: rmsnorm -> gate|up -> silu(gate) * up
+        norm_split<<<n, ROW_THREADS, 0, s>>>(sc.X, H, nrm + H, w.eps, sc.ahi, sc.alo);
+        const uint16_t* Wgu = W + (size_t)QKVR * H + (size_t)H * QD;
+        if ((rc = tc::gemm(sc.ahi, sc.alo, H, Wgu, H, sc.Y, 2 * I, n, 2 * I, H, err_word, s, err))) return rc;
+        silu_split<<<grid_for((size_t)n * I), 256, 0, s>>>(sc.Y, (size_t)n * I, sc.ahi, sc.alo);
+        // E: down + residual
+        const uint16_t* Wd = Wgu + (size_t)2 * I * H;
+        if ((rc = tc::gemm(sc.ahi, sc.alo, I, Wd, I, sc.Y, H, n, H, I, err_word, s, err))) return rc;
+        residual_add<<<grid_for(nH), 256, 0, s>>>(sc.X, sc.Y, nH);
+    }
+    if (d_logits) {
+        norm_split<<<n, ROW_THREADS, 0, s>>>(sc.X, H, w.final_norm, w.eps, sc.ahi, sc.alo);
+        int rc;
+        if ((rc = tc::gemm(sc.ahi, sc.alo, H, w.lm_head, H, d_logits, w.V, n, w.V, H, err_word, s, err))) return rc;
+    }
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        err = std::string("prefill launch failed: ") + cudaGetErrorString(e);
+        return QW_ERR_CUDA;
+    }
+    return QW_OK;
+}
+
+}  // namespace pf
 }  // namespace qw
 
 extern "C" {

@@ -197,7 +197,9 @@ gemm_bf16x2_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_con
             if (row < args.M && n0 + c < args.N) {
                 float* dst = args.y + (size_t)row * args.ldy + n0 + c;
                 const int nv = args.N - (n0 + c) < 32 ? args.N - (n0 + c) : 32;
-                if (nv == 32) {
+                // float4 stores only where the row is 16-byte aligned (ldy need not be a multiple of 4,
+                // e.g. an odd vocabulary size)
+                if (nv == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
 #pragma unroll
                     for (int j = 0; j < 32; j += 4)
                         *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),

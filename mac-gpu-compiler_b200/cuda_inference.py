@@ -85,6 +85,7 @@ def lib() -> ctypes.CDLL:
             "qw_cache_free": (None, [vp]),
             "qw_cache_max_seq": (sz, [vp]),
             "qw_forward": (i32, [vp, vp, u32, sz, vp]),
+            "qw_prefill": (i32, [vp, vp, vp, sz, sz, vp]),
             "qw_decode": (i32, [vp, vp, u32, sz, sz, TOKEN_FN, vp]),
             "qw_forward_device": (i32, [vp, vp, vp, sz, vp, vp]),
             "qw_decode_device": (i32, [vp, vp, vp, sz, sz, vp]),
@@ -165,6 +166,15 @@ class CudaModel:
     def forward(self, token: int, pos: int, cache: "CudaKVCache") -> np.ndarray:
         out = np.empty(self.config.vocab_size, np.float32)
         _check(lib().qw_forward(self._h, cache._h, token, pos, out.ctypes.data))
+        return out
+
+    def prefill(self, ids, start_pos: int, cache: "CudaKVCache", logits: bool = True) -> np.ndarray | None:
+        """One batched pass over the prompt ids at positions start_pos.. (qw_prefill): fills the KV
+        cache like len(ids) forward calls; returns the [len(ids), vocab] logits when asked."""
+        a = np.ascontiguousarray(np.asarray(ids, dtype=np.uint32))
+        out = np.empty((a.size, self.config.vocab_size), np.float32) if logits else None
+        _check(lib().qw_prefill(self._h, cache._h, a.ctypes.data, a.size, start_pos,
+                                out.ctypes.data if out is not None else None))
         return out
 
     def decode(self, first: int, start_pos: int, steps: int, cache: "CudaKVCache",

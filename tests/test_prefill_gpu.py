@@ -1,0 +1,76 @@
+"""Batched prefill (qw_prefill) against the reference CPU engine's token-by-token
+prefill (the oracle, cpu_inference.rs:100-179): every position's logits within 1e-2 max-abs, the
+K/V cache filled at the same slots (indexing exact, values within the f32 tolerance of the
+reordered arithmetic), and a greedy decode continuing from a prefilled cache producing the same
+tokens as one continuing from a forward-filled cache."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import cpu_oracle as co
+import cuda_inference as ci
+import randmodel
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+TOL = 1e-2
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _need_gpu():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+@pytest.mark.parametrize("geometry,n", [("tiny", 40), ("mid", 130), ("qwen3-0.6b", 64)])
+def test_prefill_matches_token_by_token_oracle(geometry, n):
+    path = randmodel.make_model(geometry, 0)
+    om = co.Model.load_model(path)
+    oc = co.KVCache(om)
+    ids = randmodel.prompt_ids(n, om.config.vocab_size, seed=3)
+    want = np.stack([om.forward(t, p, oc) for p, t in enumerate(ids)])
+    m = ci.CudaModel.load_model(path)
+    cache = ci.CudaKVCache(m, n + 8)
+    got = m.prefill(ids, 0, cache)
+    assert got.shape == want.shape
+    assert np.abs(got - want).max() <= TOL
+    for l in (0, om.config.num_hidden_layers - 1):
+        k, v = cache.layer(l, n)
+        ko, vo = oc.layer(l)
+        assert np.abs(k - ko).max() <= 1e-3 and np.abs(v - vo).max() <= 1e-3
+
+
+def test_prefill_then_decode_matches_forward_then_decode(mid_model_path):
+    m = ci.CudaModel.load_model(mid_model_path)
+    ids = randmodel.prompt_ids(48, m.config.vocab_size, seed=5)
+    c1, c2 = ci.CudaKVCache(m, 80), ci.CudaKVCache(m, 80)
+    lg = m.prefill(ids, 0, c1)
+    for p, t in enumerate(ids):
+        lf = m.forward(t, p, c2)
+    assert np.abs(lg[-1] - lf).max() <= TOL
+    first = int(np.argmax(lf))
+    assert m.decode(first, len(ids), 16, c1) == m.decode(first, len(ids), 16, c2)
+
+
+def test_prefill_continues_an_existing_cache(mid_model_path):
+    # two prefill calls (positions 0..19, then 20..49) equal one call over all 50 positions
+    m = ci.CudaModel.load_model(mid_model_path)
+    ids = randmodel.prompt_ids(50, m.config.vocab_size, seed=7)
+    c1, c2 = ci.CudaKVCache(m, 64), ci.CudaKVCache(m, 64)
+    whole = m.prefill(ids, 0, c1)
+    m.prefill(ids[:20], 0, c2, logits=False)
+    tail = m.prefill(ids[20:], 20, c2)
+    assert np.abs(tail - whole[20:]).max() <= 1e-4
+
+
+def test_prefill_argument_errors(tiny_model_path):
+    m = ci.CudaModel.load_model(tiny_model_path)
+    cache = ci.CudaKVCache(m, 16)
+    with pytest.raises(ci.QwError) as e:
+        m.prefill([1, 2, 3], 14, cache)                 # runs past the cache
+    assert e.value.code == ci.QW_ERR_ARG
+    with pytest.raises(ci.QwError) as e:
+        m.prefill([1, m.config.vocab_size], 0, cache)   # token id out of range
+    assert e.value.code == ci.QW_ERR_ARG

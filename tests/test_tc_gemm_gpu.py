@@ -1,7 +1,8 @@
 """The prefill's tcgen05 tensor-core GEMM through the C ABI (qw_gemm_bf16x2), against a float64
 product of the same bf16 operands: Y = (A_hi + A_lo) . B^T, with A_hi + A_lo the two-bf16 split of
 f32 activations. Shapes cover the prefill's projections (K = 1024, 2048, 3072), a ragged M (rows
-that are not a multiple of the 128-row tile, which the TMA zero-fills) and the lm_head width."""
+that are not a multiple of the 128-row tile, which the TMA zero-fills), the lm_head width and an
+odd output width (rows of the f32 output that are not 16-byte aligned)."""
 from __future__ import annotations
 
 import pytest
@@ -25,7 +26,7 @@ def split_bf16(a: "torch.Tensor"):
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 128, 64), (512, 4096, 1024), (200, 1024, 2048), (77, 6144, 1024),
-                                   (512, 1024, 3072), (33, 151936, 1024)])
+                                   (512, 1024, 3072), (33, 151936, 1024), (130, 10007, 1024)])
 def test_gemm_matches_f64(M, N, K):
     g = torch.Generator(device="cuda").manual_seed(M * 7 + N + K)
     a = torch.randn(M, K, device="cuda", generator=g)
