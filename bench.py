@@ -46,6 +46,8 @@ import replicas  # noqa: E402
 CONFIGS = {
     "ai130": dict(prompt=130, decode=128, label="configs[0]: 130-id prompt token-by-token, then 128 greedy decode steps (pos 130..257)"),
     "long": dict(prompt=2048, decode=512, label="configs[1]: 2048-id prompt token-by-token, then 512 greedy decode steps (pos 2048..2559)"),
+    "prefill": dict(prompt=512, decode=64,
+                    label="configs[3]: 512-id prompt in one batched prefill pass (tcgen05 GEMMs), then 64 greedy decode steps"),
     "box": dict(prompt=130, decode=128, sequences=64,
                 label="configs[4]: 64 independent sequences (130-id prompt + 128 greedy steps each) sharded over the GPUs"),
 }
@@ -63,6 +65,116 @@ NCU_TRAFFIC_RATIO = (4_777_293_000 + 5_276_928) / 4_778_041_344
 def kv_bytes_at(cfg, pos: int) -> int:
     """tests/mbu.rs:32-37 — f32 K and V for every cached position (0..=pos) in every layer."""
     return 2 * cfg.num_hidden_layers * (pos + 1) * cfg.num_key_value_heads * cfg.head_dim * 4
+
+
+def load_tensor_peak() -> tuple[float, str]:
+    """Sustained dense bf16 TFLOP/s (a prefill is a multi-millisecond chain of GEMMs)."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops_sustained"]), "measured sustained"
+        except (ValueError, KeyError):
+            pass
+    return 1400.0, "fallback sustained"
+
+
+def prefill_flops(cfg, n: int, start: int = 0) -> float:
+    """Algorithmic FLOPs of one prefill pass over n tokens: 2 per weight per token for every
+    projection and the lm_head, plus q.k and p.v over each token's causal window (the split-bf16
+    operands double the tensor-core work; that is not counted)."""
+    H, I, L, V = cfg.hidden_size, cfg.intermediate_size, cfg.num_hidden_layers, cfg.vocab_size
+    QD = cfg.num_attention_heads * cfg.head_dim
+    KVD = cfg.num_key_value_heads * cfg.head_dim
+    per_tok = 2 * L * ((QD + 2 * KVD) * H + H * QD + 2 * I * H + H * I) + 2 * V * H
+    attn = sum(4 * QD * (start + t + 1) for t in range(n)) * L
+    return float(per_tok * n + attn)
+
+
+def run_prefill(args, world: int, rank: int, local: int, pg) -> None:
+    """one batched prefill of a 512-id prompt per step (device-resident ids and logits,
+    CUDA events on the model stream), then 64 greedy decode steps from the prefilled cache."""
+    import numpy as np
+    import torch
+    import cuda_inference as ci
+    c = CONFIGS["prefill"]
+    n, n_dec = c["prompt"], c["decode"]
+    path = randmodel.make_model("qwen3-0.6b", 0)
+    model = ci.CudaModel.load_model(path, device=local)
+    cfg = model.config
+    cache = ci.CudaKVCache(model, n + n_dec + 1)
+    ids = randmodel.prompt_ids(n, cfg.vocab_size, seed=replicas.prompt_seed(rank))
+    d_ids = torch.tensor(ids, dtype=torch.int32, device=f"cuda:{local}")
+    d_logits = torch.empty(n, cfg.vocab_size, dtype=torch.float32, device=f"cuda:{local}")
+    stream = torch.cuda.ExternalStream(model.stream)
+
+    def step():
+        model.prefill_device(cache, d_ids.data_ptr(), n, 0, d_logits.data_ptr(), stream=model.stream)
+
+    for _ in range(args.warmup):
+        step()
+    model.sync()
+    if pg is not None:
+        pg.barrier()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        t0.record(stream)
+        for i in range(args.steps):
+            evs[i][0].record(stream)
+            step()
+            evs[i][1].record(stream)
+        t1.record(stream)
+        torch.cuda.synchronize()
+    model.sync()
+    elapsed = t0.elapsed_time(t1) / 1e3
+    step_s = statistics.mean(a.elapsed_time(b) for a, b in evs) / 1e3
+    timings = replicas.reduce_timings(replicas.RankTiming(n * args.steps, elapsed),
+                                      group=pg.group.WORLD if pg is not None else None)
+    box = replicas.aggregate(timings)
+    # then 64 greedy decode steps from the prefilled cache (the rest of configs[3])
+    first = int(torch.argmax(d_logits[-1]).item())
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    toks = model.decode(first, n, n_dec, cache)
+    b.record(stream)
+    torch.cuda.synchronize()
+    dec_s = a.elapsed_time(b) / 1e3
+    # e2e through the host API: ids from host memory in, all logits (n x vocab f32) back out
+    e2e = []
+    for i in range(3):
+        ea, eb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ea.record(stream)
+        model.prefill(ids, 0, cache)
+        eb.record(stream)
+        torch.cuda.synchronize()
+        if i:
+            e2e.append(ea.elapsed_time(eb) / 1e3)
+    e2e_box = replicas.aggregate(replicas.reduce_timings(replicas.RankTiming(n * len(e2e), sum(e2e)),
+                                                         group=pg.group.WORLD if pg is not None else None))
+    if rank == 0:
+        flops = prefill_flops(cfg, n)
+        peak, kind = load_tensor_peak()
+        achieved = flops / step_s / 1e12
+        print(json.dumps({
+            "metric": "Qwen3-0.6B bf16 batched prefill tok/s (512-token prompt, per-position logits)",
+            "value": box["tok_per_s"], "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": box["seconds"] / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "accumulate": "f32 (split-bf16 activations)", "data": "synthetic",
+            "config": {"workload": c["label"], "model": "Qwen3-0.6B geometry, random-init bf16 (seed 0)",
+                       "global_batch": world, "seq_len": n + n_dec,
+                       "parallelism": f"replicas x{world}, one independent prompt per GPU, no collective",
+                       "step": f"one {n}-token prefill pass incl. the lm_head over all positions"},
+            "e2e": {"value": e2e_box["tok_per_s"], "unit": "tok/s", "h2d_bytes_per_step": 4 * n,
+                    "d2h_bytes_per_step": 4 * n * cfg.vocab_size, "api": "qw_prefill (host ids in, host logits out)"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                         "peak_kind": f"{kind} (bf16_tflops_sustained, cuBLAS)", "traffic": None,
+                         "algorithmic_flops_per_step": flops, "kernel": "prefill pass (qw::tc::gemm_bf16x2_kernel + elementwise)"},
+            "decode_after_prefill": {"steps": n_dec, "tok_per_s": n_dec / dec_s, "first_tokens": toks[:8]},
+            "gpu_launches": args.steps * (1 + 9 * cfg.num_hidden_layers + 2),
+            "clocks": clocks.summary(),
+        }), flush=True)
+    model.close()
 
 
 def load_peaks() -> tuple[float, str]:
@@ -184,7 +296,10 @@ def run_reference(args, cfg_name: str) -> None:
     sample = (f"{per_step} greedy decode tokens per step at positions {c['prompt']}..{pos - 1} after a "
               f"synthetic {c['prompt']}-position K/V cache, {co.threads()} host threads")
     print(json.dumps({
-        "impl": "reference", "metric": "Qwen3-0.6B bf16 decode tok/s @bs1", "value": v, "unit": "tok/s",
+        "impl": "reference",
+        "metric": ("Qwen3-0.6B bf16 batched prefill tok/s (512-token prompt, per-position logits)" if cfg_name == "prefill"
+                   else "Qwen3-0.6B bf16 decode tok/s @bs1"),
+        "value": v, "unit": "tok/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "dtype": "bf16", "data": "synthetic",
         "config": {"workload": c["label"], "model": "Qwen3-0.6B geometry, random-init bf16 (seed 0)",
@@ -223,6 +338,12 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
         pg = dist
+    if args.config == "prefill":
+        run_prefill(args, world, rank, local, pg)
+        if pg is not None:
+            pg.barrier()
+            pg.destroy_process_group()
+        return
 
     c = CONFIGS[args.config]
     n_prompt, n_dec = c["prompt"], c["decode"]

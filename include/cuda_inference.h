@@ -89,6 +89,11 @@ int qw_forward(qw_model* model, qw_cache* cache, uint32_t token, size_t pos, flo
  * (host, n * vocab_size floats, row t = position start_pos + t) also every position's logits.
  * Synchronous. */
 int qw_prefill(qw_model* model, qw_cache* cache, const uint32_t* ids, size_t n, size_t start_pos, float* logits_out);
+/* qw_prefill with device-resident ids (d_ids[n]) and logits (d_logits[n * vocab_size] or NULL),
+ * stream-ordered on `stream` (NULL = the model's stream), without synchronisation; token ids are not
+ * range-checked here (they must be < vocab_size). A GEMM wait that expired is reported by qw_sync. */
+int qw_prefill_device(qw_model* model, qw_cache* cache, const uint32_t* d_ids, size_t n, size_t start_pos,
+                      float* d_logits, void* stream);
 
 /* MetalModel::decode (metal_inference.rs:297-316): greedy decode; `first` goes in at `start_pos`,
  * each step's argmax feeds the next, and on_token(user, t) is called with each step's output

@@ -611,6 +611,26 @@ int qw_prefill(qw_model* m, qw_cache* c, const uint32_t* ids, size_t n, size_t s
     return QW_OK;
 }
 
+int qw_prefill_device(qw_model* m, qw_cache* c, const uint32_t* d_ids, size_t n, size_t start_pos, float* d_logits,
+                      void* stream) {
+    if (!m || !c || !d_ids || c->m != m || c->model_id != m->id) return set_err(QW_ERR_ARG, "null or mismatched handle");
+    if (n == 0) return QW_OK;
+    if (n > (1u << 20) || start_pos + n > c->max_seq) return set_err(QW_ERR_ARG, "start_pos + n exceeds the KV cache size");
+    QW_CUDA(cudaSetDevice(m->device));
+    if (int e = ensure_prefill(m, n, false)) return e;
+    int* ew = qw::device_err_word_for(m->device);
+    if (!ew) return set_err(QW_ERR_NOMEM, "error word allocation failed");
+    cudaStream_t s = pick_stream(m, stream);
+    QW_CUDA(cudaMemsetAsync(ew, 0, sizeof(int), s));
+    const ModelConfig& cf = m->cfg;
+    qw::pf::Weights w{m->d_layer_w, m->d_layer_n, m->d_final_norm, m->d_embed, m->d_lm_head, m->layer_stride, m->norm_stride,
+                      (int)cf.hidden, (int)cf.inter, (int)cf.layers, (int)cf.heads, (int)cf.kv_heads, (int)cf.vocab, cf.eps};
+    qw::pf::CacheView cv{c->d_k, c->d_v, c->d_rope, (int)c->max_seq};
+    std::string err;
+    if (int e = qw::pf::run(w, cv, d_ids, (int)n, (int)start_pos, d_logits, m->pf, ew, s, err)) return set_err(e, err);
+    return QW_OK;
+}
+
 int qw_forward(qw_model* m, qw_cache* c, uint32_t token, size_t pos, float* logits_out) {
     if (!m || !c || !logits_out || c->m != m || c->model_id != m->id) return set_err(QW_ERR_ARG, "null or mismatched handle");
     if (token >= m->cfg.vocab) return set_err(QW_ERR_ARG, "token id >= vocab_size");
@@ -684,7 +704,17 @@ int qw_sync(qw_model* m, void* stream) {
     if (!m) return set_err(QW_ERR_ARG, "null handle");
     QW_CUDA(cudaSetDevice(m->device));
     QW_CUDA(cudaStreamSynchronize(pick_stream(m, stream)));
-    return check_device_err(m);
+    if (int e = check_device_err(m)) return e;
+    // the prefill GEMMs report an expired pipeline wait through the device's shared error word
+    if (int* ew = qw::device_err_word_for(m->device)) {
+        int h = 0;
+        QW_CUDA(cudaMemcpy(&h, ew, sizeof(int), cudaMemcpyDeviceToHost));
+        if (h) {
+            QW_CUDA(cudaMemset(ew, 0, sizeof(int)));
+            return set_err(QW_ERR_DEVICE_TIMEOUT, "prefill: a GEMM pipeline wait expired on the device");
+        }
+    }
+    return QW_OK;
 }
 
 int qw_cache_read(qw_cache* c, size_t layer, size_t n, float* k_out, float* v_out) {

@@ -86,6 +86,7 @@ def lib() -> ctypes.CDLL:
             "qw_cache_max_seq": (sz, [vp]),
             "qw_forward": (i32, [vp, vp, u32, sz, vp]),
             "qw_prefill": (i32, [vp, vp, vp, sz, sz, vp]),
+            "qw_prefill_device": (i32, [vp, vp, vp, sz, sz, vp, vp]),
             "qw_decode": (i32, [vp, vp, u32, sz, sz, TOKEN_FN, vp]),
             "qw_forward_device": (i32, [vp, vp, vp, sz, vp, vp]),
             "qw_decode_device": (i32, [vp, vp, vp, sz, sz, vp]),
@@ -176,6 +177,10 @@ class CudaModel:
         _check(lib().qw_prefill(self._h, cache._h, a.ctypes.data, a.size, start_pos,
                                 out.ctypes.data if out is not None else None))
         return out
+
+    def prefill_device(self, cache: "CudaKVCache", d_ids: int, n: int, start_pos: int, d_logits: int = 0,
+                       stream: int = 0) -> None:
+        _check(lib().qw_prefill_device(self._h, cache._h, d_ids, n, start_pos, d_logits or None, stream or None))
 
     def decode(self, first: int, start_pos: int, steps: int, cache: "CudaKVCache",
                on_token: Callable[[int], None] | None = None) -> list[int]:
