@@ -202,76 +202,179 @@ __global__ void qkv_post(const float* Y, int n, int start, int NQ, int NKV, cons
     else reinterpret_cast<float4*>(Kc + head_stride_l + ((size_t)(hh - NQ) * max_seq + pos) * 128)[lane] = out;
 }
 
-constexpr int ATT_TOK = 8;    // tokens per attention CTA (one warp each)
-constexpr int ATT_CHUNK = 32; // cached positions staged in shared memory at a time
+// Causal GQA attention for the prefill as a small f32 flash attention on the CUDA cores (the
+// same math as cpu_inference.rs:143-161, a running softmax over position chunks). CTA = (tile of
+// QT query tokens, kv head g): its QT x G query rows meet chunks of PC cached positions staged in
+// shared memory; per chunk every thread computes a 4 x 4 block of scores (rows x positions), the
+// row groups update their running max / sum, and every thread adds P . V into a 4-row x 8-dim
+// block of outputs. Positions after a row's own position are masked (causal).
+constexpr int PC = 64;                 // positions per chunk
+constexpr int AT_THREADS = 256;
+constexpr int KPAD = 132;              // K row pitch in floats (bank spread for the score loads)
 
-// Causal GQA attention for the prefill: CTA (token tile, kv head g), warp w = token t0 + w with its
-// G query heads; every warp runs the same online softmax as the decode kernel over positions
-// 0 .. start + t, reading the K/V rows the CTA stages in shared memory (cpu_inference.rs:143-161).
+// query tokens per CTA: 64 query rows for 1 or 2 query heads per KV head, 48 for 3
 template <int G>
-__global__ void __launch_bounds__(ATT_TOK * 32) attention(const float* Q, float* att, const float* Kc, const float* Vc, int n,
-                                                          int start, int NQ, size_t head_stride_l, int max_seq, float scale) {
-    __shared__ __align__(16) float Ks[ATT_CHUNK][128];
-    __shared__ __align__(16) float Vs[ATT_CHUNK][128];
-    const int g = blockIdx.y, t0 = blockIdx.x * ATT_TOK;
-    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = t0 + w;
-    const bool valid = t < n;
-    const int pos = start + t;
-    const int last = start + min(n, t0 + ATT_TOK) - 1;
-    float4 q4[G];
-    float m[G], l[G];
-    float4 acc[G];
-    for (int h = 0; h < G; h++) {
-        q4[h] = valid ? reinterpret_cast<const float4*>(Q + (size_t)t * NQ * 128 + (size_t)(g * G + h) * 128)[lane]
-                      : make_float4(0.f, 0.f, 0.f, 0.f);
-        m[h] = -INFINITY;
-        l[h] = 0.f;
-        acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+struct AttTile {
+    static constexpr int QT = G == 1 ? 64 : G == 2 ? 32 : 16;
+};
+
+template <int G>
+struct AttSmem {
+    static constexpr int QT = AttTile<G>::QT;
+    float q[QT * G][KPAD];
+    float k[PC][KPAD];
+    float v[PC][128];
+    float p[QT * G][PC + 1];
+    float corr[QT * G];
+    float linv[QT * G];
+};
+
+template <int G>
+__global__ void __launch_bounds__(AT_THREADS) attention(const float* Q, float* att, const float* Kc, const float* Vc, int n,
+                                                        int start, int NQ, size_t head_stride_l, int max_seq, float scale) {
+    constexpr int QT = AttTile<G>::QT;
+    constexpr int R = QT * G;           // query rows of the tile
+    constexpr int RB = R / 4;           // row blocks of 4
+    static_assert(R % 4 == 0 && RB * 16 <= AT_THREADS, "row blocks x 16 must fit the CTA");
+    extern __shared__ __align__(16) uint8_t att_raw[];
+    AttSmem<G>& sm = *reinterpret_cast<AttSmem<G>*>(att_raw);
+    const int g = blockIdx.y, t0 = blockIdx.x * QT;
+    const int tid = threadIdx.x;
+    const int ntok = min(QT, n - t0);
+    // query rows: row r = token (r / G) of the tile, head g*G + r % G
+    for (int i = tid; i < R * 32; i += AT_THREADS) {
+        const int r = i >> 5, c = i & 31, tl = r / G, h = r % G;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (tl < ntok) v = reinterpret_cast<const float4*>(Q + (size_t)(t0 + tl) * NQ * 128 + (size_t)(g * G + h) * 128)[c];
+        reinterpret_cast<float4*>(sm.q[r])[c] = v;
+    }
+    // score block: rows 4*rb.., positions pb + 16 j; output block: rows 4*rb.., dims 8*db..
+    const int rb = tid >> 4, pb = tid & 15;
+    const bool active = rb < RB;
+    float m_run[4], l_run[4];
+    float o[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        m_run[i] = -INFINITY;
+        l_run[i] = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; j++) o[i][j] = 0.f;
     }
     const float* kb = Kc + head_stride_l + (size_t)g * max_seq * 128;
     const float* vb = Vc + head_stride_l + (size_t)g * max_seq * 128;
-    for (int p0 = 0; p0 <= last; p0 += ATT_CHUNK) {
-        const int np = min(ATT_CHUNK, last + 1 - p0);
+    const int last = start + t0 + ntok - 1;  // the tile's last position
+    for (int p0 = 0; p0 <= last; p0 += PC) {
+        const int np = min(PC, last + 1 - p0);
         __syncthreads();
-        for (int i = threadIdx.x; i < np * 32; i += blockDim.x) {
+        for (int i = tid; i < PC * 32; i += AT_THREADS) {
             const int r = i >> 5, c = i & 31;
-            reinterpret_cast<float4*>(Ks[r])[c] = reinterpret_cast<const float4*>(kb + (size_t)(p0 + r) * 128)[c];
-            reinterpret_cast<float4*>(Vs[r])[c] = reinterpret_cast<const float4*>(vb + (size_t)(p0 + r) * 128)[c];
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+            if (r < np) {
+                kv = reinterpret_cast<const float4*>(kb + (size_t)(p0 + r) * 128)[c];
+                vv = reinterpret_cast<const float4*>(vb + (size_t)(p0 + r) * 128)[c];
+            }
+            reinterpret_cast<float4*>(sm.k[r])[c] = kv;
+            reinterpret_cast<float4*>(sm.v[r])[c] = vv;
         }
         __syncthreads();
-        if (!valid) continue;
-        const int myn = min(np, pos + 1 - p0);  // positions of this chunk this token attends to
-        for (int pp = 0; pp < myn; pp++) {
-            const float4 k4 = reinterpret_cast<const float4*>(Ks[pp])[lane];
-            const float4 v4 = reinterpret_cast<const float4*>(Vs[pp])[lane];
-            float sc[G];
+        if (active) {
+            // S = q . k for rows 4rb..4rb+3 and positions pb, pb+16, pb+32, pb+48
+            float s[4][4];
 #pragma unroll
-            for (int h = 0; h < G; h++) sc[h] = q4[h].x * k4.x + q4[h].y * k4.y + q4[h].z * k4.z + q4[h].w * k4.w;
+            for (int i = 0; i < 4; i++)
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1)
+                for (int j = 0; j < 4; j++) s[i][j] = 0.f;
+#pragma unroll 4
+            for (int d = 0; d < 128; d += 4) {
+                float4 qv[4], kv[4];
 #pragma unroll
-                for (int h = 0; h < G; h++) sc[h] += __shfl_xor_sync(0xFFFFFFFFu, sc[h], o);
+                for (int i = 0; i < 4; i++) qv[i] = *reinterpret_cast<const float4*>(&sm.q[4 * rb + i][d]);
 #pragma unroll
-            for (int h = 0; h < G; h++) {
-                const float a = sc[h] * scale;
-                const float mn = fmaxf(m[h], a);
-                const float corr = __expf(m[h] - mn), pw = __expf(a - mn);
-                l[h] = fmaf(l[h], corr, pw);
-                acc[h].x = fmaf(acc[h].x, corr, pw * v4.x);
-                acc[h].y = fmaf(acc[h].y, corr, pw * v4.y);
-                acc[h].z = fmaf(acc[h].z, corr, pw * v4.z);
-                acc[h].w = fmaf(acc[h].w, corr, pw * v4.w);
-                m[h] = mn;
+                for (int j = 0; j < 4; j++) kv[j] = *reinterpret_cast<const float4*>(&sm.k[pb + 16 * j][d]);
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+                        s[i][j] = fmaf(qv[i].x, kv[j].x, fmaf(qv[i].y, kv[j].y, fmaf(qv[i].z, kv[j].z, fmaf(qv[i].w, kv[j].w, s[i][j]))));
+            }
+            // running softmax per row over this chunk (the 16 threads of a row block share its rows)
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int r = 4 * rb + i;
+                const int pos = start + t0 + r / G;
+                float mx = -INFINITY;
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int pp = pb + 16 * j;
+                    s[i][j] = (pp < np && p0 + pp <= pos) ? s[i][j] * scale : -INFINITY;
+                    mx = fmaxf(mx, s[i][j]);
+                }
+#pragma unroll
+                for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xFFFFFFFFu, mx, off));
+                const float mn = fmaxf(m_run[i], mx);
+                float sum = 0.f;
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const float e = mn == -INFINITY ? 0.f : __expf(s[i][j] - mn);
+                    sm.p[r][pb + 16 * j] = e;
+                    sum += e;
+                }
+#pragma unroll
+                for (int off = 8; off > 0; off >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, off);
+                const float corr = m_run[i] == -INFINITY ? 0.f : __expf(m_run[i] - mn);
+                l_run[i] = l_run[i] * corr + sum;
+                m_run[i] = mn;
+                if (pb == 0) sm.corr[r] = corr;
+            }
+        }
+        __syncthreads();
+        if (active) {
+            // O = O * corr + P . V for rows 4rb.. and dims 8pb..8pb+7
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float c = sm.corr[4 * rb + i];
+#pragma unroll
+                for (int j = 0; j < 8; j++) o[i][j] *= c;
+            }
+            for (int pp = 0; pp < np; pp++) {
+                const float4 va = *reinterpret_cast<const float4*>(&sm.v[pp][8 * pb]);
+                const float4 vb4 = *reinterpret_cast<const float4*>(&sm.v[pp][8 * pb + 4]);
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const float pw = sm.p[4 * rb + i][pp];
+                    o[i][0] = fmaf(pw, va.x, o[i][0]);
+                    o[i][1] = fmaf(pw, va.y, o[i][1]);
+                    o[i][2] = fmaf(pw, va.z, o[i][2]);
+                    o[i][3] = fmaf(pw, va.w, o[i][3]);
+                    o[i][4] = fmaf(pw, vb4.x, o[i][4]);
+                    o[i][5] = fmaf(pw, vb4.y, o[i][5]);
+                    o[i][6] = fmaf(pw, vb4.z, o[i][6]);
+                    o[i][7] = fmaf(pw, vb4.w, o[i][7]);
+                }
             }
         }
     }
-    if (!valid) return;
-    for (int h = 0; h < G; h++) {
-        const float inv = 1.0f / l[h];
-        reinterpret_cast<float4*>(att + (size_t)t * NQ * 128 + (size_t)(g * G + h) * 128)[lane] =
-            make_float4(acc[h].x * inv, acc[h].y * inv, acc[h].z * inv, acc[h].w * inv);
+    if (!active) return;
+    // the row sums live with the score threads of the same row block (identical in all 16)
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int r = 4 * rb + i, tl = r / G, h = r % G;
+        if (tl >= ntok) continue;
+        const float inv = 1.0f / l_run[i];
+        float* dst = att + (size_t)(t0 + tl) * NQ * 128 + (size_t)(g * G + h) * 128 + 8 * pb;
+        reinterpret_cast<float4*>(dst)[0] = make_float4(o[i][0] * inv, o[i][1] * inv, o[i][2] * inv, o[i][3] * inv);
+        reinterpret_cast<float4*>(dst)[1] = make_float4(o[i][4] * inv, o[i][5] * inv, o[i][6] * inv, o[i][7] * inv);
     }
+}
+
+template <int G>
+int launch_attention(const float* Q, float* att, const float* Kc, const float* Vc, int n, int start, int NQ, int NKV,
+                     size_t hsl, int max_seq, float scale, cudaStream_t s) {
+    const int smem = (int)sizeof(AttSmem<G>);
+    if (cudaFuncSetAttribute(attention<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return QW_ERR_CUDA;
+    dim3 grid((n + AttTile<G>::QT - 1) / AttTile<G>::QT, NKV);
+    attention<G><<<grid, AT_THREADS, smem, s>>>(Q, att, Kc, Vc, n, start, NQ, hsl, max_seq, scale);
+    return QW_OK;
 }
 
 int grid_for(size_t total) { return (int)std::min<size_t>((total + 255) / 256, 148 * 8); }
@@ -295,10 +398,13 @@ int run(const Weights& w, const CacheView& c, const uint32_t* d_ids, int n, int 
         const int items = n * (NQ + 2 * NKV);
         qkv_post<<<(items + 7) / 8, 256, 0, s>>>(sc.Y, n, start, NQ, NKV, nrm + 2 * H, nrm + 2 * H + 128, w.eps, c.rope, sc.Q,
                                                  c.k, c.v, hsl, c.max_seq);
-        dim3 ag((n + ATT_TOK - 1) / ATT_TOK, NKV);
-        if (G == 1) attention<1><<<ag, ATT_TOK * 32, 0, s>>>(sc.Q, sc.att, c.k, c.v, n, start, NQ, hsl, c.max_seq, scale);
-        else if (G == 2) attention<2><<<ag, ATT_TOK * 32, 0, s>>>(sc.Q, sc.att, c.k, c.v, n, start, NQ, hsl, c.max_seq, scale);
-        else attention<3><<<ag, ATT_TOK * 32, 0, s>>>(sc.Q, sc.att, c.k, c.v, n, start, NQ, hsl, c.max_seq, scale);
+        rc = G == 1 ? launch_attention<1>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, s)
+           : G == 2 ? launch_attention<2>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, s)
+                    : launch_attention<3>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, s);
+        if (rc) {
+            err = "cannot raise the prefill attention kernel's shared-memory limit";
+            return rc;
+        }
         // C: o_proj + residual
         split_rows<<<grid_for((size_t)n * QD), 256, 0, s>>>(sc.att, (size_t)n * QD, sc.ahi, sc.alo);
         if ((rc = tc::gemm(sc.ahi, sc.alo, QD, W + (size_t)QKVR * H, QD, sc.Y, H, n, H, QD, err_word, s, err))) return rc;

@@ -205,7 +205,9 @@ gemm_bf16x2_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_con
                         *reinterpret_cast<float4*>(dst + j) = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
                                                                           __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
                 } else {
-                    for (int j = 0; j < nv; j++) dst[j] = __uint_as_float(r[j]);
+#pragma unroll
+                    for (int j = 0; j < 32; j++)  // unrolled: r stays in registers
+                        if (j < nv) dst[j] = __uint_as_float(r[j]);
                 }
             }
         }
