@@ -441,6 +441,7 @@ void qw_free(qw_model* m) {
     cudaFree(m->pf.att);
     cudaFree(m->pf.ahi);
     cudaFree(m->pf.alo);
+    cudaFree(m->pf.attp);
     cudaFree(m->d_pf_ids);
     cudaFree(m->d_pf_logits);
     if (m->h_tok) cudaFreeHost(m->h_tok);
@@ -548,14 +549,14 @@ size_t qw_cache_max_seq(const qw_cache* c) { return c ? c->max_seq : 0; }
 namespace {
 
 // grow the prefill scratch to hold n tokens (and, with logits, n rows of logits)
-int ensure_prefill(qw_model* m, size_t n, bool logits) {
+int ensure_prefill(qw_model* m, size_t n, size_t start, bool logits) {
     const ModelConfig& c = m->cfg;
     const size_t H = c.hidden, I = c.inter, QD = c.heads * c.head_dim, KVD = c.kv_heads * c.head_dim;
     const size_t QKVR = QD + 2 * KVD;
     if ((int)n > m->pf.cap) {
         const size_t cap = std::max<size_t>(n, 2 * (size_t)m->pf.cap);
         qw::pf::Scratch sc;
-        const size_t ycols = std::max({QKVR, 2 * I, H}), acols = std::max({H, QD, I});
+        const size_t ycols = std::max({QKVR, 2 * I, (size_t)qw::pf::KSPLIT_MAX * H}), acols = std::max({H, QD, I});
         bool ok = cudaMalloc(&sc.X, cap * H * 4) == cudaSuccess && cudaMalloc(&sc.Y, cap * ycols * 4) == cudaSuccess &&
                   cudaMalloc(&sc.Q, cap * QD * 4) == cudaSuccess && cudaMalloc(&sc.att, cap * QD * 4) == cudaSuccess &&
                   cudaMalloc(&sc.ahi, cap * acols * 2) == cudaSuccess && cudaMalloc(&sc.alo, cap * acols * 2) == cudaSuccess;
@@ -568,8 +569,19 @@ int ensure_prefill(qw_model* m, size_t n, bool logits) {
         cudaFree(m->pf.X); cudaFree(m->pf.Y); cudaFree(m->pf.Q); cudaFree(m->pf.att); cudaFree(m->pf.ahi); cudaFree(m->pf.alo);
         cudaFree(m->d_pf_ids);
         sc.cap = (int)cap;
+        sc.attp = m->pf.attp;
+        sc.attp_cap = m->pf.attp_cap;
         m->pf = sc;
         m->d_pf_ids = ids;
+    }
+    const size_t attp = qw::pf::attention_partial_floats((int)n, (int)start, (int)c.heads, (int)c.kv_heads);
+    if (attp > m->pf.attp_cap) {
+        float* d = nullptr;
+        const size_t cap = std::max(attp, 2 * m->pf.attp_cap);
+        if (cudaMalloc(&d, cap * 4) != cudaSuccess) return set_err(QW_ERR_NOMEM, "prefill attention scratch allocation failed");
+        cudaFree(m->pf.attp);
+        m->pf.attp = d;
+        m->pf.attp_cap = cap;
     }
     if (logits && n > m->pf_logits_cap) {
         float* d = nullptr;
@@ -590,7 +602,7 @@ int qw_prefill(qw_model* m, qw_cache* c, const uint32_t* ids, size_t n, size_t s
     for (size_t i = 0; i < n; i++)
         if (ids[i] >= m->cfg.vocab) return set_err(QW_ERR_ARG, "token id >= vocab_size");
     QW_CUDA(cudaSetDevice(m->device));
-    if (int e = ensure_prefill(m, n, logits_out != nullptr)) return e;
+    if (int e = ensure_prefill(m, n, start_pos, logits_out != nullptr)) return e;
     int* ew = qw::device_err_word_for(m->device);
     if (!ew) return set_err(QW_ERR_NOMEM, "error word allocation failed");
     QW_CUDA(cudaMemsetAsync(ew, 0, sizeof(int), m->stream));
@@ -617,7 +629,7 @@ int qw_prefill_device(qw_model* m, qw_cache* c, const uint32_t* d_ids, size_t n,
     if (n == 0) return QW_OK;
     if (n > (1u << 20) || start_pos + n > c->max_seq) return set_err(QW_ERR_ARG, "start_pos + n exceeds the KV cache size");
     QW_CUDA(cudaSetDevice(m->device));
-    if (int e = ensure_prefill(m, n, false)) return e;
+    if (int e = ensure_prefill(m, n, start_pos, false)) return e;
     int* ew = qw::device_err_word_for(m->device);
     if (!ew) return set_err(QW_ERR_NOMEM, "error word allocation failed");
     cudaStream_t s = pick_stream(m, stream);

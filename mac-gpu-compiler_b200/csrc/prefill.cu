@@ -72,10 +72,12 @@ int make_map_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t co
 }
 
 // Y[M][ldy] = (A_hi + A_lo)[M][K] . B[N][K]^T ; A halves with row pitch lda, B with row pitch ldb
+// With ksplit > 1 the K blocks are split over ksplit CTAs per tile, each writing its partial
+// product to its own slice y + z * M * ldy (the caller sums the slices in a fixed order).
 int gemm(const uint16_t* a_hi, const uint16_t* a_lo, int lda, const uint16_t* b, int ldb, float* y, int ldy, int M, int N,
-         int K, int* err_word, cudaStream_t s, std::string& err) {
-    if (M <= 0 || N <= 0 || K <= 0 || K % BK != 0) {
-        err = "gemm: M, N, K must be positive and K a multiple of 64";
+         int K, int* err_word, cudaStream_t s, std::string& err, int ksplit) {
+    if (M <= 0 || N <= 0 || K <= 0 || K % BK != 0 || ksplit < 1 || ksplit > K / BK) {
+        err = "gemm: M, N, K must be positive, K a multiple of 64 and 1 <= ksplit <= K / 64";
         return QW_ERR_ARG;
     }
     CUtensorMap mh, ml, mb;
@@ -87,8 +89,8 @@ int gemm(const uint16_t* a_hi, const uint16_t* a_lo, int lda, const uint16_t* b,
         err = "cannot raise the GEMM kernel's shared-memory limit";
         return QW_ERR_CUDA;
     }
-    GemmArgs args{y, M, N, K, ldy, err_word};
-    dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
+    GemmArgs args{y, M, N, K, ldy, err_word, (long long)M * ldy};
+    dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, ksplit);
     gemm_bf16x2_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(mh, ml, mb, args);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
@@ -108,6 +110,13 @@ int gemm(const uint16_t* a_hi, const uint16_t* a_lo, int lda, const uint16_t* b,
 namespace pf {
 
 constexpr int ROW_THREADS = 256;
+
+// K splits for an [M x N] x K GEMM whose output tiles alone would leave most SMs idle (o_proj and
+// down_proj, N = hidden): enough splits to come near one CTA per SM, at most KSPLIT_MAX and K / 64.
+int ksplit_for(int M, int N, int K) {
+    const int tiles = ((M + 127) / 128) * ((N + 127) / 128);
+    return std::max(1, std::min({148 / tiles, KSPLIT_MAX, K / 64}));
+}
 
 __device__ __forceinline__ float bf16f(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
 
@@ -134,14 +143,21 @@ __device__ float block_sum256(float v, float* red) {
     return t;
 }
 
-// A_hi/A_lo[t] = split(rmsnorm(X[t]) * gain) (cpu_inference.rs:189-194)
-__global__ void __launch_bounds__(ROW_THREADS) norm_split(const float* X, int H, const uint16_t* gain, float eps, uint16_t* hi,
-                                                          uint16_t* lo) {
+// X[t] += the nparts split-K slices of the previous projection (residual add, cpu_inference.rs:
+// 163-164, :171-172; slices summed in order), then A_hi/A_lo[t] = split(rmsnorm(X[t]) * gain)
+// (cpu_inference.rs:189-194)
+__global__ void __launch_bounds__(ROW_THREADS) norm_split(float* X, int H, const uint16_t* gain, float eps, uint16_t* hi,
+                                                          uint16_t* lo, const float* parts, int nparts, size_t part_stride) {
     __shared__ float red[ROW_THREADS / 32];
     const int t = blockIdx.x;
-    const float* x = X + (size_t)t * H;
+    float* x = X + (size_t)t * H;
     float ss = 0.f;
-    for (int i = threadIdx.x; i < H; i += ROW_THREADS) ss = fmaf(x[i], x[i], ss);
+    for (int i = threadIdx.x; i < H; i += ROW_THREADS) {
+        float v = x[i];
+        for (int z = 0; z < nparts; z++) v += parts[z * part_stride + (size_t)t * H + i];
+        if (nparts) x[i] = v;
+        ss = fmaf(v, v, ss);
+    }
     const float sc = rsqrtf(block_sum256(ss, red) / (float)H + eps);
     for (int i = threadIdx.x; i < H; i += ROW_THREADS) split_store(x[i] * sc * bf16f(gain[i]), hi, lo, (size_t)t * H + i);
 }
@@ -152,10 +168,13 @@ __global__ void split_rows(const float* src, size_t total, uint16_t* hi, uint16_
         split_store(src[i], hi, lo, i);
 }
 
-// X += Y (cpu_inference.rs:163-164, :171-172)
-__global__ void residual_add(float* X, const float* Y, size_t total) {
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x)
-        X[i] += Y[i];
+// X += the nparts slices of Y, in order (cpu_inference.rs:171-172)
+__global__ void residual_add(float* X, const float* Y, size_t total, int nparts) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        float v = X[i];
+        for (int z = 0; z < nparts; z++) v += Y[z * total + i];
+        X[i] = v;
+    }
 }
 
 // h[t][i] = silu(gate) * up from the interleaved gate/up outputs Y[t][2i], Y[t][2i+1], split for
@@ -208,9 +227,39 @@ __global__ void qkv_post(const float* Y, int n, int start, int NQ, int NKV, cons
 // shared memory; per chunk every thread computes a 4 x 4 block of scores (rows x positions), the
 // row groups update their running max / sum, and every thread adds P . V into a 4-row x 8-dim
 // block of outputs. Positions after a row's own position are masked (causal).
+//
+// Causal tiles carry unequal work (the last tile reads every position, the first one chunk), so a
+// tile that needs more than CMAX chunks is split over several CTAs by position range; each split
+// writes its unnormalised output and running max / sum to a partial slot, and attention_merge
+// combines the splits of a tile in split order. Work items are numbered longest tiles first.
 constexpr int PC = 64;                 // positions per chunk
+constexpr int CMAX = 4;                // most chunks one CTA processes
 constexpr int AT_THREADS = 256;
 constexpr int KPAD = 132;              // K row pitch in floats (bank spread for the score loads)
+constexpr int PPITCH = 132;            // partial row: 128 output dims, running max, running sum, pad
+
+// chunks tile `tile` (QT query tokens) reads: positions 0 .. its last token's position
+__host__ __device__ inline int tile_chunks(int tile, int QT, int n, int start) {
+    const int last = start + min(QT * (tile + 1), n) - 1;
+    return last / PC + 1;
+}
+__host__ __device__ inline int tile_splits(int tile, int QT, int n, int start) {
+    return (tile_chunks(tile, QT, n, start) + CMAX - 1) / CMAX;
+}
+
+// work items and partial slots of one KV head: tiles from the last down, each as its splits
+struct AttPlan {
+    int items = 0, slots = 0;  // CTAs per KV head; partial slots per KV head (split tiles only)
+};
+inline AttPlan att_plan(int QT, int n, int start) {
+    AttPlan pl;
+    for (int t = (n + QT - 1) / QT - 1; t >= 0; t--) {
+        const int sp = tile_splits(t, QT, n, start);
+        pl.items += sp;
+        if (sp > 1) pl.slots += sp;
+    }
+    return pl;
+}
 
 // query tokens per CTA: 64 query rows for 1 or 2 query heads per KV head, 48 for 3
 template <int G>
@@ -231,14 +280,28 @@ struct AttSmem {
 
 template <int G>
 __global__ void __launch_bounds__(AT_THREADS) attention(const float* Q, float* att, const float* Kc, const float* Vc, int n,
-                                                        int start, int NQ, size_t head_stride_l, int max_seq, float scale) {
+                                                        int start, int NQ, size_t head_stride_l, int max_seq, float scale,
+                                                        float* part, int slots) {
     constexpr int QT = AttTile<G>::QT;
     constexpr int R = QT * G;           // query rows of the tile
     constexpr int RB = R / 4;           // row blocks of 4
     static_assert(R % 4 == 0 && RB * 16 <= AT_THREADS, "row blocks x 16 must fit the CTA");
     extern __shared__ __align__(16) uint8_t att_raw[];
     AttSmem<G>& sm = *reinterpret_cast<AttSmem<G>*>(att_raw);
-    const int g = blockIdx.y, t0 = blockIdx.x * QT;
+    const int g = blockIdx.y;
+    // work item blockIdx.x -> (tile, split); slot = partial slot of a split tile (-1: write att)
+    int tile = (n + QT - 1) / QT - 1, item = blockIdx.x, slot = 0, nsp = 1;
+    for (; tile >= 0; tile--) {
+        nsp = tile_splits(tile, QT, n, start);
+        if (item < nsp) break;
+        item -= nsp;
+        if (nsp > 1) slot += nsp;
+    }
+    if (tile < 0) return;  // (the grid holds exactly the plan's items)
+    slot = nsp > 1 ? slot + item : -1;
+    const int nch = tile_chunks(tile, QT, n, start);
+    const int c_begin = nch * item / nsp, c_end = nch * (item + 1) / nsp;
+    const int t0 = tile * QT;
     const int tid = threadIdx.x;
     const int ntok = min(QT, n - t0);
     // query rows: row r = token (r / G) of the tile, head g*G + r % G
@@ -262,8 +325,8 @@ __global__ void __launch_bounds__(AT_THREADS) attention(const float* Q, float* a
     }
     const float* kb = Kc + head_stride_l + (size_t)g * max_seq * 128;
     const float* vb = Vc + head_stride_l + (size_t)g * max_seq * 128;
-    const int last = start + t0 + ntok - 1;  // the tile's last position
-    for (int p0 = 0; p0 <= last; p0 += PC) {
+    const int last = min(start + t0 + ntok - 1, c_end * PC - 1);  // this item's last position
+    for (int p0 = c_begin * PC; p0 <= last; p0 += PC) {
         const int np = min(PC, last + 1 - p0);
         __syncthreads();
         for (int i = tid; i < PC * 32; i += AT_THREADS) {
@@ -355,6 +418,21 @@ __global__ void __launch_bounds__(AT_THREADS) attention(const float* Q, float* a
         }
     }
     if (!active) return;
+    if (slot >= 0) {
+        // partial: unnormalised output rows plus (running max, sum) for attention_merge
+        float* po = part + ((size_t)g * slots + slot) * R * PPITCH;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            float* dst = po + (size_t)(4 * rb + i) * PPITCH;
+            reinterpret_cast<float4*>(dst + 8 * pb)[0] = make_float4(o[i][0], o[i][1], o[i][2], o[i][3]);
+            reinterpret_cast<float4*>(dst + 8 * pb)[1] = make_float4(o[i][4], o[i][5], o[i][6], o[i][7]);
+            if (pb == 0) {
+                dst[128] = m_run[i];
+                dst[129] = l_run[i];
+            }
+        }
+        return;
+    }
     // the row sums live with the score threads of the same row block (identical in all 16)
 #pragma unroll
     for (int i = 0; i < 4; i++) {
@@ -367,14 +445,68 @@ __global__ void __launch_bounds__(AT_THREADS) attention(const float* Q, float* a
     }
 }
 
+// Combines the splits of each split tile: per row, M = max of the splits' running maxima, then
+// out = sum_j o_j e^(m_j - M) / sum_j l_j e^(m_j - M), splits in order. Grid (split tiles, KV heads,
+// row groups of 4); warp w takes row 4 * blockIdx.z + w, lane the dims 4 lane .. 4 lane + 3.
+template <int G>
+__global__ void __launch_bounds__(128) attention_merge(float* att, const float* part, int n, int start, int NQ, int slots) {
+    constexpr int QT = AttTile<G>::QT, R = QT * G;
+    const int g = blockIdx.y, lane = threadIdx.x & 31, r = blockIdx.z * 4 + (threadIdx.x >> 5);
+    int tile = (n + QT - 1) / QT - 1, slot = 0, k = blockIdx.x, nsp = 1;
+    for (; tile >= 0; tile--) {
+        nsp = tile_splits(tile, QT, n, start);
+        if (nsp > 1) {
+            if (k == 0) break;
+            k--;
+            slot += nsp;
+        }
+    }
+    if (tile < 0) return;
+    const int t0 = tile * QT, ntok = min(QT, n - t0);
+    const int tl = r / G, h = r % G;
+    if (tl >= ntok) return;
+    const float* po = part + ((size_t)g * slots + slot) * R * PPITCH;
+    float M = -INFINITY;
+    for (int j = 0; j < nsp; j++) M = fmaxf(M, po[((size_t)j * R + r) * PPITCH + 128]);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float l = 0.f;
+    for (int j = 0; j < nsp; j++) {
+        const float* pr = po + ((size_t)j * R + r) * PPITCH;
+        const float mj = pr[128];
+        const float w = mj == -INFINITY ? 0.f : __expf(mj - M);
+        const float4 v = reinterpret_cast<const float4*>(pr)[lane];
+        acc.x = fmaf(v.x, w, acc.x);
+        acc.y = fmaf(v.y, w, acc.y);
+        acc.z = fmaf(v.z, w, acc.z);
+        acc.w = fmaf(v.w, w, acc.w);
+        l = fmaf(pr[129], w, l);
+    }
+    const float inv = 1.0f / l;
+    reinterpret_cast<float4*>(att + (size_t)(t0 + tl) * NQ * 128 + (size_t)(g * G + h) * 128)[lane] =
+        make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+}
+
 template <int G>
 int launch_attention(const float* Q, float* att, const float* Kc, const float* Vc, int n, int start, int NQ, int NKV,
-                     size_t hsl, int max_seq, float scale, cudaStream_t s) {
+                     size_t hsl, int max_seq, float scale, float* part, size_t part_cap, cudaStream_t s) {
     const int smem = (int)sizeof(AttSmem<G>);
     if (cudaFuncSetAttribute(attention<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return QW_ERR_CUDA;
-    dim3 grid((n + AttTile<G>::QT - 1) / AttTile<G>::QT, NKV);
-    attention<G><<<grid, AT_THREADS, smem, s>>>(Q, att, Kc, Vc, n, start, NQ, hsl, max_seq, scale);
+    const AttPlan pl = att_plan(AttTile<G>::QT, n, start);
+    if ((size_t)NKV * pl.slots * AttTile<G>::QT * G * PPITCH > part_cap) return QW_ERR_ARG;
+    attention<G><<<dim3(pl.items, NKV), AT_THREADS, smem, s>>>(Q, att, Kc, Vc, n, start, NQ, hsl, max_seq, scale, part,
+                                                                 pl.slots);
+    int split_tiles = 0;
+    for (int t = (n + AttTile<G>::QT - 1) / AttTile<G>::QT - 1; t >= 0; t--)
+        split_tiles += tile_splits(t, AttTile<G>::QT, n, start) > 1;
+    if (split_tiles)
+        attention_merge<G><<<dim3(split_tiles, NKV, AttTile<G>::QT * G / 4), 128, 0, s>>>(att, part, n, start, NQ, pl.slots);
     return QW_OK;
+}
+
+// floats of attention partials a pass over n tokens from `start` needs (G = query heads per KV head)
+size_t attention_partial_floats(int n, int start, int NQ, int NKV) {
+    const int G = NQ / NKV, QT = G == 1 ? AttTile<1>::QT : G == 2 ? AttTile<2>::QT : AttTile<3>::QT;
+    return (size_t)NKV * att_plan(QT, n, start).slots * QT * G * PPITCH;
 }
 
 int grid_for(size_t total) { return (int)std::min<size_t>((total + 255) / 256, 148 * 8); }
@@ -386,43 +518,47 @@ int run(const Weights& w, const CacheView& c, const uint32_t* d_ids, int n, int 
     embed_rows<<<n, 256, 0, s>>>(d_ids, H, w.embed, sc.X);
     const int G = NQ / NKV;
     const float scale = 1.0f / sqrtf(128.0f);
+    const int ks_o = ksplit_for(n, H, QD), ks_d = ksplit_for(n, H, I);
     for (int l = 0; l < w.L; l++) {
         const uint16_t* W = w.layer_w + (size_t)l * w.layer_stride;
         const uint16_t* nrm = w.layer_n + (size_t)l * w.norm_stride;
         const size_t hsl = (size_t)l * NKV * c.max_seq * 128;
         int rc;
         // A: rmsnorm -> q|k|v
-        norm_split<<<n, ROW_THREADS, 0, s>>>(sc.X, H, nrm, w.eps, sc.ahi, sc.alo);
-        if ((rc = tc::gemm(sc.ahi, sc.alo, H, W, H, sc.Y, QKVR, n, QKVR, H, err_word, s, err))) return rc;
+        // (the previous layer's down_proj slices are added into X here)
+        norm_split<<<n, ROW_THREADS, 0, s>>>(sc.X, H, nrm, w.eps, sc.ahi, sc.alo, sc.Y, l == 0 ? 0 : ks_d, nH);
+        if ((rc = tc::gemm(sc.ahi, sc.alo, H, W, H, sc.Y, QKVR, n, QKVR, H, err_word, s, err, 1))) return rc;
         // B: q/k norm + RoPE, K/V into the cache, causal attention
         const int items = n * (NQ + 2 * NKV);
         qkv_post<<<(items + 7) / 8, 256, 0, s>>>(sc.Y, n, start, NQ, NKV, nrm + 2 * H, nrm + 2 * H + 128, w.eps, c.rope, sc.Q,
                                                  c.k, c.v, hsl, c.max_seq);
-        rc = G == 1 ? launch_attention<1>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, s)
-           : G == 2 ? launch_attention<2>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, s)
-                    : launch_attention<3>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, s);
+        rc = G == 1 ? launch_attention<1>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, sc.attp, sc.attp_cap, s)
+           : G == 2 ? launch_attention<2>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, sc.attp, sc.attp_cap, s)
+                    : launch_attention<3>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, sc.attp, sc.attp_cap, s);
         if (rc) {
-            err = "cannot raise the prefill attention kernel's shared-memory limit";
+            err = rc == QW_ERR_ARG ? "prefill attention partial buffer too small"
+                                   : "cannot raise the prefill attention kernel's shared-memory limit";
             return rc;
         }
         // C: o_proj + residual
         split_rows<<<grid_for((size_t)n * QD), 256, 0, s>>>(sc.att, (size_t)n * QD, sc.ahi, sc.alo);
-        if ((rc = tc::gemm(sc.ahi, sc.alo, QD, W + (size_t)QKVR * H, QD, sc.Y, H, n, H, QD, err_word, s, err))) return rc;
-        residual_add<<<grid_for(nH), 256, 0, s>>>(sc.X, sc.Y, nH);
-        // D: rmsnorm -> gate|up -> silu(gate) * up
-        norm_split<<<n, ROW_THREADS, 0, s>>>(sc.X, H, nrm + H, w.eps, sc.ahi, sc.alo);
+        if ((rc = tc::gemm(sc.ahi, sc.alo, QD, W + (size_t)QKVR * H, QD, sc.Y, H, n, H, QD, err_word, s, err, ks_o))) return rc;
+        // D: residual (the o_proj slices) + rmsnorm -> gate|up -> silu(gate) * up
+        norm_split<<<n, ROW_THREADS, 0, s>>>(sc.X, H, nrm + H, w.eps, sc.ahi, sc.alo, sc.Y, ks_o, nH);
         const uint16_t* Wgu = W + (size_t)QKVR * H + (size_t)H * QD;
-        if ((rc = tc::gemm(sc.ahi, sc.alo, H, Wgu, H, sc.Y, 2 * I, n, 2 * I, H, err_word, s, err))) return rc;
+        if ((rc = tc::gemm(sc.ahi, sc.alo, H, Wgu, H, sc.Y, 2 * I, n, 2 * I, H, err_word, s, err, 1))) return rc;
         silu_split<<<grid_for((size_t)n * I), 256, 0, s>>>(sc.Y, (size_t)n * I, sc.ahi, sc.alo);
         // E: down + residual
         const uint16_t* Wd = Wgu + (size_t)2 * I * H;
-        if ((rc = tc::gemm(sc.ahi, sc.alo, I, Wd, I, sc.Y, H, n, H, I, err_word, s, err))) return rc;
-        residual_add<<<grid_for(nH), 256, 0, s>>>(sc.X, sc.Y, nH);
+        if ((rc = tc::gemm(sc.ahi, sc.alo, I, Wd, I, sc.Y, H, n, H, I, err_word, s, err, ks_d))) return rc;
     }
+    // the last down_proj's slices go into X with the final norm; without logits, add them alone
     if (d_logits) {
-        norm_split<<<n, ROW_THREADS, 0, s>>>(sc.X, H, w.final_norm, w.eps, sc.ahi, sc.alo);
+        norm_split<<<n, ROW_THREADS, 0, s>>>(sc.X, H, w.final_norm, w.eps, sc.ahi, sc.alo, sc.Y, ks_d, nH);
         int rc;
-        if ((rc = tc::gemm(sc.ahi, sc.alo, H, w.lm_head, H, d_logits, w.V, n, w.V, H, err_word, s, err))) return rc;
+        if ((rc = tc::gemm(sc.ahi, sc.alo, H, w.lm_head, H, d_logits, w.V, n, w.V, H, err_word, s, err, 1))) return rc;
+    } else {
+        residual_add<<<grid_for(nH), 256, 0, s>>>(sc.X, sc.Y, nH, ks_d);
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
@@ -448,7 +584,7 @@ int qw_gemm_bf16x2(int device, const uint16_t* d_a_hi, const uint16_t* d_a_lo, c
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (cudaMemsetAsync(ew, 0, sizeof(int), s) != cudaSuccess) return set_error(QW_ERR_CUDA, "error word reset failed");
     std::string err;
-    int rc = tc::gemm(d_a_hi, d_a_lo, (int)K, d_b, (int)K, d_y, (int)N, (int)M, (int)N, (int)K, ew, s, err);
+    int rc = tc::gemm(d_a_hi, d_a_lo, (int)K, d_b, (int)K, d_y, (int)N, (int)M, (int)N, (int)K, ew, s, err, 1);
     if (rc) return set_error(rc, err.c_str());
     int h = 0;
     if (cudaMemcpyAsync(&h, ew, sizeof(int), cudaMemcpyDeviceToHost, s) != cudaSuccess || cudaStreamSynchronize(s) != cudaSuccess)

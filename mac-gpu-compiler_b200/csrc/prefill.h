@@ -30,16 +30,24 @@ struct CacheView {
     int max_seq;
 };
 
+// most K splits of one GEMM; each split writes its own [n][H] slice of Scratch::Y
+constexpr int KSPLIT_MAX = 4;
+
 // device scratch for n tokens
 struct Scratch {
     float* X = nullptr;        // [n][H] residual stream
-    float* Y = nullptr;        // [n][max(QKVR, 2I)] GEMM outputs
+    float* Y = nullptr;        // [n][max(QKVR, 2I, KSPLIT_MAX * H)] GEMM outputs
     float* Q = nullptr;        // [n][QD] normed, rotated queries
     float* att = nullptr;      // [n][QD] attention outputs
     uint16_t* ahi = nullptr;   // [n][max(H, QD, I)] GEMM input, high bf16 halves
     uint16_t* alo = nullptr;   // ... low halves
     int cap = 0;               // tokens the buffers hold
+    float* attp = nullptr;     // attention partials of split query tiles
+    size_t attp_cap = 0;       // floats attp holds
 };
+
+// floats of attention partials a pass over n tokens from position `start` needs
+size_t attention_partial_floats(int n, int start, int NQ, int NKV);
 
 // One forward pass over n tokens d_ids (device) at positions start .. start+n-1: writes their K/V
 // into the cache and, with d_logits ([n][V] device), every position's logits. Stream-ordered.

@@ -116,10 +116,11 @@ __device__ __forceinline__ bool bounded_wait(uint64_t* bar, uint32_t parity, vol
 }
 
 struct GemmArgs {
-    float* y;          // [M][ldy] f32 output
+    float* y;          // [M][ldy] f32 output; split z writes y + z * split_stride
     int M, N, K;
     int ldy;
     int* err;          // kernel error word (nonzero: a wait ran out)
+    long long split_stride;  // elements between the outputs of K splits (blockIdx.z)
 };
 
 __global__ void __launch_bounds__(THREADS, 1)
@@ -133,7 +134,11 @@ gemm_bf16x2_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_con
     uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
-    const int nkb = args.K / BK;
+    // split-K: CTA z of gridDim.z covers K blocks [kb0, kb0 + nkb) and writes its own output slice
+    const int nkb_all = args.K / BK;
+    const int kb0 = (int)((long long)nkb_all * blockIdx.z / gridDim.z);
+    const int nkb = (int)((long long)nkb_all * (blockIdx.z + 1) / gridDim.z) - kb0;
+    float* const y = args.y + (long long)blockIdx.z * args.split_stride;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
@@ -162,9 +167,9 @@ gemm_bf16x2_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_con
             if (kb >= STAGES && !bounded_wait(&empty[s], ((kb / STAGES) - 1) & 1, &abort_flag)) break;
             uint8_t* st = ring + s * STAGE_BYTES;
             mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-            tma_load_2d(st, &map_ahi, kb * BK, m0, &full[s]);
-            tma_load_2d(st + TILE_A, &map_alo, kb * BK, m0, &full[s]);
-            tma_load_2d(st + 2 * TILE_A, &map_b, kb * BK, n0, &full[s]);
+            tma_load_2d(st, &map_ahi, (kb0 + kb) * BK, m0, &full[s]);
+            tma_load_2d(st + TILE_A, &map_alo, (kb0 + kb) * BK, m0, &full[s]);
+            tma_load_2d(st + 2 * TILE_A, &map_b, (kb0 + kb) * BK, n0, &full[s]);
             issued_kb = kb + 1;
         }
     } else if (warp == 1 && lane == 0) {
@@ -195,7 +200,7 @@ gemm_bf16x2_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_con
             uint32_t r[32];
             tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, r);
             if (row < args.M && n0 + c < args.N) {
-                float* dst = args.y + (size_t)row * args.ldy + n0 + c;
+                float* dst = y + (size_t)row * args.ldy + n0 + c;
                 const int nv = args.N - (n0 + c) < 32 ? args.N - (n0 + c) : 32;
                 // float4 stores only where the row is 16-byte aligned (ldy need not be a multiple of 4,
                 // e.g. an odd vocabulary size)

@@ -24,7 +24,9 @@ def _need_gpu():
         pytest.skip("no CUDA device")
 
 
-@pytest.mark.parametrize("geometry,n", [("tiny", 40), ("mid", 130), ("qwen3-0.6b", 64)])
+# n = 300 and 600 reach query tiles whose positions span more than one attention split (256
+# positions), so those cases also check the split merge
+@pytest.mark.parametrize("geometry,n", [("tiny", 40), ("mid", 130), ("qwen3-0.6b", 64), ("mid", 300), ("tiny", 600)])
 def test_prefill_matches_token_by_token_oracle(geometry, n):
     path = randmodel.make_model(geometry, 0)
     om = co.Model.load_model(path)
@@ -63,6 +65,18 @@ def test_prefill_continues_an_existing_cache(mid_model_path):
     m.prefill(ids[:20], 0, c2, logits=False)
     tail = m.prefill(ids[20:], 20, c2)
     assert np.abs(tail - whole[20:]).max() <= 1e-4
+
+
+def test_prefill_continuation_across_attention_splits(mid_model_path):
+    # the second call's tiles start at position 40 and read up to 330 positions, split differently
+    # from the single call's: only the summation order of the softmax differs
+    m = ci.CudaModel.load_model(mid_model_path)
+    ids = randmodel.prompt_ids(330, m.config.vocab_size, seed=9)
+    c1, c2 = ci.CudaKVCache(m, 336), ci.CudaKVCache(m, 336)
+    whole = m.prefill(ids, 0, c1)
+    m.prefill(ids[:40], 0, c2, logits=False)
+    tail = m.prefill(ids[40:], 40, c2)
+    assert np.abs(tail - whole[40:]).max() <= 1e-4
 
 
 def test_prefill_argument_errors(tiny_model_path):
