@@ -95,6 +95,30 @@ int qw_prefill(qw_model* model, qw_cache* cache, const uint32_t* ids, size_t n, 
 int qw_prefill_device(qw_model* model, qw_cache* cache, const uint32_t* d_ids, size_t n, size_t start_pos,
                       float* d_logits, void* stream);
 
+/* Batch decode (its per-GPU batch-8 variant): B independent sequences, each
+ * with its own cache, advance one token per step together, so each step streams the weights once
+ * for all B (the reference decodes one sequence per engine, metal_inference.rs:286-387). Every
+ * projection is a tcgen05 GEMM over the B rows; attention runs per row over the row's own cache.
+ * 1 <= B <= QW_BATCH_MAX; the caches must be distinct and belong to `model`.
+ *
+ * qw_forward_batch: row b feeds tokens[b] at positions[b] into caches[b] (forward() for each row,
+ * metal_inference.rs:286); logits_out is B * vocab_size floats, row b at b * vocab_size. Synchronous.
+ *
+ * qw_decode_batch: decode() for each row (metal_inference.rs:297): firsts[b] goes in at
+ * start_pos[b], each step's argmax feeds the row's next step, and tokens_out[b * steps + i] receives
+ * row b's i-th output token. One step is captured once as a CUDA graph and replayed. Synchronous.
+ *
+ * qw_decode_batch_device: the same with device first tokens (d_firsts[B]) and a device token
+ * record d_out[steps * B] in step-major order (d_out[i * B + b]), stream-ordered on `stream`
+ * (NULL = the model's stream) without synchronisation; start_pos stays a host array. */
+#define QW_BATCH_MAX 16
+int qw_forward_batch(qw_model* model, qw_cache* const* caches, size_t B, const uint32_t* tokens, const size_t* positions,
+                     float* logits_out);
+int qw_decode_batch(qw_model* model, qw_cache* const* caches, size_t B, const uint32_t* firsts, const size_t* start_pos,
+                    size_t steps, uint32_t* tokens_out);
+int qw_decode_batch_device(qw_model* model, qw_cache* const* caches, size_t B, const uint32_t* d_firsts,
+                           const size_t* start_pos, size_t steps, uint32_t* d_out, void* stream);
+
 /* MetalModel::decode (metal_inference.rs:297-316): greedy decode; `first` goes in at `start_pos`,
  * each step's argmax feeds the next, and on_token(user, t) is called with each step's output
  * token as soon as the GPU produces it (steps calls). The whole run is one kernel launch. */

@@ -151,6 +151,15 @@ struct qw_model {
     uint32_t* d_pf_ids = nullptr;
     float* d_pf_logits = nullptr;
     size_t pf_logits_cap = 0;    // tokens d_pf_logits holds
+    // batch decode (row mode): row views, current tokens, the [steps][B] token record, and the
+    // captured graph of one step with the configuration it was captured for
+    qw::pf::RowView* d_rows = nullptr;   // [ROWS_MAX]
+    uint32_t* d_btok = nullptr;          // [ROWS_MAX]
+    uint32_t* d_bout = nullptr;
+    size_t bout_cap = 0;                 // entries of d_bout
+    cudaGraphExec_t bgraph = nullptr;
+    struct { int B = 0, splits = 0; const void *X = nullptr, *Y = nullptr, *attp = nullptr, *logits = nullptr, *out = nullptr;
+             cudaStream_t stream = nullptr; } bsig;
     unsigned epoch = 0;
     int S = 0, part_cap = 0, xs_cap = 0, xloc_cap = 0;
     u64* d_trace = nullptr;      // phase timeline of the most recent launch's first step, if enabled
@@ -442,6 +451,10 @@ void qw_free(qw_model* m) {
     cudaFree(m->pf.ahi);
     cudaFree(m->pf.alo);
     cudaFree(m->pf.attp);
+    if (m->bgraph) cudaGraphExecDestroy(m->bgraph);
+    cudaFree(m->d_rows);
+    cudaFree(m->d_btok);
+    cudaFree(m->d_bout);
     cudaFree(m->d_pf_ids);
     cudaFree(m->d_pf_logits);
     if (m->h_tok) cudaFreeHost(m->h_tok);
@@ -549,32 +562,43 @@ size_t qw_cache_max_seq(const qw_cache* c) { return c ? c->max_seq : 0; }
 namespace {
 
 // grow the prefill scratch to hold n tokens (and, with logits, n rows of logits)
-int ensure_prefill(qw_model* m, size_t n, size_t start, bool logits) {
+int ensure_prefill(qw_model* m, size_t n, size_t start, bool logits, size_t row_attp = 0) {
     const ModelConfig& c = m->cfg;
-    const size_t H = c.hidden, I = c.inter, QD = c.heads * c.head_dim, KVD = c.kv_heads * c.head_dim;
-    const size_t QKVR = QD + 2 * KVD;
+    const size_t H = c.hidden, I = c.inter, QD = c.heads * c.head_dim;
     if ((int)n > m->pf.cap) {
         const size_t cap = std::max<size_t>(n, 2 * (size_t)m->pf.cap);
         qw::pf::Scratch sc;
-        const size_t ycols = std::max({QKVR, 2 * I, (size_t)qw::pf::KSPLIT_MAX * H}), acols = std::max({H, QD, I});
-        bool ok = cudaMalloc(&sc.X, cap * H * 4) == cudaSuccess && cudaMalloc(&sc.Y, cap * ycols * 4) == cudaSuccess &&
+        const size_t acols = std::max({H, QD, I});
+        bool ok = cudaMalloc(&sc.X, cap * H * 4) == cudaSuccess &&
                   cudaMalloc(&sc.Q, cap * QD * 4) == cudaSuccess && cudaMalloc(&sc.att, cap * QD * 4) == cudaSuccess &&
                   cudaMalloc(&sc.ahi, cap * acols * 2) == cudaSuccess && cudaMalloc(&sc.alo, cap * acols * 2) == cudaSuccess;
         uint32_t* ids = nullptr;
         ok = ok && cudaMalloc(&ids, cap * 4) == cudaSuccess;
         if (!ok) {
-            cudaFree(sc.X); cudaFree(sc.Y); cudaFree(sc.Q); cudaFree(sc.att); cudaFree(sc.ahi); cudaFree(sc.alo); cudaFree(ids);
+            cudaFree(sc.X); cudaFree(sc.Q); cudaFree(sc.att); cudaFree(sc.ahi); cudaFree(sc.alo); cudaFree(ids);
             return set_err(QW_ERR_NOMEM, "prefill scratch allocation failed");
         }
-        cudaFree(m->pf.X); cudaFree(m->pf.Y); cudaFree(m->pf.Q); cudaFree(m->pf.att); cudaFree(m->pf.ahi); cudaFree(m->pf.alo);
+        cudaFree(m->pf.X); cudaFree(m->pf.Q); cudaFree(m->pf.att); cudaFree(m->pf.ahi); cudaFree(m->pf.alo);
         cudaFree(m->d_pf_ids);
         sc.cap = (int)cap;
+        sc.Y = m->pf.Y;
+        sc.ycap = m->pf.ycap;
         sc.attp = m->pf.attp;
         sc.attp_cap = m->pf.attp_cap;
         m->pf = sc;
         m->d_pf_ids = ids;
     }
-    const size_t attp = qw::pf::attention_partial_floats((int)n, (int)start, (int)c.heads, (int)c.kv_heads);
+    const size_t ycap = qw::pf::y_floats((int)n, (int)H, (int)I, (int)c.heads, (int)c.kv_heads);
+    if (ycap > m->pf.ycap) {
+        float* d = nullptr;
+        const size_t cap = std::max(ycap, 2 * m->pf.ycap);
+        if (cudaMalloc(&d, cap * 4) != cudaSuccess) return set_err(QW_ERR_NOMEM, "prefill GEMM scratch allocation failed");
+        cudaFree(m->pf.Y);
+        m->pf.Y = d;
+        m->pf.ycap = cap;
+    }
+    const size_t attp = std::max(qw::pf::attention_partial_floats((int)n, (int)start, (int)c.heads, (int)c.kv_heads),
+                                 row_attp);
     if (attp > m->pf.attp_cap) {
         float* d = nullptr;
         const size_t cap = std::max(attp, 2 * m->pf.attp_cap);
@@ -641,6 +665,170 @@ int qw_prefill_device(qw_model* m, qw_cache* c, const uint32_t* d_ids, size_t n,
     std::string err;
     if (int e = qw::pf::run(w, cv, d_ids, (int)n, (int)start_pos, d_logits, m->pf, ew, s, err)) return set_err(e, err);
     return QW_OK;
+}
+
+namespace {
+
+// Row views of a batch over `caches` (distinct, all of model m) with rows at pos[b], each
+// running `steps` steps from there.
+int batch_rows(qw_model* m, qw_cache* const* caches, size_t B, const size_t* pos, size_t steps,
+               std::vector<qw::pf::RowView>& rows, int& splits) {
+    if (!caches || !pos || B == 0 || B > (size_t)qw::pf::ROWS_MAX)
+        return set_err(QW_ERR_ARG, "batch: 1 <= rows <= 16 caches and positions required");
+    rows.resize(B);
+    size_t last = 0;
+    for (size_t b = 0; b < B; b++) {
+        const qw_cache* c = caches[b];
+        if (!c || c->m != m || c->model_id != m->id) return set_err(QW_ERR_ARG, "batch: null or mismatched cache");
+        for (size_t j = 0; j < b; j++)
+            if (caches[j] == c) return set_err(QW_ERR_ARG, "batch: a cache appears twice");
+        if (pos[b] + steps > c->max_seq) return set_err(QW_ERR_ARG, "batch: position + steps exceeds the KV cache size");
+        rows[b] = qw::pf::RowView{c->d_k, c->d_v, c->d_rope, (int)c->max_seq, (int)pos[b], (int)pos[b], 0};
+        last = std::max(last, pos[b] + steps - 1);
+    }
+    splits = (int)(last / qw::pf::ROW_SPLIT + 1);
+    return QW_OK;
+}
+
+int ensure_batch(qw_model* m, size_t B, int splits, size_t out_entries) {
+    if (!m->d_rows) QW_CUDA(cudaMalloc(&m->d_rows, qw::pf::ROWS_MAX * sizeof(qw::pf::RowView)));
+    if (!m->d_btok) QW_CUDA(cudaMalloc(&m->d_btok, qw::pf::ROWS_MAX * 4));
+    if (out_entries > m->bout_cap) {
+        uint32_t* d = nullptr;
+        const size_t cap = std::max(out_entries, 2 * m->bout_cap);
+        if (cudaMalloc(&d, cap * 4) != cudaSuccess) return set_err(QW_ERR_NOMEM, "batch token record allocation failed");
+        cudaFree(m->d_bout);
+        m->d_bout = d;
+        m->bout_cap = cap;
+    }
+    return ensure_prefill(m, B, 0, true, qw::pf::row_partial_floats((int)B, (int)m->cfg.heads, splits));
+}
+
+qw::pf::Weights weights_of(const qw_model* m) {
+    const ModelConfig& cf = m->cfg;
+    return qw::pf::Weights{m->d_layer_w, m->d_layer_n, m->d_final_norm, m->d_embed, m->d_lm_head, m->layer_stride,
+                           m->norm_stride, (int)cf.hidden, (int)cf.inter, (int)cf.layers, (int)cf.heads,
+                           (int)cf.kv_heads, (int)cf.vocab, cf.eps};
+}
+
+// The graph of one greedy batch step (row-mode forward + argmax_rows into `out`), captured on the
+// model's stream the first time a configuration is used and replayed for every step after.
+int batch_graph(qw_model* m, int B, int splits, uint32_t* out, int* ew) {
+    auto& g = m->bsig;
+    if (m->bgraph && g.B == B && g.splits == splits && g.X == m->pf.X && g.Y == m->pf.Y && g.attp == m->pf.attp &&
+        g.logits == m->d_pf_logits && g.out == out)
+        return QW_OK;
+    if (m->bgraph) {
+        cudaGraphExecDestroy(m->bgraph);
+        m->bgraph = nullptr;
+    }
+    cudaStream_t s = m->stream;
+    QW_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    std::string err;
+    int rc = qw::pf::run_rows(weights_of(m), m->d_rows, B, splits, m->d_btok, m->d_pf_logits, m->pf, ew, s, err);
+    if (!rc) rc = qw::pf::argmax_rows(m->d_pf_logits, (int)m->cfg.vocab, B, m->d_rows, m->d_btok, out, s, err);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t ce = cudaStreamEndCapture(s, &graph);
+    if (rc) {
+        if (graph) cudaGraphDestroy(graph);
+        return set_err(rc, err);
+    }
+    if (ce != cudaSuccess) return cuda_err(ce, "cudaStreamEndCapture (batch step)");
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ie != cudaSuccess) return cuda_err(ie, "cudaGraphInstantiate (batch step)");
+    m->bgraph = exec;
+    g.B = B;
+    g.splits = splits;
+    g.X = m->pf.X;
+    g.Y = m->pf.Y;
+    g.attp = m->pf.attp;
+    g.logits = m->d_pf_logits;
+    g.out = out;
+    return QW_OK;
+}
+
+// stream-ordered batch decode: rows from host positions, first tokens already in m->d_btok
+int batch_decode_launch(qw_model* m, qw_cache* const* caches, size_t B, const size_t* start_pos, size_t steps,
+                        uint32_t* d_out, cudaStream_t s, bool out_is_record) {
+    std::vector<qw::pf::RowView> rows;
+    int splits = 0;
+    if (int e = batch_rows(m, caches, B, start_pos, steps, rows, splits)) return e;
+    if (int e = ensure_batch(m, B, splits, out_is_record ? steps * B : 0)) return e;
+    if (out_is_record) d_out = m->d_bout;
+    int* ew = qw::device_err_word_for(m->device);
+    if (!ew) return set_err(QW_ERR_NOMEM, "error word allocation failed");
+    if (int e = batch_graph(m, (int)B, splits, d_out, ew)) return e;
+    QW_CUDA(cudaMemsetAsync(ew, 0, sizeof(int), s));
+    QW_CUDA(cudaMemcpyAsync(m->d_rows, rows.data(), B * sizeof(qw::pf::RowView), cudaMemcpyHostToDevice, s));
+    for (size_t i = 0; i < steps; i++) QW_CUDA(cudaGraphLaunch(m->bgraph, s));
+    return QW_OK;
+}
+
+}  // namespace
+
+int qw_forward_batch(qw_model* m, qw_cache* const* caches, size_t B, const uint32_t* tokens, const size_t* positions,
+                     float* logits_out) {
+    if (!m || !tokens || !logits_out) return set_err(QW_ERR_ARG, "null argument");
+    for (size_t b = 0; b < B && b < (size_t)qw::pf::ROWS_MAX; b++)
+        if (tokens[b] >= m->cfg.vocab) return set_err(QW_ERR_ARG, "token id >= vocab_size");
+    QW_CUDA(cudaSetDevice(m->device));
+    std::vector<qw::pf::RowView> rows;
+    int splits = 0;
+    if (int e = batch_rows(m, caches, B, positions, 1, rows, splits)) return e;
+    if (int e = ensure_batch(m, B, splits, 0)) return e;
+    int* ew = qw::device_err_word_for(m->device);
+    if (!ew) return set_err(QW_ERR_NOMEM, "error word allocation failed");
+    cudaStream_t s = m->stream;
+    QW_CUDA(cudaMemsetAsync(ew, 0, sizeof(int), s));
+    QW_CUDA(cudaMemcpyAsync(m->d_rows, rows.data(), B * sizeof(qw::pf::RowView), cudaMemcpyHostToDevice, s));
+    QW_CUDA(cudaMemcpyAsync(m->d_btok, tokens, B * 4, cudaMemcpyHostToDevice, s));
+    std::string err;
+    if (int e = qw::pf::run_rows(weights_of(m), m->d_rows, (int)B, splits, m->d_btok, m->d_pf_logits, m->pf, ew, s, err))
+        return set_err(e, err);
+    QW_CUDA(cudaMemcpyAsync(logits_out, m->d_pf_logits, B * m->cfg.vocab * 4, cudaMemcpyDeviceToHost, s));
+    int h = 0;
+    QW_CUDA(cudaMemcpyAsync(&h, ew, sizeof(int), cudaMemcpyDeviceToHost, s));
+    QW_CUDA(cudaStreamSynchronize(s));
+    if (h) return set_err(QW_ERR_DEVICE_TIMEOUT, "forward_batch: a GEMM pipeline wait expired on the device");
+    return QW_OK;
+}
+
+int qw_decode_batch(qw_model* m, qw_cache* const* caches, size_t B, const uint32_t* firsts, const size_t* start_pos,
+                    size_t steps, uint32_t* tokens_out) {
+    if (!m || !firsts || !tokens_out) return set_err(QW_ERR_ARG, "null argument");
+    if (steps == 0) return QW_OK;
+    for (size_t b = 0; b < B && b < (size_t)qw::pf::ROWS_MAX; b++)
+        if (firsts[b] >= m->cfg.vocab) return set_err(QW_ERR_ARG, "token id >= vocab_size");
+    QW_CUDA(cudaSetDevice(m->device));
+    cudaStream_t s = m->stream;
+    if (B >= 1 && B <= (size_t)qw::pf::ROWS_MAX && !m->d_btok) QW_CUDA(cudaMalloc(&m->d_btok, qw::pf::ROWS_MAX * 4));
+    if (m->d_btok && B >= 1 && B <= (size_t)qw::pf::ROWS_MAX)
+        QW_CUDA(cudaMemcpyAsync(m->d_btok, firsts, B * 4, cudaMemcpyHostToDevice, s));
+    if (int e = batch_decode_launch(m, caches, B, start_pos, steps, nullptr, s, true)) return e;
+    std::vector<uint32_t> rec(steps * B);
+    QW_CUDA(cudaMemcpyAsync(rec.data(), m->d_bout, steps * B * 4, cudaMemcpyDeviceToHost, s));
+    int h = 0;
+    int* ew = qw::device_err_word_for(m->device);
+    QW_CUDA(cudaMemcpyAsync(&h, ew, sizeof(int), cudaMemcpyDeviceToHost, s));
+    QW_CUDA(cudaStreamSynchronize(s));
+    if (h) return set_err(QW_ERR_DEVICE_TIMEOUT, "decode_batch: a GEMM pipeline wait expired on the device");
+    for (size_t b = 0; b < B; b++)
+        for (size_t i = 0; i < steps; i++) tokens_out[b * steps + i] = rec[i * B + b];
+    return QW_OK;
+}
+
+int qw_decode_batch_device(qw_model* m, qw_cache* const* caches, size_t B, const uint32_t* d_firsts,
+                           const size_t* start_pos, size_t steps, uint32_t* d_out, void* stream) {
+    if (!m || !d_firsts || !d_out) return set_err(QW_ERR_ARG, "null argument");
+    if (steps == 0) return QW_OK;
+    QW_CUDA(cudaSetDevice(m->device));
+    cudaStream_t s = pick_stream(m, stream);
+    if (!m->d_btok) QW_CUDA(cudaMalloc(&m->d_btok, qw::pf::ROWS_MAX * 4));
+    if (B >= 1 && B <= (size_t)qw::pf::ROWS_MAX)
+        QW_CUDA(cudaMemcpyAsync(m->d_btok, d_firsts, B * 4, cudaMemcpyDeviceToDevice, s));
+    return batch_decode_launch(m, caches, B, start_pos, steps, d_out, s, false);
 }
 
 int qw_forward(qw_model* m, qw_cache* c, uint32_t token, size_t pos, float* logits_out) {

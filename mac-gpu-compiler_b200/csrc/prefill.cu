@@ -82,6 +82,24 @@ int gemm(const uint16_t* a_hi, const uint16_t* a_lo, int lda, const uint16_t* b,
     }
     CUtensorMap mh, ml, mb;
     int rc;
+    if (M <= SK_NB) {  // weights-bound: the swapped-operand kernel
+        if ((rc = make_map_bf16(&mh, a_hi, (uint64_t)M, (uint64_t)K, (uint64_t)lda, SK_NB, err))) return rc;
+        if ((rc = make_map_bf16(&ml, a_lo, (uint64_t)M, (uint64_t)K, (uint64_t)lda, SK_NB, err))) return rc;
+        if ((rc = make_map_bf16(&mb, b, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, BN, err))) return rc;
+        if (cudaFuncSetAttribute(gemm_skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM_BYTES) !=
+            cudaSuccess) {
+            err = "cannot raise the skinny GEMM kernel's shared-memory limit";
+            return QW_ERR_CUDA;
+        }
+        GemmArgs args{y, M, N, K, ldy, err_word, (long long)M * ldy};
+        gemm_skinny_kernel<<<dim3((N + BN - 1) / BN, 1, ksplit), THREADS, SK_SMEM_BYTES, s>>>(mh, ml, mb, args);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) {
+            err = std::string("GEMM launch failed: ") + cudaGetErrorString(e);
+            return QW_ERR_CUDA;
+        }
+        return QW_OK;
+    }
     if ((rc = make_map_bf16(&mh, a_hi, (uint64_t)M, (uint64_t)K, (uint64_t)lda, BM, err))) return rc;
     if ((rc = make_map_bf16(&ml, a_lo, (uint64_t)M, (uint64_t)K, (uint64_t)lda, BM, err))) return rc;
     if ((rc = make_map_bf16(&mb, b, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, BN, err))) return rc;
@@ -111,11 +129,16 @@ namespace pf {
 
 constexpr int ROW_THREADS = 256;
 
-// K splits for an [M x N] x K GEMM whose output tiles alone would leave most SMs idle (o_proj and
-// down_proj, N = hidden): enough splits to come near one CTA per SM, at most KSPLIT_MAX and K / 64.
 int ksplit_for(int M, int N, int K) {
     const int tiles = ((M + 127) / 128) * ((N + 127) / 128);
     return std::max(1, std::min({148 / tiles, KSPLIT_MAX, K / 64}));
+}
+
+size_t y_floats(int n, int H, int I, int NQ, int NKV) {
+    const int QD = NQ * 128, QKVR = QD + 2 * NKV * 128;
+    const size_t a = (size_t)ksplit_for(n, QKVR, H) * QKVR, b = (size_t)ksplit_for(n, H, QD) * H,
+                 c = (size_t)ksplit_for(n, 2 * I, H) * 2 * I, d = (size_t)ksplit_for(n, H, I) * H;
+    return (size_t)n * std::max({a, b, c, d});
 }
 
 __device__ __forceinline__ float bf16f(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
@@ -177,27 +200,54 @@ __global__ void residual_add(float* X, const float* Y, size_t total, int nparts)
     }
 }
 
-// h[t][i] = silu(gate) * up from the interleaved gate/up outputs Y[t][2i], Y[t][2i+1], split for
-// the down GEMM (cpu_inference.rs:166-170, :187)
-__global__ void silu_split(const float* Y, size_t n_inter, uint16_t* hi, uint16_t* lo) {
+// h[t][i] = silu(gate) * up from the interleaved gate/up outputs Y[t][2i], Y[t][2i+1] (the sum of
+// nparts split-K slices, in order), split for the down GEMM (cpu_inference.rs:166-170, :187)
+__global__ void silu_split(const float* Y, size_t n_inter, uint16_t* hi, uint16_t* lo, int nparts) {
+    const size_t ps = 2 * n_inter;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_inter; i += (size_t)gridDim.x * blockDim.x) {
-        const float g = Y[2 * i], u = Y[2 * i + 1];
+        float g = Y[2 * i], u = Y[2 * i + 1];
+        for (int z = 1; z < nparts; z++) {
+            g += Y[z * ps + 2 * i];
+            u += Y[z * ps + 2 * i + 1];
+        }
         split_store(g / (1.0f + __expf(-g)) * u, hi, lo, i);
     }
 }
 
-// Per token and head of the q|k|v outputs Y[t][QKVR]: q heads get q_norm + RoPE into Q[t][NQ*128];
-// k heads k_norm + RoPE and v heads as they are go into the cache at position start + t
-// (cpu_inference.rs:134-141, :196-215; the RoPE table is the decode path's). One warp per head.
-__global__ void qkv_post(const float* Y, int n, int start, int NQ, int NKV, const uint16_t* qn, const uint16_t* kn, float eps,
-                         const float2* rope, float* Q, float* Kc, float* Vc, size_t head_stride_l, int max_seq) {
+// Per token and head of the q|k|v outputs Y[t][QKVR] (the sum of nparts split-K slices, in order):
+// q heads get q_norm + RoPE into Q[t][NQ*128]; k heads k_norm + RoPE and v heads as they are go
+// into the cache (cpu_inference.rs:134-141, :196-215; the RoPE table is the decode path's). One
+// warp per head. Prefill: token t is at position start + t of cache `c`. Row mode (rows != null):
+// token t is row t, at rows[t].pos of its own cache.
+__global__ void qkv_post(const float* Y, int nparts, int n, int start, int NQ, int NKV, const uint16_t* qn,
+                         const uint16_t* kn, float eps, CacheView c, const RowView* rows, int layer, float* Q) {
     const int warps = blockDim.x >> 5;
     const int item = blockIdx.x * warps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     const int per_tok = NQ + 2 * NKV;
     if (item >= n * per_tok) return;
-    const int t = item / per_tok, hh = item - t * per_tok, pos = start + t;
+    const int t = item / per_tok, hh = item - t * per_tok;
+    int pos = start + t, max_seq = c.max_seq;
+    float *Kc = c.k, *Vc = c.v;
+    const float2* rope = c.rope;
+    if (rows) {
+        const RowView& rv = rows[t];
+        pos = rv.pos;
+        max_seq = rv.max_seq;
+        Kc = rv.k;
+        Vc = rv.v;
+        rope = rv.rope;
+    }
+    const size_t head_stride_l = (size_t)layer * NKV * max_seq * 128;
     const int QKVR = per_tok * 128;
-    const float4 v = reinterpret_cast<const float4*>(Y + (size_t)t * QKVR + (size_t)hh * 128)[lane];
+    const size_t ps = (size_t)n * QKVR;
+    float4 v = reinterpret_cast<const float4*>(Y + (size_t)t * QKVR + (size_t)hh * 128)[lane];
+    for (int z = 1; z < nparts; z++) {
+        const float4 w = reinterpret_cast<const float4*>(Y + z * ps + (size_t)t * QKVR + (size_t)hh * 128)[lane];
+        v.x += w.x;
+        v.y += w.y;
+        v.z += w.z;
+        v.w += w.w;
+    }
     if (hh >= NQ + NKV) {  // v head: straight into the cache
         const int g = hh - NQ - NKV;
         reinterpret_cast<float4*>(Vc + head_stride_l + ((size_t)g * max_seq + pos) * 128)[lane] = v;
@@ -511,44 +561,252 @@ size_t attention_partial_floats(int n, int start, int NQ, int NKV) {
 
 int grid_for(size_t total) { return (int)std::min<size_t>((total + 255) / 256, 148 * 8); }
 
-int run(const Weights& w, const CacheView& c, const uint32_t* d_ids, int n, int start, float* d_logits, Scratch& sc,
-        int* err_word, cudaStream_t s, std::string& err) {
+// ---------------------------------------------------------------------------------------------
+// Row mode (a decode batch): row b is one sequence's single token at its own position in its own
+// cache. Attention is per (row, KV head, split of ROW_SPLIT positions) — flash-decoding — and a
+// merge per (row, q head) combines the splits and writes the o_proj input halves directly.
+
+constexpr int RA_THREADS = 128;        // 4 warps; warp w takes positions p0 + w, p0 + w + 4, ...
+
+// One (row b, KV head g, split z): the G query heads of g against positions
+// [z * ROW_SPLIT, min((z + 1) * ROW_SPLIT, pos + 1)) of the row's cache; writes (unnormalised
+// output, running max, running sum) per head to part[((b * NQ + head) * splits + z) * PPITCH].
+// Same math as cpu_inference.rs:143-161 (scores scaled by 1/sqrt(128), softmax, sum of p . v),
+// with the softmax done online.
+template <int G>
+__global__ void __launch_bounds__(RA_THREADS) row_attention(const float* Q, const RowView* rows, int NQ, int NKV, int layer,
+                                                            float scale, float* part, int splits) {
+    __shared__ float sm_o[4][G][128];
+    __shared__ float sm_m[4][G], sm_l[4][G];
+    const int b = blockIdx.x, g = blockIdx.y, z = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const RowView rv = rows[b];
+    const int p_begin = z * ROW_SPLIT;
+    if (p_begin > rv.pos) return;  // past this row's positions (the merge reads only live splits)
+    const int p_end = min(p_begin + ROW_SPLIT, rv.pos + 1);
+    const size_t head_off = ((size_t)layer * NKV + g) * rv.max_seq * 128;
+    const float* kb = rv.k + head_off;
+    const float* vb = rv.v + head_off;
+    float4 q[G], o[G];
+    float m[G], l[G];
+#pragma unroll
+    for (int h = 0; h < G; h++) {
+        q[h] = reinterpret_cast<const float4*>(Q + (size_t)b * NQ * 128 + (size_t)(g * G + h) * 128)[lane];
+        o[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+        m[h] = -INFINITY;
+        l[h] = 0.f;
+    }
+    for (int p = p_begin + warp; p < p_end; p += 4) {
+        const float4 k4 = reinterpret_cast<const float4*>(kb + (size_t)p * 128)[lane];
+        const float4 v4 = reinterpret_cast<const float4*>(vb + (size_t)p * 128)[lane];
+#pragma unroll
+        for (int h = 0; h < G; h++) {
+            float d = q[h].x * k4.x + q[h].y * k4.y + q[h].z * k4.z + q[h].w * k4.w;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) d += __shfl_xor_sync(0xFFFFFFFFu, d, off);
+            const float sc = d * scale;
+            const float mn = fmaxf(m[h], sc);
+            const float corr = m[h] == -INFINITY ? 0.f : __expf(m[h] - mn);
+            const float e = __expf(sc - mn);
+            l[h] = l[h] * corr + e;
+            o[h].x = fmaf(e, v4.x, o[h].x * corr);
+            o[h].y = fmaf(e, v4.y, o[h].y * corr);
+            o[h].z = fmaf(e, v4.z, o[h].z * corr);
+            o[h].w = fmaf(e, v4.w, o[h].w * corr);
+            m[h] = mn;
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < G; h++) {
+        reinterpret_cast<float4*>(sm_o[warp][h])[lane] = o[h];
+        if (lane == 0) {
+            sm_m[warp][h] = m[h];
+            sm_l[warp][h] = l[h];
+        }
+    }
+    __syncthreads();
+    // combine the 4 warps in warp order: thread t -> head t / 32 .. (dims 4 lane), one head per warp
+    for (int h = warp; h < G; h += 4) {
+        float M = -INFINITY;
+        for (int w = 0; w < 4; w++) M = fmaxf(M, sm_m[w][h]);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        float L = 0.f;
+        for (int w = 0; w < 4; w++) {
+            const float mw = sm_m[w][h];
+            const float f = mw == -INFINITY ? 0.f : __expf(mw - M);
+            const float4 ow = reinterpret_cast<const float4*>(sm_o[w][h])[lane];
+            acc.x = fmaf(ow.x, f, acc.x);
+            acc.y = fmaf(ow.y, f, acc.y);
+            acc.z = fmaf(ow.z, f, acc.z);
+            acc.w = fmaf(ow.w, f, acc.w);
+            L = fmaf(sm_l[w][h], f, L);
+        }
+        float* dst = part + (((size_t)b * NQ + g * G + h) * splits + z) * PPITCH;
+        reinterpret_cast<float4*>(dst)[lane] = acc;
+        if (lane == 0) {
+            dst[128] = M;
+            dst[129] = L;
+        }
+    }
+}
+
+// Per (row b, q head): combine the row's live splits in split order and write the normalised
+// attention output as the o_proj GEMM's bf16 hi/lo halves at [b][head * 128 + d]. One warp per
+// head, 4 heads per block.
+__global__ void __launch_bounds__(128) row_merge(const float* part, const RowView* rows, int NQ, int splits, uint16_t* hi,
+                                                 uint16_t* lo) {
+    const int b = blockIdx.x, head = blockIdx.y * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (head >= NQ) return;
+    const int live = rows[b].pos / ROW_SPLIT + 1;
+    const float* base = part + ((size_t)b * NQ + head) * splits * PPITCH;
+    float M = -INFINITY;
+    for (int z = 0; z < live; z++) M = fmaxf(M, base[(size_t)z * PPITCH + 128]);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float L = 0.f;
+    for (int z = 0; z < live; z++) {
+        const float* pz = base + (size_t)z * PPITCH;
+        const float mz = pz[128];
+        const float f = mz == -INFINITY ? 0.f : __expf(mz - M);
+        const float4 v = reinterpret_cast<const float4*>(pz)[lane];
+        acc.x = fmaf(v.x, f, acc.x);
+        acc.y = fmaf(v.y, f, acc.y);
+        acc.z = fmaf(v.z, f, acc.z);
+        acc.w = fmaf(v.w, f, acc.w);
+        L = fmaf(pz[129], f, L);
+    }
+    const float inv = 1.0f / L;
+    const size_t i0 = (size_t)b * NQ * 128 + (size_t)head * 128 + 4 * lane;
+    split_store(acc.x * inv, hi, lo, i0);
+    split_store(acc.y * inv, hi, lo, i0 + 1);
+    split_store(acc.z * inv, hi, lo, i0 + 2);
+    split_store(acc.w * inv, hi, lo, i0 + 3);
+}
+
+// argmax order: larger value wins, ties to the lower index, NaN never wins (the reference CPU rule,
+// common/mod.rs:17-22)
+constexpr unsigned AM_NONE = 0xFFFFFFFFu;
+__device__ __forceinline__ bool am_wins(float av, unsigned ai, float bv, unsigned bi) {
+    if (ai == AM_NONE) return false;
+    if (bi == AM_NONE) return true;
+    return av > bv || (av == bv && ai < bi);
+}
+
+constexpr int AR_THREADS = 1024;
+
+// One block per row: next token = argmax of the row's logits, recorded at d_out[(pos - start) * B
+// + b]; the row then advances to pos + 1 (the next step's input position).
+__global__ void __launch_bounds__(AR_THREADS) argmax_rows_kernel(const float* logits, int V, int B, RowView* rows,
+                                                                 uint32_t* tok, uint32_t* out) {
+    __shared__ float sv[AR_THREADS / 32];
+    __shared__ unsigned si[AR_THREADS / 32];
+    const int b = blockIdx.x;
+    const float* x = logits + (size_t)b * V;
+    float bv = -INFINITY;
+    unsigned bi = AM_NONE;
+    for (int i = threadIdx.x; i < V; i += AR_THREADS) {
+        const float v = x[i];
+        if (!isnan(v) && am_wins(v, (unsigned)i, bv, bi)) {
+            bv = v;
+            bi = (unsigned)i;
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+        const unsigned oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+        if (am_wins(ov, oi, bv, bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    if ((threadIdx.x & 31) == 0) {
+        sv[threadIdx.x >> 5] = bv;
+        si[threadIdx.x >> 5] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < AR_THREADS / 32; w++)
+            if (am_wins(sv[w], si[w], bv, bi)) {
+                bv = sv[w];
+                bi = si[w];
+            }
+        // a NaN at index 0 sticks, and with nothing comparable the CPU argmax stays at 0
+        const unsigned t = (isnan(x[0]) || bi == AM_NONE) ? 0u : bi;
+        tok[b] = t;
+        RowView& rv = rows[b];
+        if (out) out[(size_t)(rv.pos - rv.start) * B + b] = t;
+        rv.pos += 1;
+    }
+}
+
+size_t row_partial_floats(int B, int NQ, int splits) { return (size_t)B * NQ * splits * PPITCH; }
+
+int argmax_rows(const float* d_logits, int V, int B, RowView* d_rows, uint32_t* d_tok, uint32_t* d_out, cudaStream_t s,
+                std::string& err) {
+    argmax_rows_kernel<<<B, AR_THREADS, 0, s>>>(d_logits, V, B, d_rows, d_tok, d_out);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        err = std::string("argmax launch failed: ") + cudaGetErrorString(e);
+        return QW_ERR_CUDA;
+    }
+    return QW_OK;
+}
+
+// One forward pass over n rows: prefill (rows == null; token t at position start + t of cache c)
+// or row mode (rows != null; token t at rows[t].pos of its own cache, `splits` attention splits).
+static int forward_pass(const Weights& w, const CacheView& c, const RowView* rows, int splits, const uint32_t* d_ids, int n,
+                        int start, float* d_logits, Scratch& sc, int* err_word, cudaStream_t s, std::string& err) {
     const int H = w.H, I = w.I, NQ = w.NQ, NKV = w.NKV, QD = NQ * 128, KVD = NKV * 128, QKVR = QD + 2 * KVD;
     const size_t nH = (size_t)n * H;
+    if (sc.ycap < y_floats(n, H, I, NQ, NKV)) {
+        err = "GEMM output scratch too small";
+        return QW_ERR_ARG;
+    }
     embed_rows<<<n, 256, 0, s>>>(d_ids, H, w.embed, sc.X);
     const int G = NQ / NKV;
     const float scale = 1.0f / sqrtf(128.0f);
-    const int ks_o = ksplit_for(n, H, QD), ks_d = ksplit_for(n, H, I);
+    const int ks_qkv = ksplit_for(n, QKVR, H), ks_o = ksplit_for(n, H, QD), ks_gu = ksplit_for(n, 2 * I, H),
+              ks_d = ksplit_for(n, H, I);
     for (int l = 0; l < w.L; l++) {
         const uint16_t* W = w.layer_w + (size_t)l * w.layer_stride;
         const uint16_t* nrm = w.layer_n + (size_t)l * w.norm_stride;
-        const size_t hsl = (size_t)l * NKV * c.max_seq * 128;
         int rc;
-        // A: rmsnorm -> q|k|v
-        // (the previous layer's down_proj slices are added into X here)
+        // A: (the previous layer's down_proj slices into X) rmsnorm -> q|k|v
         norm_split<<<n, ROW_THREADS, 0, s>>>(sc.X, H, nrm, w.eps, sc.ahi, sc.alo, sc.Y, l == 0 ? 0 : ks_d, nH);
-        if ((rc = tc::gemm(sc.ahi, sc.alo, H, W, H, sc.Y, QKVR, n, QKVR, H, err_word, s, err, 1))) return rc;
-        // B: q/k norm + RoPE, K/V into the cache, causal attention
+        if ((rc = tc::gemm(sc.ahi, sc.alo, H, W, H, sc.Y, QKVR, n, QKVR, H, err_word, s, err, ks_qkv))) return rc;
+        // B: q/k norm + RoPE, K/V into the cache, attention -> o_proj input halves
         const int items = n * (NQ + 2 * NKV);
-        qkv_post<<<(items + 7) / 8, 256, 0, s>>>(sc.Y, n, start, NQ, NKV, nrm + 2 * H, nrm + 2 * H + 128, w.eps, c.rope, sc.Q,
-                                                 c.k, c.v, hsl, c.max_seq);
-        rc = G == 1 ? launch_attention<1>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, sc.attp, sc.attp_cap, s)
-           : G == 2 ? launch_attention<2>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, sc.attp, sc.attp_cap, s)
-                    : launch_attention<3>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, sc.attp, sc.attp_cap, s);
-        if (rc) {
-            err = rc == QW_ERR_ARG ? "prefill attention partial buffer too small"
-                                   : "cannot raise the prefill attention kernel's shared-memory limit";
-            return rc;
+        qkv_post<<<(items + 7) / 8, 256, 0, s>>>(sc.Y, ks_qkv, n, start, NQ, NKV, nrm + 2 * H, nrm + 2 * H + 128, w.eps, c,
+                                                 rows, l, sc.Q);
+        if (rows) {
+            if (row_partial_floats(n, NQ, splits) > sc.attp_cap) {
+                err = "row attention partial buffer too small";
+                return QW_ERR_ARG;
+            }
+            const dim3 ag(n, NKV, splits);
+            if (G == 1) row_attention<1><<<ag, RA_THREADS, 0, s>>>(sc.Q, rows, NQ, NKV, l, scale, sc.attp, splits);
+            else if (G == 2) row_attention<2><<<ag, RA_THREADS, 0, s>>>(sc.Q, rows, NQ, NKV, l, scale, sc.attp, splits);
+            else row_attention<3><<<ag, RA_THREADS, 0, s>>>(sc.Q, rows, NQ, NKV, l, scale, sc.attp, splits);
+            row_merge<<<dim3(n, (NQ + 3) / 4), 128, 0, s>>>(sc.attp, rows, NQ, splits, sc.ahi, sc.alo);
+        } else {
+            const size_t hsl = (size_t)l * NKV * c.max_seq * 128;
+            rc = G == 1 ? launch_attention<1>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, sc.attp, sc.attp_cap, s)
+               : G == 2 ? launch_attention<2>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, sc.attp, sc.attp_cap, s)
+                        : launch_attention<3>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, sc.attp, sc.attp_cap, s);
+            if (rc) {
+                err = rc == QW_ERR_ARG ? "prefill attention partial buffer too small"
+                                       : "cannot raise the prefill attention kernel's shared-memory limit";
+                return rc;
+            }
+            split_rows<<<grid_for((size_t)n * QD), 256, 0, s>>>(sc.att, (size_t)n * QD, sc.ahi, sc.alo);
         }
-        // C: o_proj + residual
-        split_rows<<<grid_for((size_t)n * QD), 256, 0, s>>>(sc.att, (size_t)n * QD, sc.ahi, sc.alo);
+        // C: o_proj (its slices go into X in the next norm)
         if ((rc = tc::gemm(sc.ahi, sc.alo, QD, W + (size_t)QKVR * H, QD, sc.Y, H, n, H, QD, err_word, s, err, ks_o))) return rc;
-        // D: residual (the o_proj slices) + rmsnorm -> gate|up -> silu(gate) * up
+        // D: residual + rmsnorm -> gate|up -> silu(gate) * up
         norm_split<<<n, ROW_THREADS, 0, s>>>(sc.X, H, nrm + H, w.eps, sc.ahi, sc.alo, sc.Y, ks_o, nH);
         const uint16_t* Wgu = W + (size_t)QKVR * H + (size_t)H * QD;
-        if ((rc = tc::gemm(sc.ahi, sc.alo, H, Wgu, H, sc.Y, 2 * I, n, 2 * I, H, err_word, s, err, 1))) return rc;
-        silu_split<<<grid_for((size_t)n * I), 256, 0, s>>>(sc.Y, (size_t)n * I, sc.ahi, sc.alo);
-        // E: down + residual
+        if ((rc = tc::gemm(sc.ahi, sc.alo, H, Wgu, H, sc.Y, 2 * I, n, 2 * I, H, err_word, s, err, ks_gu))) return rc;
+        silu_split<<<grid_for((size_t)n * I), 256, 0, s>>>(sc.Y, (size_t)n * I, sc.ahi, sc.alo, ks_gu);
+        // E: down (its slices go into X in the next layer's norm)
         const uint16_t* Wd = Wgu + (size_t)2 * I * H;
         if ((rc = tc::gemm(sc.ahi, sc.alo, I, Wd, I, sc.Y, H, n, H, I, err_word, s, err, ks_d))) return rc;
     }
@@ -562,10 +820,24 @@ int run(const Weights& w, const CacheView& c, const uint32_t* d_ids, int n, int 
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
-        err = std::string("prefill launch failed: ") + cudaGetErrorString(e);
+        err = std::string("forward pass launch failed: ") + cudaGetErrorString(e);
         return QW_ERR_CUDA;
     }
     return QW_OK;
+}
+
+int run(const Weights& w, const CacheView& c, const uint32_t* d_ids, int n, int start, float* d_logits, Scratch& sc,
+        int* err_word, cudaStream_t s, std::string& err) {
+    return forward_pass(w, c, nullptr, 0, d_ids, n, start, d_logits, sc, err_word, s, err);
+}
+
+int run_rows(const Weights& w, const RowView* d_rows, int B, int splits, const uint32_t* d_tok, float* d_logits,
+             Scratch& sc, int* err_word, cudaStream_t s, std::string& err) {
+    if (B < 1 || B > ROWS_MAX || splits < 1) {
+        err = "row step: 1 <= rows <= 16 and splits >= 1";
+        return QW_ERR_ARG;
+    }
+    return forward_pass(w, CacheView{}, d_rows, splits, d_tok, B, 0, d_logits, sc, err_word, s, err);
 }
 
 }  // namespace pf

@@ -30,13 +30,32 @@ struct CacheView {
     int max_seq;
 };
 
-// most K splits of one GEMM; each split writes its own [n][H] slice of Scratch::Y
-constexpr int KSPLIT_MAX = 4;
+// most K splits of one GEMM; split z writes its own [n][N] slice of Scratch::Y
+constexpr int KSPLIT_MAX = 16;
+
+// most rows of one row-mode step (the skinny GEMM's activation rows)
+constexpr int ROWS_MAX = 16;
+
+// K splits of an [M x N] x K GEMM: enough to come near one CTA per SM when the output tiles alone
+// would leave SMs idle, at most KSPLIT_MAX and K / 64
+int ksplit_for(int M, int N, int K);
+
+// One row of a row-mode step (a decode batch): sequence b's cache and position. Lives in device
+// memory; the step's argmax advances `pos`, so a captured step replays without host writes.
+struct RowView {
+    float* k;                  // cache K [layer][kv_head][max_seq][128]
+    float* v;                  // cache V, same layout
+    const float2* rope;        // cache RoPE table [max_seq][64]
+    int max_seq;
+    int pos;                   // position of the row's input token this step
+    int start;                 // position of the row's first decode input (output index = pos - start)
+    int pad;
+};
 
 // device scratch for n tokens
 struct Scratch {
     float* X = nullptr;        // [n][H] residual stream
-    float* Y = nullptr;        // [n][max(QKVR, 2I, KSPLIT_MAX * H)] GEMM outputs
+    float* Y = nullptr;        // GEMM outputs, ycap floats: [ksplit][n][N] for the widest use
     float* Q = nullptr;        // [n][QD] normed, rotated queries
     float* att = nullptr;      // [n][QD] attention outputs
     uint16_t* ahi = nullptr;   // [n][max(H, QD, I)] GEMM input, high bf16 halves
@@ -44,7 +63,11 @@ struct Scratch {
     int cap = 0;               // tokens the buffers hold
     float* attp = nullptr;     // attention partials of split query tiles
     size_t attp_cap = 0;       // floats attp holds
+    size_t ycap = 0;           // floats Y holds
 };
+
+// floats of Scratch::Y a pass over n rows needs (largest ksplit x n x N over the four GEMMs)
+size_t y_floats(int n, int H, int I, int NQ, int NKV);
 
 // floats of attention partials a pass over n tokens from position `start` needs
 size_t attention_partial_floats(int n, int start, int NQ, int NKV);
@@ -53,6 +76,23 @@ size_t attention_partial_floats(int n, int start, int NQ, int NKV);
 // into the cache and, with d_logits ([n][V] device), every position's logits. Stream-ordered.
 int run(const Weights& w, const CacheView& c, const uint32_t* d_ids, int n, int start, float* d_logits, Scratch& sc,
         int* err_word, cudaStream_t s, std::string& err);
+
+// Positions per attention split of a row-mode step
+constexpr int ROW_SPLIT = 64;
+
+// floats of attention partials a row-mode step over B rows with `splits` position splits needs
+size_t row_partial_floats(int B, int NQ, int splits);
+
+// One row-mode step over B rows (B <= ROWS_MAX): row b feeds d_tok[b] at d_rows[b].pos into its
+// own cache and, with d_logits ([B][V]), gets its logits. `splits` position splits of ROW_SPLIT
+// cover every row's positions (pos < splits * ROW_SPLIT). Stream-ordered; capturable.
+int run_rows(const Weights& w, const RowView* d_rows, int B, int splits, const uint32_t* d_tok, float* d_logits,
+             Scratch& sc, int* err_word, cudaStream_t s, std::string& err);
+
+// Greedy step end for B rows: d_tok[b] = argmax(d_logits[b]) (the reference CPU rule),
+// d_out[(pos - start) * B + b] = the same token, then pos += 1. Stream-ordered; capturable.
+int argmax_rows(const float* d_logits, int V, int B, RowView* d_rows, uint32_t* d_tok, uint32_t* d_out, cudaStream_t s,
+                std::string& err);
 
 }  // namespace pf
 }  // namespace qw

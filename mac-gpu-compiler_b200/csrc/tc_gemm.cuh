@@ -22,6 +22,13 @@
 // Every wait is bounded: a wait that runs out sets `err` (the kernel's error word) and the CTA
 // skips the remaining work, still waiting (bounded) for the copies and MMAs it issued and freeing
 // its tensor memory before it exits.
+//
+// gemm_skinny_kernel is the same product for M <= 16 activation rows (a decode batch, a short
+// verify pass). There the weights are the only real traffic, so the roles swap: the weight tile
+// is the MMA's A operand (M = 128 weight rows) and the activations its B operand (N = 16), giving
+// D[128][16] = W . X^T per CTA in 32 TMEM columns. Tensor work per weight byte drops 8x against a
+// 128-row activation tile, and a 20 KB stage (16 KB weights) lets an 8-deep ring keep 128 KB of
+// weights in flight per SM.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -83,6 +90,16 @@ __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a_desc, uint6
 
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
@@ -239,6 +256,115 @@ gemm_bf16x2_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_con
         __syncwarp();
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)TMEM_COLS) : "memory");
+    }
+}
+
+constexpr int SK_NB = 16;                          // most activation rows of the skinny GEMM
+constexpr int SK_STAGES = 8;
+constexpr int SK_TILE_W = BN * BK * 2;             // 16 KB weight tile (128 rows x 64)
+constexpr int SK_TILE_X = SK_NB * BK * 2;          // 2 KB activation half tile (16 rows x 64)
+constexpr int SK_STAGE_BYTES = SK_TILE_W + 2 * SK_TILE_X;
+constexpr int SK_SMEM_BYTES = SK_STAGES * SK_STAGE_BYTES + 1024;
+constexpr int SK_TMEM_COLS = 32;                   // smallest allocation; columns 0..15 used
+
+// Y[M][ldy] (M <= 16) = (X_hi + X_lo)[M][K] . W[N][K]^T; CTA = 128 weight rows x one K range
+__global__ void __launch_bounds__(THREADS, 1)
+gemm_skinny_kernel(const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
+                   const __grid_constant__ CUtensorMap map_w, const GemmArgs args) {
+    extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
+    __shared__ uint64_t full[SK_STAGES], empty[SK_STAGES], done;
+    __shared__ uint32_t tmem_base;
+    __shared__ volatile int abort_flag;
+    uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * BN;
+    const int nkb_all = args.K / BK;
+    const int kb0 = (int)((long long)nkb_all * blockIdx.z / gridDim.z);
+    const int nkb = (int)((long long)nkb_all * (blockIdx.z + 1) / gridDim.z) - kb0;
+    float* const y = args.y + (long long)blockIdx.z * args.split_stride;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < SK_STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&done, 1);
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32(&tmem_base)), "r"((uint32_t)SK_TMEM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_base;
+    const uint32_t idesc = idesc_bf16_f32(BN, SK_NB);
+    int issued_kb = 0;
+
+    if (warp == 0 && lane == 0) {
+        for (int kb = 0; kb < nkb; kb++) {
+            const int s = kb % SK_STAGES;
+            if (kb >= SK_STAGES && !bounded_wait(&empty[s], ((kb / SK_STAGES) - 1) & 1, &abort_flag)) break;
+            uint8_t* st = ring + s * SK_STAGE_BYTES;
+            mbar_arrive_expect_tx(&full[s], SK_STAGE_BYTES);
+            tma_load_2d(st, &map_w, (kb0 + kb) * BK, n0, &full[s]);
+            tma_load_2d(st + SK_TILE_W, &map_xhi, (kb0 + kb) * BK, 0, &full[s]);
+            tma_load_2d(st + SK_TILE_W + SK_TILE_X, &map_xlo, (kb0 + kb) * BK, 0, &full[s]);
+            issued_kb = kb + 1;
+        }
+    } else if (warp == 1 && lane == 0) {
+        for (int kb = 0; kb < nkb; kb++) {
+            const int s = kb % SK_STAGES;
+            if (!bounded_wait(&full[s], (kb / SK_STAGES) & 1, &abort_flag)) break;
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t st = smem_u32(ring + s * SK_STAGE_BYTES);
+            const uint64_t dw = smem_desc_k128(st), dhi = smem_desc_k128(st + SK_TILE_W),
+                           dlo = smem_desc_k128(st + SK_TILE_W + SK_TILE_X);
+#pragma unroll
+            for (int kk = 0; kk < BK / 16; kk++) {
+                mma_bf16(tmem, dw + 2 * kk, dhi + 2 * kk, idesc, (kb | kk) != 0);
+                mma_bf16(tmem, dw + 2 * kk, dlo + 2 * kk, idesc, 1u);
+            }
+            mma_commit(&empty[s]);
+        }
+        mma_commit(&done);
+    }
+    __syncwarp();
+    const bool ok = bounded_wait(&done, 0, &abort_flag) && !abort_flag;
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (ok) {
+        // thread = weight row n0 + 32 warp + lane (TMEM lane), column j = activation row j
+        uint32_t r[16];
+        tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16), r);
+        const int row = n0 + warp * 32 + lane;
+        if (row < args.N) {
+#pragma unroll
+            for (int j = 0; j < SK_NB; j++)
+                if (j < args.M) y[(size_t)j * args.ldy + row] = __uint_as_float(r[j]);
+        }
+    }
+    if (!ok && threadIdx.x == 0) atomicExch(args.err, 1);
+    if (!ok && warp == 0 && lane == 0) {
+        for (int kb = issued_kb - SK_STAGES > 0 ? issued_kb - SK_STAGES : 0; kb < issued_kb; kb++) {
+            const uint64_t t0 = globaltimer_ns();
+            while (!mbar_try_wait(&full[kb % SK_STAGES], (kb / SK_STAGES) & 1))
+                if (globaltimer_ns() - t0 > (uint64_t)WAIT_LIMIT_NS) break;
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        if (!ok && lane == 0) {
+            const uint64_t t0 = globaltimer_ns();
+            while (!mbar_try_wait(&done, 0))
+                if (globaltimer_ns() - t0 > (uint64_t)WAIT_LIMIT_NS) break;
+        }
+        __syncwarp();
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)SK_TMEM_COLS) : "memory");
     }
 }
 

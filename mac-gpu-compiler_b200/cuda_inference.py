@@ -88,6 +88,9 @@ def lib() -> ctypes.CDLL:
             "qw_prefill": (i32, [vp, vp, vp, sz, sz, vp]),
             "qw_prefill_device": (i32, [vp, vp, vp, sz, sz, vp, vp]),
             "qw_decode": (i32, [vp, vp, u32, sz, sz, TOKEN_FN, vp]),
+            "qw_forward_batch": (i32, [vp, vp, sz, vp, vp, vp]),
+            "qw_decode_batch": (i32, [vp, vp, sz, vp, vp, sz, vp]),
+            "qw_decode_batch_device": (i32, [vp, vp, sz, vp, vp, sz, vp, vp]),
             "qw_forward_device": (i32, [vp, vp, vp, sz, vp, vp]),
             "qw_decode_device": (i32, [vp, vp, vp, sz, sz, vp]),
             "qw_sync": (i32, [vp, vp]),
@@ -195,6 +198,35 @@ class CudaModel:
         fn = TOKEN_FN(cb)
         _check(lib().qw_decode(self._h, cache._h, first, start_pos, steps, fn, None))
         return got
+
+    # batch decode: B independent sequences, one cache each, stepping together (qw_*_batch)
+    @staticmethod
+    def _caches(caches) -> "ctypes.Array":
+        return (ctypes.c_void_p * len(caches))(*[c._h for c in caches])
+
+    def forward_batch(self, tokens, positions, caches) -> np.ndarray:
+        """Row b feeds tokens[b] at positions[b] into caches[b]; returns [B, vocab] logits."""
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32))
+        p = np.ascontiguousarray(np.asarray(positions, dtype=np.uint64))
+        out = np.empty((t.size, self.config.vocab_size), np.float32)
+        _check(lib().qw_forward_batch(self._h, self._caches(caches), t.size, t.ctypes.data, p.ctypes.data,
+                                      out.ctypes.data))
+        return out
+
+    def decode_batch(self, firsts, start_pos, steps: int, caches) -> np.ndarray:
+        """decode() for every row at once; returns [B, steps] output tokens."""
+        f = np.ascontiguousarray(np.asarray(firsts, dtype=np.uint32))
+        p = np.ascontiguousarray(np.asarray(start_pos, dtype=np.uint64))
+        out = np.empty((f.size, steps), np.uint32)
+        _check(lib().qw_decode_batch(self._h, self._caches(caches), f.size, f.ctypes.data, p.ctypes.data, steps,
+                                     out.ctypes.data))
+        return out
+
+    def decode_batch_device(self, d_firsts: int, start_pos, steps: int, caches, d_out: int, stream: int = 0) -> None:
+        """Stream-ordered decode_batch: device first tokens, device record d_out[steps][B]."""
+        p = np.ascontiguousarray(np.asarray(start_pos, dtype=np.uint64))
+        _check(lib().qw_decode_batch_device(self._h, self._caches(caches), p.size, d_firsts, p.ctypes.data, steps,
+                                            d_out, stream or None))
 
     # device-resident variants: raw device pointers (ints) and an optional cudaStream_t handle
     def forward_device(self, cache: "CudaKVCache", d_token: int, pos: int, d_logits: int, stream: int = 0) -> None:

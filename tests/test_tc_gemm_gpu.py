@@ -2,7 +2,8 @@
 product of the same bf16 operands: Y = (A_hi + A_lo) . B^T, with A_hi + A_lo the two-bf16 split of
 f32 activations. Shapes cover the prefill's projections (K = 1024, 2048, 3072), a ragged M (rows
 that are not a multiple of the 128-row tile, which the TMA zero-fills), the lm_head width and an
-odd output width (rows of the f32 output that are not 16-byte aligned)."""
+odd output width (rows of the f32 output that are not 16-byte aligned), and the few-row shapes of a
+decode batch."""
 from __future__ import annotations
 
 import pytest
@@ -25,8 +26,11 @@ def split_bf16(a: "torch.Tensor"):
     return hi.contiguous(), lo.contiguous()
 
 
+# M <= 16 takes the swapped-operand (skinny) kernel: weights as the MMA's 128-row operand
 @pytest.mark.parametrize("M,N,K", [(128, 128, 64), (512, 4096, 1024), (200, 1024, 2048), (77, 6144, 1024),
-                                   (512, 1024, 3072), (33, 151936, 1024), (130, 10007, 1024)])
+                                   (512, 1024, 3072), (33, 151936, 1024), (130, 10007, 1024),
+                                   (1, 4096, 1024), (8, 1024, 2048), (16, 6144, 1024), (5, 10007, 1024),
+                                   (16, 1024, 3072), (3, 151936, 1024)])
 def test_gemm_matches_f64(M, N, K):
     g = torch.Generator(device="cuda").manual_seed(M * 7 + N + K)
     a = torch.randn(M, K, device="cuda", generator=g)
