@@ -50,6 +50,9 @@ CONFIGS = {
                     label="configs[3]: 512-id prompt in one batched prefill pass (tcgen05 GEMMs), then 64 greedy decode steps"),
     "box": dict(prompt=130, decode=128, sequences=64,
                 label="configs[4]: 64 independent sequences (130-id prompt + 128 greedy steps each) sharded over the GPUs"),
+    "box8": dict(prompt=130, decode=128, sequences=64, batch=8,
+                 label="configs[4], batch-8 variant: 64 independent sequences (130-id prompt + 128 greedy steps each) "
+                       "sharded over the GPUs, decoded 8 at a time per GPU (qw_decode_batch)"),
 }
 # reference's published decode tok/s for this metric and config: Metal engine, f32 KV cache, Apple M1
 # (metal_infrence_engine/README.md:22)
@@ -174,6 +177,110 @@ def run_prefill(args, world: int, rank: int, local: int, pg) -> None:
             "gpu_launches": args.steps * (1 + 9 * cfg.num_hidden_layers + 2),
             "clocks": clocks.summary(),
         }), flush=True)
+    model.close()
+
+
+def run_batch(args, world: int, rank: int, local: int, pg) -> None:
+    """configs[4]'s batch-8 variant: this rank's share of the 64 sequences, in groups of 8 that
+    decode together (one captured graph step per token of all 8 rows). A bench step is one
+    128-token greedy decode of every group. The weights are read once per step of a group."""
+    import numpy as np
+    import torch
+    import cuda_inference as ci
+    c = CONFIGS["box8"]
+    n_prompt, n_dec, B = c["prompt"], c["decode"], c["batch"]
+    path = randmodel.make_model("qwen3-0.6b", 0)
+    model = ci.CudaModel.load_model(path, device=local)
+    cfg = model.config
+    seqs = list(replicas.shard(c["sequences"], world, rank))
+    groups = [seqs[i:i + B] for i in range(0, len(seqs), B)]
+    caches, firsts = {}, {}
+    for sq in seqs:                                    # untimed: batched prefill of all but the last id
+        cache = ci.CudaKVCache(model, n_prompt + n_dec + 1)
+        ids = randmodel.prompt_ids(n_prompt, cfg.vocab_size, seed=replicas.prompt_seed(sq))
+        model.prefill(ids[:-1], 0, cache, logits=False)
+        firsts[sq] = int(np.argmax(model.forward(ids[-1], n_prompt - 1, cache)))
+        caches[sq] = cache
+    dev = f"cuda:{local}"
+    d_first = [torch.tensor([firsts[s] for s in g], dtype=torch.int32, device=dev) for g in groups]
+    d_out = [torch.zeros(n_dec * len(g), dtype=torch.int32, device=dev) for g in groups]
+    stream = torch.cuda.ExternalStream(model.stream)
+    torch.cuda.synchronize()
+
+    def step():
+        for g, f, o in zip(groups, d_first, d_out):
+            model.decode_batch_device(f.data_ptr(), [n_prompt] * len(g), n_dec, [caches[s] for s in g], o.data_ptr(),
+                                      stream=model.stream)
+
+    for _ in range(args.warmup):
+        step()
+    model.sync()
+    if pg is not None:
+        pg.barrier()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            evs[i][0].record(stream)
+            step()
+            evs[i][1].record(stream)
+        torch.cuda.synchronize()
+    model.sync()
+    elapsed = sum(a.elapsed_time(b) for a, b in evs) / 1e3
+    if pg is not None:
+        pg.barrier()
+    group_arg = pg.group.WORLD if pg is not None else None
+    box = replicas.aggregate(replicas.reduce_timings(replicas.RankTiming(n_dec * args.steps * len(seqs), elapsed),
+                                                     group=group_arg))
+    dev_tokens = [o.view(n_dec, -1).t().cpu().numpy() for o in d_out]
+
+    # e2e: the host API (qw_decode_batch: host first tokens and positions in, [B][steps] tokens out)
+    rounds = max(2, min(args.steps, 3))
+    e2e_sec = 0.0
+    for i in range(rounds + 1):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for k, g in enumerate(groups):
+            got = model.decode_batch([firsts[s] for s in g], [n_prompt] * len(g), n_dec, [caches[s] for s in g])
+            assert (got == dev_tokens[k].astype(np.uint32)).all(), "host-API batch decode disagrees with the device one"
+        b.record(stream)
+        torch.cuda.synchronize()
+        if i > 0:
+            e2e_sec += a.elapsed_time(b) / 1e3
+    e2e_box = replicas.aggregate(replicas.reduce_timings(replicas.RankTiming(n_dec * rounds * len(seqs), e2e_sec),
+                                                         group=group_arg))
+    if rank == 0:
+        W = model.weight_bytes_per_token()
+        # algorithmic bytes of one graph step of a group: the weights once, plus every row's K/V history
+        step_bytes = [W + sum(kv_bytes_at(cfg, pos) for _ in g) for g in groups[:1] for pos in range(n_prompt, n_prompt + n_dec)]
+        bytes_group = sum(step_bytes)
+        group_s = elapsed / args.steps / max(1, len(groups))
+        achieved = bytes_group / group_s / 1e9
+        peak, peak_kind = load_peaks()
+        per_step_kernels = 10 * cfg.num_hidden_layers + 4
+        line = {
+            "metric": "Qwen3-0.6B bf16 decode tok/s @bs1 & % of HBM roofline; box tok/s at 1-8 GPUs",
+            "value": box["tok_per_s"], "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": box["seconds"] / args.steps * 1e3,
+            "ms_per_batch_token_step": group_s / n_dec * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "accumulate": "f32 (split-bf16 activations)", "data": "synthetic",
+            "config": {"workload": c["label"], "model": "Qwen3-0.6B geometry, random-init bf16 (seed 0)",
+                       "global_batch": c["sequences"], "per_gpu_batch": B, "seq_len": n_prompt + n_dec,
+                       "parallelism": f"replicas x{world}, {len(seqs)} sequences on rank 0 in groups of {B}, no collective",
+                       "l2": "inputs larger than L2: 1.19 GB of weights streamed per batch step",
+                       "step": f"one {n_dec}-token greedy decode of every group ({n_dec} graph replays per group)"},
+            "e2e": {"value": e2e_box["tok_per_s"], "unit": "tok/s", "h2d_bytes_per_step": 4 * len(seqs) + 8 * len(seqs),
+                    "d2h_bytes_per_step": 4 * n_dec * len(seqs), "api": "qw_decode_batch (host tokens in and out)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_kind": f"{peak_kind} (hbm_gbs, copy)", "traffic": None,
+                         "algorithmic_bytes_per_group_decode": bytes_group,
+                         "kernel": "batch step graph (skinny tcgen05 GEMMs, row attention, elementwise)"},
+            "gpu_launches": args.steps * len(groups) * n_dec * per_step_kernels,
+            "clocks": clocks.summary(),
+            "first_tokens": [int(x) for x in dev_tokens[0][0][:8]] if groups else [],
+        }
+        print(json.dumps(line), flush=True)
     model.close()
 
 
@@ -338,8 +445,8 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
         pg = dist
-    if args.config == "prefill":
-        run_prefill(args, world, rank, local, pg)
+    if args.config in ("prefill", "box8"):
+        (run_prefill if args.config == "prefill" else run_batch)(args, world, rank, local, pg)
         if pg is not None:
             pg.barrier()
             pg.destroy_process_group()

@@ -158,8 +158,7 @@ struct qw_model {
     uint32_t* d_bout = nullptr;
     size_t bout_cap = 0;                 // entries of d_bout
     cudaGraphExec_t bgraph = nullptr;
-    struct { int B = 0, splits = 0; const void *X = nullptr, *Y = nullptr, *attp = nullptr, *logits = nullptr, *out = nullptr;
-             cudaStream_t stream = nullptr; } bsig;
+    struct { int B = 0, splits = 0; const void *X = nullptr, *Y = nullptr, *attp = nullptr, *logits = nullptr, *out = nullptr; } bsig;
     unsigned epoch = 0;
     int S = 0, part_cap = 0, xs_cap = 0, xloc_cap = 0;
     u64* d_trace = nullptr;      // phase timeline of the most recent launch's first step, if enabled
@@ -749,17 +748,18 @@ int batch_graph(qw_model* m, int B, int splits, uint32_t* out, int* ew) {
     return QW_OK;
 }
 
-// stream-ordered batch decode: rows from host positions, first tokens already in m->d_btok
+// stream-ordered batch decode: rows from host positions, first tokens already in m->d_btok; the
+// step graph records tokens into m->d_bout ([steps][B]), so one capture serves every batch of the
+// same shape
 int batch_decode_launch(qw_model* m, qw_cache* const* caches, size_t B, const size_t* start_pos, size_t steps,
-                        uint32_t* d_out, cudaStream_t s, bool out_is_record) {
+                        cudaStream_t s) {
     std::vector<qw::pf::RowView> rows;
     int splits = 0;
     if (int e = batch_rows(m, caches, B, start_pos, steps, rows, splits)) return e;
-    if (int e = ensure_batch(m, B, splits, out_is_record ? steps * B : 0)) return e;
-    if (out_is_record) d_out = m->d_bout;
+    if (int e = ensure_batch(m, B, splits, steps * B)) return e;
     int* ew = qw::device_err_word_for(m->device);
     if (!ew) return set_err(QW_ERR_NOMEM, "error word allocation failed");
-    if (int e = batch_graph(m, (int)B, splits, d_out, ew)) return e;
+    if (int e = batch_graph(m, (int)B, splits, m->d_bout, ew)) return e;
     QW_CUDA(cudaMemsetAsync(ew, 0, sizeof(int), s));
     QW_CUDA(cudaMemcpyAsync(m->d_rows, rows.data(), B * sizeof(qw::pf::RowView), cudaMemcpyHostToDevice, s));
     for (size_t i = 0; i < steps; i++) QW_CUDA(cudaGraphLaunch(m->bgraph, s));
@@ -806,7 +806,7 @@ int qw_decode_batch(qw_model* m, qw_cache* const* caches, size_t B, const uint32
     if (B >= 1 && B <= (size_t)qw::pf::ROWS_MAX && !m->d_btok) QW_CUDA(cudaMalloc(&m->d_btok, qw::pf::ROWS_MAX * 4));
     if (m->d_btok && B >= 1 && B <= (size_t)qw::pf::ROWS_MAX)
         QW_CUDA(cudaMemcpyAsync(m->d_btok, firsts, B * 4, cudaMemcpyHostToDevice, s));
-    if (int e = batch_decode_launch(m, caches, B, start_pos, steps, nullptr, s, true)) return e;
+    if (int e = batch_decode_launch(m, caches, B, start_pos, steps, s)) return e;
     std::vector<uint32_t> rec(steps * B);
     QW_CUDA(cudaMemcpyAsync(rec.data(), m->d_bout, steps * B * 4, cudaMemcpyDeviceToHost, s));
     int h = 0;
@@ -828,7 +828,9 @@ int qw_decode_batch_device(qw_model* m, qw_cache* const* caches, size_t B, const
     if (!m->d_btok) QW_CUDA(cudaMalloc(&m->d_btok, qw::pf::ROWS_MAX * 4));
     if (B >= 1 && B <= (size_t)qw::pf::ROWS_MAX)
         QW_CUDA(cudaMemcpyAsync(m->d_btok, d_firsts, B * 4, cudaMemcpyDeviceToDevice, s));
-    return batch_decode_launch(m, caches, B, start_pos, steps, d_out, s, false);
+    if (int e = batch_decode_launch(m, caches, B, start_pos, steps, s)) return e;
+    QW_CUDA(cudaMemcpyAsync(d_out, m->d_bout, steps * B * 4, cudaMemcpyDeviceToDevice, s));
+    return QW_OK;
 }
 
 int qw_forward(qw_model* m, qw_cache* c, uint32_t token, size_t pos, float* logits_out) {

@@ -21,6 +21,26 @@ int set_error(int code, const char* msg);
 using namespace qw;
 
 namespace qw {
+
+// Every kernel of the prefill and the batch step is launched with programmatic stream
+// serialization: it may start (and run its prologue, e.g. a GEMM's first weight copies) while the
+// previous kernel finishes; each calls pdl_wait() before it touches memory an earlier kernel wrote
+// or reads. Launch errors surface through cudaGetLastError.
+template <typename... KArgs, typename... Args>
+void launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 namespace tc {
 
 // cuTensorMapEncodeTiled, fetched from the driver through the runtime (the library links the
@@ -92,7 +112,7 @@ int gemm(const uint16_t* a_hi, const uint16_t* a_lo, int lda, const uint16_t* b,
             return QW_ERR_CUDA;
         }
         GemmArgs args{y, M, N, K, ldy, err_word, (long long)M * ldy};
-        gemm_skinny_kernel<<<dim3((N + BN - 1) / BN, 1, ksplit), THREADS, SK_SMEM_BYTES, s>>>(mh, ml, mb, args);
+        launch(gemm_skinny_kernel, dim3((N + BN - 1) / BN, 1, ksplit), dim3(THREADS), SK_SMEM_BYTES, s, mh, ml, mb, args);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) {
             err = std::string("GEMM launch failed: ") + cudaGetErrorString(e);
@@ -109,7 +129,7 @@ int gemm(const uint16_t* a_hi, const uint16_t* a_lo, int lda, const uint16_t* b,
     }
     GemmArgs args{y, M, N, K, ldy, err_word, (long long)M * ldy};
     dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, ksplit);
-    gemm_bf16x2_kernel<<<grid, THREADS, SMEM_BYTES, s>>>(mh, ml, mb, args);
+    launch(gemm_bf16x2_kernel, dim3(grid), dim3(THREADS), SMEM_BYTES, s, mh, ml, mb, args);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         err = std::string("GEMM launch failed: ") + cudaGetErrorString(e);
@@ -127,7 +147,7 @@ int gemm(const uint16_t* a_hi, const uint16_t* a_lo, int lda, const uint16_t* b,
 // bf16 hi/lo halves of f32 activations (see tc_gemm.cuh).
 namespace pf {
 
-constexpr int ROW_THREADS = 256;
+constexpr int ROW_THREADS = 1024;  // norm_split: one row per CTA, one hidden element per thread
 
 int ksplit_for(int M, int N, int K) {
     const int tiles = ((M + 127) / 128) * ((N + 127) / 128);
@@ -151,12 +171,14 @@ __device__ __forceinline__ void split_store(float v, uint16_t* hi, uint16_t* lo,
 
 // X[t] = f32(embed[ids[t]]) (cpu_inference.rs:109-111)
 __global__ void embed_rows(const uint32_t* ids, int H, const uint16_t* embed, float* X) {
+    pdl_wait();
+    pdl_trigger();
     const int t = blockIdx.x;
     const uint16_t* e = embed + (size_t)ids[t] * H;
     for (int i = threadIdx.x; i < H; i += blockDim.x) X[(size_t)t * H + i] = bf16f(e[i]);
 }
 
-__device__ float block_sum256(float v, float* red) {
+__device__ float block_sum(float v, float* red) {
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
     __syncthreads();
@@ -171,28 +193,44 @@ __device__ float block_sum256(float v, float* red) {
 // (cpu_inference.rs:189-194)
 __global__ void __launch_bounds__(ROW_THREADS) norm_split(float* X, int H, const uint16_t* gain, float eps, uint16_t* hi,
                                                           uint16_t* lo, const float* parts, int nparts, size_t part_stride) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float red[ROW_THREADS / 32];
     const int t = blockIdx.x;
     float* x = X + (size_t)t * H;
     float ss = 0.f;
     for (int i = threadIdx.x; i < H; i += ROW_THREADS) {
         float v = x[i];
-        for (int z = 0; z < nparts; z++) v += parts[z * part_stride + (size_t)t * H + i];
+        const float* p = parts + (size_t)t * H + i;
+        int z = 0;
+        for (; z + 4 <= nparts; z += 4) {  // four slice loads in flight, added in slice order
+            const float a = p[z * part_stride], b = p[(z + 1) * part_stride], c = p[(z + 2) * part_stride],
+                        d = p[(z + 3) * part_stride];
+            v += a;
+            v += b;
+            v += c;
+            v += d;
+        }
+        for (; z < nparts; z++) v += p[z * part_stride];
         if (nparts) x[i] = v;
         ss = fmaf(v, v, ss);
     }
-    const float sc = rsqrtf(block_sum256(ss, red) / (float)H + eps);
+    const float sc = rsqrtf(block_sum(ss, red) / (float)H + eps);
     for (int i = threadIdx.x; i < H; i += ROW_THREADS) split_store(x[i] * sc * bf16f(gain[i]), hi, lo, (size_t)t * H + i);
 }
 
 // A_hi/A_lo = split(src) over n rows of K
 __global__ void split_rows(const float* src, size_t total, uint16_t* hi, uint16_t* lo) {
+    pdl_wait();
+    pdl_trigger();
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x)
         split_store(src[i], hi, lo, i);
 }
 
 // X += the nparts slices of Y, in order (cpu_inference.rs:171-172)
 __global__ void residual_add(float* X, const float* Y, size_t total, int nparts) {
+    pdl_wait();
+    pdl_trigger();
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         float v = X[i];
         for (int z = 0; z < nparts; z++) v += Y[z * total + i];
@@ -203,6 +241,8 @@ __global__ void residual_add(float* X, const float* Y, size_t total, int nparts)
 // h[t][i] = silu(gate) * up from the interleaved gate/up outputs Y[t][2i], Y[t][2i+1] (the sum of
 // nparts split-K slices, in order), split for the down GEMM (cpu_inference.rs:166-170, :187)
 __global__ void silu_split(const float* Y, size_t n_inter, uint16_t* hi, uint16_t* lo, int nparts) {
+    pdl_wait();
+    pdl_trigger();
     const size_t ps = 2 * n_inter;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_inter; i += (size_t)gridDim.x * blockDim.x) {
         float g = Y[2 * i], u = Y[2 * i + 1];
@@ -221,6 +261,8 @@ __global__ void silu_split(const float* Y, size_t n_inter, uint16_t* hi, uint16_
 // token t is row t, at rows[t].pos of its own cache.
 __global__ void qkv_post(const float* Y, int nparts, int n, int start, int NQ, int NKV, const uint16_t* qn,
                          const uint16_t* kn, float eps, CacheView c, const RowView* rows, int layer, float* Q) {
+    pdl_wait();
+    pdl_trigger();
     const int warps = blockDim.x >> 5;
     const int item = blockIdx.x * warps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     const int per_tok = NQ + 2 * NKV;
@@ -332,6 +374,8 @@ template <int G>
 __global__ void __launch_bounds__(AT_THREADS) attention(const float* Q, float* att, const float* Kc, const float* Vc, int n,
                                                         int start, int NQ, size_t head_stride_l, int max_seq, float scale,
                                                         float* part, int slots) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int QT = AttTile<G>::QT;
     constexpr int R = QT * G;           // query rows of the tile
     constexpr int RB = R / 4;           // row blocks of 4
@@ -500,6 +544,8 @@ __global__ void __launch_bounds__(AT_THREADS) attention(const float* Q, float* a
 // row groups of 4); warp w takes row 4 * blockIdx.z + w, lane the dims 4 lane .. 4 lane + 3.
 template <int G>
 __global__ void __launch_bounds__(128) attention_merge(float* att, const float* part, int n, int start, int NQ, int slots) {
+    pdl_wait();
+    pdl_trigger();
     constexpr int QT = AttTile<G>::QT, R = QT * G;
     const int g = blockIdx.y, lane = threadIdx.x & 31, r = blockIdx.z * 4 + (threadIdx.x >> 5);
     int tile = (n + QT - 1) / QT - 1, slot = 0, k = blockIdx.x, nsp = 1;
@@ -543,13 +589,14 @@ int launch_attention(const float* Q, float* att, const float* Kc, const float* V
     if (cudaFuncSetAttribute(attention<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return QW_ERR_CUDA;
     const AttPlan pl = att_plan(AttTile<G>::QT, n, start);
     if ((size_t)NKV * pl.slots * AttTile<G>::QT * G * PPITCH > part_cap) return QW_ERR_ARG;
-    attention<G><<<dim3(pl.items, NKV), AT_THREADS, smem, s>>>(Q, att, Kc, Vc, n, start, NQ, hsl, max_seq, scale, part,
-                                                                 pl.slots);
+    launch(attention<G>, dim3(pl.items, NKV), dim3(AT_THREADS), smem, s, Q, att, Kc, Vc, n, start, NQ, hsl, max_seq, scale,
+           part, pl.slots);
     int split_tiles = 0;
     for (int t = (n + AttTile<G>::QT - 1) / AttTile<G>::QT - 1; t >= 0; t--)
         split_tiles += tile_splits(t, AttTile<G>::QT, n, start) > 1;
     if (split_tiles)
-        attention_merge<G><<<dim3(split_tiles, NKV, AttTile<G>::QT * G / 4), 128, 0, s>>>(att, part, n, start, NQ, pl.slots);
+        launch(attention_merge<G>, dim3(split_tiles, NKV, AttTile<G>::QT * G / 4), dim3(128), 0, s, att, part, n, start, NQ,
+               pl.slots);
     return QW_OK;
 }
 
@@ -566,7 +613,9 @@ int grid_for(size_t total) { return (int)std::min<size_t>((total + 255) / 256, 1
 // cache. Attention is per (row, KV head, split of ROW_SPLIT positions) — flash-decoding — and a
 // merge per (row, q head) combines the splits and writes the o_proj input halves directly.
 
-constexpr int RA_THREADS = 128;        // 4 warps; warp w takes positions p0 + w, p0 + w + 4, ...
+constexpr int RA_WARPS = 8;            // warp w takes positions p0 + w + 8 j, j < ROW_SPLIT / 8
+constexpr int RA_THREADS = RA_WARPS * 32;
+constexpr int RA_PER_WARP = ROW_SPLIT / RA_WARPS;
 
 // One (row b, KV head g, split z): the G query heads of g against positions
 // [z * ROW_SPLIT, min((z + 1) * ROW_SPLIT, pos + 1)) of the row's cache; writes (unnormalised
@@ -576,8 +625,10 @@ constexpr int RA_THREADS = 128;        // 4 warps; warp w takes positions p0 + w
 template <int G>
 __global__ void __launch_bounds__(RA_THREADS) row_attention(const float* Q, const RowView* rows, int NQ, int NKV, int layer,
                                                             float scale, float* part, int splits) {
-    __shared__ float sm_o[4][G][128];
-    __shared__ float sm_m[4][G], sm_l[4][G];
+    pdl_wait();
+    pdl_trigger();
+    __shared__ float sm_o[RA_WARPS][G][128];
+    __shared__ float sm_m[RA_WARPS][G], sm_l[RA_WARPS][G];
     const int b = blockIdx.x, g = blockIdx.y, z = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const RowView rv = rows[b];
@@ -596,9 +647,20 @@ __global__ void __launch_bounds__(RA_THREADS) row_attention(const float* Q, cons
         m[h] = -INFINITY;
         l[h] = 0.f;
     }
-    for (int p = p_begin + warp; p < p_end; p += 4) {
-        const float4 k4 = reinterpret_cast<const float4*>(kb + (size_t)p * 128)[lane];
-        const float4 v4 = reinterpret_cast<const float4*>(vb + (size_t)p * 128)[lane];
+    // all of this warp's K and V rows in flight at once, then the online softmax over them
+    float4 kr[RA_PER_WARP], vr[RA_PER_WARP];
+#pragma unroll
+    for (int j = 0; j < RA_PER_WARP; j++) {
+        const int p = p_begin + warp + RA_WARPS * j;
+        if (p < p_end) {
+            kr[j] = reinterpret_cast<const float4*>(kb + (size_t)p * 128)[lane];
+            vr[j] = reinterpret_cast<const float4*>(vb + (size_t)p * 128)[lane];
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < RA_PER_WARP; j++) {
+        if (p_begin + warp + RA_WARPS * j >= p_end) break;
+        const float4 k4 = kr[j], v4 = vr[j];
 #pragma unroll
         for (int h = 0; h < G; h++) {
             float d = q[h].x * k4.x + q[h].y * k4.y + q[h].z * k4.z + q[h].w * k4.w;
@@ -625,13 +687,13 @@ __global__ void __launch_bounds__(RA_THREADS) row_attention(const float* Q, cons
         }
     }
     __syncthreads();
-    // combine the 4 warps in warp order: thread t -> head t / 32 .. (dims 4 lane), one head per warp
-    for (int h = warp; h < G; h += 4) {
+    // combine the warps in warp order, one head per warp (dims 4 lane .. 4 lane + 3)
+    for (int h = warp; h < G; h += RA_WARPS) {
         float M = -INFINITY;
-        for (int w = 0; w < 4; w++) M = fmaxf(M, sm_m[w][h]);
+        for (int w = 0; w < RA_WARPS; w++) M = fmaxf(M, sm_m[w][h]);
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         float L = 0.f;
-        for (int w = 0; w < 4; w++) {
+        for (int w = 0; w < RA_WARPS; w++) {
             const float mw = sm_m[w][h];
             const float f = mw == -INFINITY ? 0.f : __expf(mw - M);
             const float4 ow = reinterpret_cast<const float4*>(sm_o[w][h])[lane];
@@ -655,6 +717,8 @@ __global__ void __launch_bounds__(RA_THREADS) row_attention(const float* Q, cons
 // head, 4 heads per block.
 __global__ void __launch_bounds__(128) row_merge(const float* part, const RowView* rows, int NQ, int splits, uint16_t* hi,
                                                  uint16_t* lo) {
+    pdl_wait();
+    pdl_trigger();
     const int b = blockIdx.x, head = blockIdx.y * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (head >= NQ) return;
     const int live = rows[b].pos / ROW_SPLIT + 1;
@@ -697,6 +761,8 @@ constexpr int AR_THREADS = 1024;
 // + b]; the row then advances to pos + 1 (the next step's input position).
 __global__ void __launch_bounds__(AR_THREADS) argmax_rows_kernel(const float* logits, int V, int B, RowView* rows,
                                                                  uint32_t* tok, uint32_t* out) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float sv[AR_THREADS / 32];
     __shared__ unsigned si[AR_THREADS / 32];
     const int b = blockIdx.x;
@@ -742,7 +808,7 @@ size_t row_partial_floats(int B, int NQ, int splits) { return (size_t)B * NQ * s
 
 int argmax_rows(const float* d_logits, int V, int B, RowView* d_rows, uint32_t* d_tok, uint32_t* d_out, cudaStream_t s,
                 std::string& err) {
-    argmax_rows_kernel<<<B, AR_THREADS, 0, s>>>(d_logits, V, B, d_rows, d_tok, d_out);
+    launch(argmax_rows_kernel, dim3(B), dim3(AR_THREADS), 0, s, d_logits, V, B, d_rows, d_tok, d_out);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         err = std::string("argmax launch failed: ") + cudaGetErrorString(e);
@@ -761,7 +827,7 @@ static int forward_pass(const Weights& w, const CacheView& c, const RowView* row
         err = "GEMM output scratch too small";
         return QW_ERR_ARG;
     }
-    embed_rows<<<n, 256, 0, s>>>(d_ids, H, w.embed, sc.X);
+    launch(embed_rows, dim3(n), dim3(256), 0, s, d_ids, H, w.embed, sc.X);
     const int G = NQ / NKV;
     const float scale = 1.0f / sqrtf(128.0f);
     const int ks_qkv = ksplit_for(n, QKVR, H), ks_o = ksplit_for(n, H, QD), ks_gu = ksplit_for(n, 2 * I, H),
@@ -771,22 +837,22 @@ static int forward_pass(const Weights& w, const CacheView& c, const RowView* row
         const uint16_t* nrm = w.layer_n + (size_t)l * w.norm_stride;
         int rc;
         // A: (the previous layer's down_proj slices into X) rmsnorm -> q|k|v
-        norm_split<<<n, ROW_THREADS, 0, s>>>(sc.X, H, nrm, w.eps, sc.ahi, sc.alo, sc.Y, l == 0 ? 0 : ks_d, nH);
+        launch(norm_split, dim3(n), dim3(ROW_THREADS), 0, s, sc.X, H, nrm, w.eps, sc.ahi, sc.alo, sc.Y, l == 0 ? 0 : ks_d, nH);
         if ((rc = tc::gemm(sc.ahi, sc.alo, H, W, H, sc.Y, QKVR, n, QKVR, H, err_word, s, err, ks_qkv))) return rc;
         // B: q/k norm + RoPE, K/V into the cache, attention -> o_proj input halves
         const int items = n * (NQ + 2 * NKV);
-        qkv_post<<<(items + 7) / 8, 256, 0, s>>>(sc.Y, ks_qkv, n, start, NQ, NKV, nrm + 2 * H, nrm + 2 * H + 128, w.eps, c,
-                                                 rows, l, sc.Q);
+        launch(qkv_post, dim3((items + 7) / 8), dim3(256), 0, s, sc.Y, ks_qkv, n, start, NQ, NKV, nrm + 2 * H,
+               nrm + 2 * H + 128, w.eps, c, rows, l, sc.Q);
         if (rows) {
             if (row_partial_floats(n, NQ, splits) > sc.attp_cap) {
                 err = "row attention partial buffer too small";
                 return QW_ERR_ARG;
             }
             const dim3 ag(n, NKV, splits);
-            if (G == 1) row_attention<1><<<ag, RA_THREADS, 0, s>>>(sc.Q, rows, NQ, NKV, l, scale, sc.attp, splits);
-            else if (G == 2) row_attention<2><<<ag, RA_THREADS, 0, s>>>(sc.Q, rows, NQ, NKV, l, scale, sc.attp, splits);
-            else row_attention<3><<<ag, RA_THREADS, 0, s>>>(sc.Q, rows, NQ, NKV, l, scale, sc.attp, splits);
-            row_merge<<<dim3(n, (NQ + 3) / 4), 128, 0, s>>>(sc.attp, rows, NQ, splits, sc.ahi, sc.alo);
+            if (G == 1) launch(row_attention<1>, dim3(ag), dim3(RA_THREADS), 0, s, sc.Q, rows, NQ, NKV, l, scale, sc.attp, splits);
+            else if (G == 2) launch(row_attention<2>, dim3(ag), dim3(RA_THREADS), 0, s, sc.Q, rows, NQ, NKV, l, scale, sc.attp, splits);
+            else launch(row_attention<3>, dim3(ag), dim3(RA_THREADS), 0, s, sc.Q, rows, NQ, NKV, l, scale, sc.attp, splits);
+            launch(row_merge, dim3(n, (NQ + 3) / 4), dim3(128), 0, s, sc.attp, rows, NQ, splits, sc.ahi, sc.alo);
         } else {
             const size_t hsl = (size_t)l * NKV * c.max_seq * 128;
             rc = G == 1 ? launch_attention<1>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, sc.attp, sc.attp_cap, s)
@@ -797,26 +863,26 @@ static int forward_pass(const Weights& w, const CacheView& c, const RowView* row
                                        : "cannot raise the prefill attention kernel's shared-memory limit";
                 return rc;
             }
-            split_rows<<<grid_for((size_t)n * QD), 256, 0, s>>>(sc.att, (size_t)n * QD, sc.ahi, sc.alo);
+            launch(split_rows, dim3(grid_for((size_t)n * QD)), dim3(256), 0, s, sc.att, (size_t)n * QD, sc.ahi, sc.alo);
         }
         // C: o_proj (its slices go into X in the next norm)
         if ((rc = tc::gemm(sc.ahi, sc.alo, QD, W + (size_t)QKVR * H, QD, sc.Y, H, n, H, QD, err_word, s, err, ks_o))) return rc;
         // D: residual + rmsnorm -> gate|up -> silu(gate) * up
-        norm_split<<<n, ROW_THREADS, 0, s>>>(sc.X, H, nrm + H, w.eps, sc.ahi, sc.alo, sc.Y, ks_o, nH);
+        launch(norm_split, dim3(n), dim3(ROW_THREADS), 0, s, sc.X, H, nrm + H, w.eps, sc.ahi, sc.alo, sc.Y, ks_o, nH);
         const uint16_t* Wgu = W + (size_t)QKVR * H + (size_t)H * QD;
         if ((rc = tc::gemm(sc.ahi, sc.alo, H, Wgu, H, sc.Y, 2 * I, n, 2 * I, H, err_word, s, err, ks_gu))) return rc;
-        silu_split<<<grid_for((size_t)n * I), 256, 0, s>>>(sc.Y, (size_t)n * I, sc.ahi, sc.alo, ks_gu);
+        launch(silu_split, dim3(grid_for((size_t)n * I)), dim3(256), 0, s, sc.Y, (size_t)n * I, sc.ahi, sc.alo, ks_gu);
         // E: down (its slices go into X in the next layer's norm)
         const uint16_t* Wd = Wgu + (size_t)2 * I * H;
         if ((rc = tc::gemm(sc.ahi, sc.alo, I, Wd, I, sc.Y, H, n, H, I, err_word, s, err, ks_d))) return rc;
     }
     // the last down_proj's slices go into X with the final norm; without logits, add them alone
     if (d_logits) {
-        norm_split<<<n, ROW_THREADS, 0, s>>>(sc.X, H, w.final_norm, w.eps, sc.ahi, sc.alo, sc.Y, ks_d, nH);
+        launch(norm_split, dim3(n), dim3(ROW_THREADS), 0, s, sc.X, H, w.final_norm, w.eps, sc.ahi, sc.alo, sc.Y, ks_d, nH);
         int rc;
         if ((rc = tc::gemm(sc.ahi, sc.alo, H, w.lm_head, H, d_logits, w.V, n, w.V, H, err_word, s, err, 1))) return rc;
     } else {
-        residual_add<<<grid_for(nH), 256, 0, s>>>(sc.X, sc.Y, nH, ks_d);
+        launch(residual_add, dim3(grid_for(nH)), dim3(256), 0, s, sc.X, sc.Y, nH, ks_d);
     }
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {

@@ -10,6 +10,14 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 }
 
 // ---- mbarrier ------------------------------------------------------------------------------
+// Programmatic dependent launch: a kernel launched with programmatic stream serialization may
+// start while the previous kernel in the stream is still running. pdl_wait() blocks the calling
+// thread until that kernel has completed and its writes are visible; pdl_trigger() lets the next
+// kernel launch once every CTA of this one has called it (or exited). Without such a launch both
+// are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }

@@ -179,9 +179,25 @@ gemm_bf16x2_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_con
     int issued_kb = 0;   // producer: K blocks whose copies were issued
 
     if (warp == 0 && lane == 0) {
-        for (int kb = 0; kb < nkb; kb++) {
+        // the first stages' weight tiles do not depend on the previous kernel: issue them before
+        // waiting for it (programmatic dependent launch), the activation tiles after
+        const int pre = nkb < STAGES ? nkb : STAGES;
+        for (int kb = 0; kb < pre; kb++) {
+            uint8_t* st = ring + (kb % STAGES) * STAGE_BYTES;
+            mbar_arrive_expect_tx(&full[kb], STAGE_BYTES);
+            tma_load_2d(st + 2 * TILE_A, &map_b, (kb0 + kb) * BK, n0, &full[kb]);
+        }
+        pdl_wait();
+        pdl_trigger();
+        for (int kb = 0; kb < pre; kb++) {
+            uint8_t* st = ring + (kb % STAGES) * STAGE_BYTES;
+            tma_load_2d(st, &map_ahi, (kb0 + kb) * BK, m0, &full[kb]);
+            tma_load_2d(st + TILE_A, &map_alo, (kb0 + kb) * BK, m0, &full[kb]);
+        }
+        issued_kb = pre;
+        for (int kb = pre; kb < nkb; kb++) {
             const int s = kb % STAGES;
-            if (kb >= STAGES && !bounded_wait(&empty[s], ((kb / STAGES) - 1) & 1, &abort_flag)) break;
+            if (!bounded_wait(&empty[s], ((kb / STAGES) - 1) & 1, &abort_flag)) break;
             uint8_t* st = ring + s * STAGE_BYTES;
             mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
             tma_load_2d(st, &map_ahi, (kb0 + kb) * BK, m0, &full[s]);
@@ -305,9 +321,23 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap map_xhi, const __grid_con
     int issued_kb = 0;
 
     if (warp == 0 && lane == 0) {
-        for (int kb = 0; kb < nkb; kb++) {
+        // weight tiles of the first stages before waiting for the previous kernel, activations after
+        const int pre = nkb < SK_STAGES ? nkb : SK_STAGES;
+        for (int kb = 0; kb < pre; kb++) {
+            mbar_arrive_expect_tx(&full[kb], SK_STAGE_BYTES);
+            tma_load_2d(ring + kb * SK_STAGE_BYTES, &map_w, (kb0 + kb) * BK, n0, &full[kb]);
+        }
+        pdl_wait();
+        pdl_trigger();
+        for (int kb = 0; kb < pre; kb++) {
+            uint8_t* st = ring + kb * SK_STAGE_BYTES;
+            tma_load_2d(st + SK_TILE_W, &map_xhi, (kb0 + kb) * BK, 0, &full[kb]);
+            tma_load_2d(st + SK_TILE_W + SK_TILE_X, &map_xlo, (kb0 + kb) * BK, 0, &full[kb]);
+        }
+        issued_kb = pre;
+        for (int kb = pre; kb < nkb; kb++) {
             const int s = kb % SK_STAGES;
-            if (kb >= SK_STAGES && !bounded_wait(&empty[s], ((kb / SK_STAGES) - 1) & 1, &abort_flag)) break;
+            if (!bounded_wait(&empty[s], ((kb / SK_STAGES) - 1) & 1, &abort_flag)) break;
             uint8_t* st = ring + s * SK_STAGE_BYTES;
             mbar_arrive_expect_tx(&full[s], SK_STAGE_BYTES);
             tma_load_2d(st, &map_w, (kb0 + kb) * BK, n0, &full[s]);
