@@ -119,6 +119,27 @@ int qw_decode_batch(qw_model* model, qw_cache* const* caches, size_t B, const ui
 int qw_decode_batch_device(qw_model* model, qw_cache* const* caches, size_t B, const uint32_t* d_firsts,
                            const size_t* start_pos, size_t steps, uint32_t* d_out, void* stream);
 
+/* Prompt-lookup speculative greedy decode (the reference's proposed route past one token per weight
+ * pass, README.md:109-111: "same greedy output with more than one token per pass"). Same contract
+ * as qw_decode (`first` goes in at start_pos, `steps` greedy output tokens into tokens_out), plus
+ * the token history `context[0..context_len)` (e.g. the prompt) that drafts are looked up in. Per
+ * pass: the longest n-gram of at most max_ngram tokens that ends the history (context, first and
+ * the tokens produced so far) and occurred earlier proposes the up to draft_max tokens that followed
+ * its latest earlier occurrence; one multi-token forward over the current token and the draft
+ * (tcgen05 GEMMs, as qw_prefill) checks them all, and the matching prefix plus the next greedy token
+ * are emitted. Without a draft a pass is one decode-kernel step. Positions written for rejected
+ * drafts are overwritten by later passes. stats (may be NULL) counts passes, drafted and accepted
+ * tokens. Synchronous. */
+#define QW_LOOKUP_DRAFT_MAX 15
+typedef struct {
+    uint64_t passes;    /* forward passes (verify passes and single decode steps) */
+    uint64_t drafted;   /* draft tokens proposed */
+    uint64_t accepted;  /* draft tokens accepted */
+} qw_lookup_stats;
+int qw_decode_lookup(qw_model* model, qw_cache* cache, const uint32_t* context, size_t context_len, uint32_t first,
+                     size_t start_pos, size_t steps, uint32_t max_ngram, uint32_t draft_max, uint32_t* tokens_out,
+                     qw_lookup_stats* stats);
+
 /* MetalModel::decode (metal_inference.rs:297-316): greedy decode; `first` goes in at `start_pos`,
  * each step's argmax feeds the next, and on_token(user, t) is called with each step's output
  * token as soon as the GPU produces it (steps calls). The whole run is one kernel launch. */

@@ -833,6 +833,104 @@ int qw_decode_batch_device(qw_model* m, qw_cache* const* caches, size_t B, const
     return QW_OK;
 }
 
+namespace {
+
+// Prompt lookup (the draft source of the reference's proposed speculation, README.md:109-111): the
+// longest n-gram, max_ngram down to 1 tokens, that ends the history and also occurs earlier; the
+// tokens that followed its most recent earlier occurrence, at most k of them, are the draft.
+size_t lookup_draft(const std::vector<uint32_t>& h, size_t max_ngram, size_t k, std::vector<uint32_t>& draft) {
+    draft.clear();
+    const size_t L = h.size();
+    if (L < 2 || k == 0) return 0;
+    for (size_t n = std::min(max_ngram, L - 1); n >= 1; n--) {
+        for (size_t i = L - n; i-- > 0;) {  // occurrences starting at i, latest first, each followed by a token
+            if (std::equal(h.begin() + (long)i, h.begin() + (long)(i + n), h.end() - (long)n)) {
+                const size_t cnt = std::min(k, L - (i + n));
+                draft.assign(h.begin() + (long)(i + n), h.begin() + (long)(i + n + cnt));
+                return cnt;
+            }
+        }
+    }
+    return 0;
+}
+
+}  // namespace
+
+int qw_decode_lookup(qw_model* m, qw_cache* c, const uint32_t* context, size_t context_len, uint32_t first,
+                     size_t start_pos, size_t steps, uint32_t max_ngram, uint32_t draft_max, uint32_t* tokens_out,
+                     qw_lookup_stats* stats) {
+    if (!m || !c || c->m != m || c->model_id != m->id || (!context && context_len)) return set_err(QW_ERR_ARG, "null or mismatched handle");
+    if (stats) *stats = qw_lookup_stats{0, 0, 0};
+    if (steps == 0) return QW_OK;
+    if (!tokens_out) return set_err(QW_ERR_ARG, "null tokens_out");
+    if (max_ngram < 1 || draft_max < 1 || draft_max > QW_LOOKUP_DRAFT_MAX)
+        return set_err(QW_ERR_ARG, "lookup: max_ngram >= 1 and 1 <= draft_max <= QW_LOOKUP_DRAFT_MAX");
+    if (start_pos + steps > c->max_seq) return set_err(QW_ERR_ARG, "start_pos + steps exceeds the KV cache size");
+    if (first >= m->cfg.vocab) return set_err(QW_ERR_ARG, "token id >= vocab_size");
+    QW_CUDA(cudaSetDevice(m->device));
+    if (int e = ensure_token_capacity(m, 2)) return e;
+    // (attention scratch sized for the last position a verify pass can start at)
+    if (int e = ensure_prefill(m, draft_max + 1, start_pos + steps, true)) return e;
+    if (!m->d_btok) QW_CUDA(cudaMalloc(&m->d_btok, qw::pf::ROWS_MAX * 4));
+    int* ew = qw::device_err_word_for(m->device);
+    if (!ew) return set_err(QW_ERR_NOMEM, "error word allocation failed");
+    cudaStream_t s = m->stream;
+    QW_CUDA(cudaMemsetAsync(ew, 0, sizeof(int), s));
+    const qw::pf::Weights w = weights_of(m);
+    const qw::pf::CacheView cv{c->d_k, c->d_v, c->d_rope, (int)c->max_seq};
+    std::vector<uint32_t> hist(context, context + context_len);
+    hist.push_back(first);
+    std::vector<uint32_t> draft, ids, got(draft_max + 1);
+    uint32_t cur = first;
+    size_t pos = start_pos, emitted = 0;
+    qw_lookup_stats st{0, 0, 0};
+    while (emitted < steps) {
+        const size_t remaining = steps - emitted;
+        lookup_draft(hist, max_ngram, std::min<size_t>(draft_max, remaining - 1), draft);
+        size_t take;
+        if (draft.empty()) {
+            // no draft: one token through the persistent decode kernel
+            m->h_stage[0] = cur;
+            QW_CUDA(cudaMemcpyAsync(m->d_tok, m->h_stage, 4, cudaMemcpyHostToDevice, s));
+            if (int e = launch_decode(m, c, m->d_tok, m->d_tok, false, nullptr, pos, 1, s)) return e;
+            QW_CUDA(cudaMemcpyAsync(got.data(), m->d_tok + 1, 4, cudaMemcpyDeviceToHost, s));
+            QW_CUDA(cudaStreamSynchronize(s));
+            if (int e = check_device_err(m)) return e;
+            take = 1;
+        } else {
+            // verify pass: cur and the drafts at pos .. pos + len in one multi-token forward
+            ids.assign(1, cur);
+            ids.insert(ids.end(), draft.begin(), draft.end());
+            const size_t n = ids.size();
+            QW_CUDA(cudaMemcpyAsync(m->d_pf_ids, ids.data(), n * 4, cudaMemcpyHostToDevice, s));
+            std::string err;
+            if (int e = qw::pf::run(w, cv, m->d_pf_ids, (int)n, (int)pos, m->d_pf_logits, m->pf, ew, s, err)) return set_err(e, err);
+            if (int e = qw::pf::argmax_each(m->d_pf_logits, (int)m->cfg.vocab, (int)n, m->d_btok, s, err)) return set_err(e, err);
+            QW_CUDA(cudaMemcpyAsync(got.data(), m->d_btok, n * 4, cudaMemcpyDeviceToHost, s));
+            int h = 0;
+            QW_CUDA(cudaMemcpyAsync(&h, ew, sizeof(int), cudaMemcpyDeviceToHost, s));
+            QW_CUDA(cudaStreamSynchronize(s));
+            if (h) return set_err(QW_ERR_DEVICE_TIMEOUT, "lookup verify pass: a GEMM pipeline wait expired on the device");
+            // got[i] is the greedy token after ids[0..i]; draft i is right while it equals got[i]
+            size_t a = 0;
+            while (a < draft.size() && draft[a] == got[a]) a++;
+            take = a + 1;
+            st.drafted += draft.size();
+            st.accepted += a;
+        }
+        st.passes++;
+        for (size_t i = 0; i < take; i++) {
+            tokens_out[emitted + i] = got[i];
+            hist.push_back(got[i]);
+        }
+        emitted += take;
+        pos += take;
+        cur = got[take - 1];
+    }
+    if (stats) *stats = st;
+    return QW_OK;
+}
+
 int qw_forward(qw_model* m, qw_cache* c, uint32_t token, size_t pos, float* logits_out) {
     if (!m || !c || !logits_out || c->m != m || c->model_id != m->id) return set_err(QW_ERR_ARG, "null or mismatched handle");
     if (token >= m->cfg.vocab) return set_err(QW_ERR_ARG, "token id >= vocab_size");

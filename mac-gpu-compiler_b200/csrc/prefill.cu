@@ -804,6 +804,55 @@ __global__ void __launch_bounds__(AR_THREADS) argmax_rows_kernel(const float* lo
     }
 }
 
+// d_out[t] = argmax of row t of d_logits ([n][V]) with the reference CPU rule; one block per row
+__global__ void __launch_bounds__(AR_THREADS) argmax_each_kernel(const float* logits, int V, uint32_t* out) {
+    pdl_wait();
+    pdl_trigger();
+    __shared__ float sv[AR_THREADS / 32];
+    __shared__ unsigned si[AR_THREADS / 32];
+    const float* x = logits + (size_t)blockIdx.x * V;
+    float bv = -INFINITY;
+    unsigned bi = AM_NONE;
+    for (int i = threadIdx.x; i < V; i += AR_THREADS) {
+        const float v = x[i];
+        if (!isnan(v) && am_wins(v, (unsigned)i, bv, bi)) {
+            bv = v;
+            bi = (unsigned)i;
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+        const unsigned oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+        if (am_wins(ov, oi, bv, bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    if ((threadIdx.x & 31) == 0) {
+        sv[threadIdx.x >> 5] = bv;
+        si[threadIdx.x >> 5] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < AR_THREADS / 32; w++)
+            if (am_wins(sv[w], si[w], bv, bi)) {
+                bv = sv[w];
+                bi = si[w];
+            }
+        out[blockIdx.x] = (isnan(x[0]) || bi == AM_NONE) ? 0u : bi;
+    }
+}
+
+int argmax_each(const float* d_logits, int V, int n, uint32_t* d_out, cudaStream_t s, std::string& err) {
+    launch(argmax_each_kernel, dim3(n), dim3(AR_THREADS), 0, s, d_logits, V, d_out);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        err = std::string("argmax launch failed: ") + cudaGetErrorString(e);
+        return QW_ERR_CUDA;
+    }
+    return QW_OK;
+}
+
 size_t row_partial_floats(int B, int NQ, int splits) { return (size_t)B * NQ * splits * PPITCH; }
 
 int argmax_rows(const float* d_logits, int V, int B, RowView* d_rows, uint32_t* d_tok, uint32_t* d_out, cudaStream_t s,

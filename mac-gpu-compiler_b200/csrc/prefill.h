@@ -94,5 +94,8 @@ int run_rows(const Weights& w, const RowView* d_rows, int B, int splits, const u
 int argmax_rows(const float* d_logits, int V, int B, RowView* d_rows, uint32_t* d_tok, uint32_t* d_out, cudaStream_t s,
                 std::string& err);
 
+// d_out[t] = argmax(d_logits[t]) for t < n (the reference CPU rule). Stream-ordered.
+int argmax_each(const float* d_logits, int V, int n, uint32_t* d_out, cudaStream_t s, std::string& err);
+
 }  // namespace pf
 }  // namespace qw

@@ -63,6 +63,11 @@ class Config:
 
 
 TOKEN_FN = ctypes.CFUNCTYPE(None, ctypes.c_void_p, ctypes.c_uint32)
+LOOKUP_DRAFT_MAX = 15
+
+
+class _LookupStats(ctypes.Structure):
+    _fields_ = [("passes", ctypes.c_uint64), ("drafted", ctypes.c_uint64), ("accepted", ctypes.c_uint64)]
 _lib = None
 
 
@@ -89,6 +94,7 @@ def lib() -> ctypes.CDLL:
             "qw_prefill_device": (i32, [vp, vp, vp, sz, sz, vp, vp]),
             "qw_decode": (i32, [vp, vp, u32, sz, sz, TOKEN_FN, vp]),
             "qw_forward_batch": (i32, [vp, vp, sz, vp, vp, vp]),
+            "qw_decode_lookup": (i32, [vp, vp, vp, sz, u32, sz, sz, u32, u32, vp, ctypes.POINTER(_LookupStats)]),
             "qw_decode_batch": (i32, [vp, vp, sz, vp, vp, sz, vp]),
             "qw_decode_batch_device": (i32, [vp, vp, sz, vp, vp, sz, vp, vp]),
             "qw_forward_device": (i32, [vp, vp, vp, sz, vp, vp]),
@@ -198,6 +204,17 @@ class CudaModel:
         fn = TOKEN_FN(cb)
         _check(lib().qw_decode(self._h, cache._h, first, start_pos, steps, fn, None))
         return got
+
+    def decode_lookup(self, context, first: int, start_pos: int, steps: int, cache: "CudaKVCache",
+                      max_ngram: int = 3, draft_max: int = 7) -> tuple[list[int], dict]:
+        """Prompt-lookup speculative greedy decode (qw_decode_lookup): the tokens decode() would give,
+        with drafts looked up in `context` + the output so far; returns (tokens, stats)."""
+        ctx = np.ascontiguousarray(np.asarray(context, dtype=np.uint32))
+        out = np.empty(steps, np.uint32)
+        st = _LookupStats()
+        _check(lib().qw_decode_lookup(self._h, cache._h, ctx.ctypes.data if ctx.size else None, ctx.size, first,
+                                      start_pos, steps, max_ngram, draft_max, out.ctypes.data, ctypes.byref(st)))
+        return [int(t) for t in out], {"passes": st.passes, "drafted": st.drafted, "accepted": st.accepted}
 
     # batch decode: B independent sequences, one cache each, stepping together (qw_*_batch)
     @staticmethod
