@@ -50,6 +50,9 @@ CONFIGS = {
                     label="configs[3]: 512-id prompt in one batched prefill pass (tcgen05 GEMMs), then 64 greedy decode steps"),
     "box": dict(prompt=130, decode=128, sequences=64,
                 label="configs[4]: 64 independent sequences (130-id prompt + 128 greedy steps each) sharded over the GPUs"),
+    "lookup": dict(prompt=130, decode=128, ngram=3, draft=15,
+                   label="configs[0] workload with prompt-lookup speculation (qw_decode_lookup, n-gram <= 3, "
+                         "draft <= 15): 130-id prompt, then 128 greedy tokens"),
     "box8": dict(prompt=130, decode=128, sequences=64, batch=8,
                  label="configs[4], batch-8 variant: 64 independent sequences (130-id prompt + 128 greedy steps each) "
                        "sharded over the GPUs, decoded 8 at a time per GPU (qw_decode_batch)"),
@@ -284,6 +287,67 @@ def run_batch(args, world: int, rank: int, local: int, pg) -> None:
     model.close()
 
 
+def run_lookup(args, world: int, rank: int, local: int, pg) -> None:
+    """configs[0]'s decode through prompt-lookup speculation: a step is one qw_decode_lookup call
+    (128 greedy tokens from position 130, drafts looked up in the prompt and the output), timed
+    with CUDA events on the model stream. The call is host-driven (each pass's accepted tokens come
+    back to the host), so `value` and `e2e` are the same call: host first token in, tokens out."""
+    import numpy as np
+    import torch
+    import cuda_inference as ci
+    c = CONFIGS["lookup"]
+    n_prompt, n_dec = c["prompt"], c["decode"]
+    path = randmodel.make_model("qwen3-0.6b", 0)
+    model = ci.CudaModel.load_model(path, device=local)
+    cfg = model.config
+    ids = randmodel.prompt_ids(n_prompt, cfg.vocab_size, seed=replicas.prompt_seed(rank))
+    cache = ci.CudaKVCache(model, n_prompt + n_dec + 1)
+    model.prefill(ids[:-1], 0, cache, logits=False)
+    first = int(np.argmax(model.forward(ids[-1], n_prompt - 1, cache)))
+    plain = model.decode(first, n_prompt, n_dec, cache)
+    stream = torch.cuda.ExternalStream(model.stream)
+
+    def step():
+        return model.decode_lookup(ids, first, n_prompt, n_dec, cache, max_ngram=c["ngram"], draft_max=c["draft"])
+
+    for _ in range(args.warmup):
+        toks, st = step()
+    torch.cuda.synchronize()
+    if pg is not None:
+        pg.barrier()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local) as clocks:
+        for i in range(args.steps):
+            evs[i][0].record(stream)
+            toks, st = step()
+            evs[i][1].record(stream)
+        torch.cuda.synchronize()
+    elapsed = sum(a.elapsed_time(b) for a, b in evs) / 1e3
+    box = replicas.aggregate(replicas.reduce_timings(replicas.RankTiming(n_dec * args.steps, elapsed),
+                                                     group=pg.group.WORLD if pg is not None else None))
+    same = next((i for i in range(n_dec) if toks[i] != plain[i]), n_dec)
+    if rank == 0:
+        line = {
+            "metric": "Qwen3-0.6B bf16 decode tok/s @bs1 & % of HBM roofline; box tok/s at 1-8 GPUs",
+            "value": box["tok_per_s"], "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": box["seconds"] / args.steps * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": box["tok_per_s"] / PUBLISHED_TPS, "dtype": "bf16", "accumulate": "f32", "data": "synthetic",
+            "config": {"workload": c["label"], "model": "Qwen3-0.6B geometry, random-init bf16 (seed 0)",
+                       "global_batch": world, "seq_len": n_prompt + n_dec,
+                       "parallelism": f"replicas x{world}, one sequence per rank, no collective",
+                       "step": f"one qw_decode_lookup call producing {n_dec} greedy tokens"},
+            "e2e": {"value": box["tok_per_s"], "unit": "tok/s", "h2d_bytes_per_step": 4 * (n_prompt + 1),
+                    "d2h_bytes_per_step": 4 * n_dec, "api": "qw_decode_lookup (host-driven passes)"},
+            "speculation": {"passes": st["passes"], "drafted": st["drafted"], "accepted": st["accepted"],
+                            "tokens_per_pass": n_dec / st["passes"],
+                            "equal_to_plain_decode_for_first": same},
+            "clocks": clocks.summary(),
+            "first_tokens": toks[:8],
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+
+
 def load_peaks() -> tuple[float, str]:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -445,8 +509,8 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
         pg = dist
-    if args.config in ("prefill", "box8"):
-        (run_prefill if args.config == "prefill" else run_batch)(args, world, rank, local, pg)
+    if args.config in ("prefill", "box8", "lookup"):
+        {"prefill": run_prefill, "box8": run_batch, "lookup": run_lookup}[args.config](args, world, rank, local, pg)
         if pg is not None:
             pg.barrier()
             pg.destroy_process_group()

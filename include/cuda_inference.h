@@ -124,12 +124,13 @@ int qw_decode_batch_device(qw_model* model, qw_cache* const* caches, size_t B, c
  * as qw_decode (`first` goes in at start_pos, `steps` greedy output tokens into tokens_out), plus
  * the token history `context[0..context_len)` (e.g. the prompt) that drafts are looked up in. Per
  * pass: the longest n-gram of at most max_ngram tokens that ends the history (context, first and
- * the tokens produced so far) and occurred earlier proposes the up to draft_max tokens that followed
- * its latest earlier occurrence; one multi-token forward over the current token and the draft
- * (tcgen05 GEMMs, as qw_prefill) checks them all, and the matching prefix plus the next greedy token
- * are emitted. Without a draft a pass is one decode-kernel step. Positions written for rejected
- * drafts are overwritten by later passes. stats (may be NULL) counts passes, drafted and accepted
- * tokens. Synchronous. */
+ * the tokens produced so far) and occurred earlier proposes the draft_max tokens that followed its
+ * latest earlier occurrence (continued periodically where that occurrence overlaps the end of the
+ * history); one multi-token forward over the current token and the draft (tcgen05 GEMMs, as
+ * qw_prefill, captured as a graph) checks them all, and the matching prefix plus the next greedy
+ * token are emitted. Without a draft of at least 2 tokens a pass is one decode-kernel step.
+ * Positions written for rejected drafts are overwritten by later passes. stats (may be NULL)
+ * counts passes, drafted and accepted tokens. Synchronous. */
 #define QW_LOOKUP_DRAFT_MAX 15
 typedef struct {
     uint64_t passes;    /* forward passes (verify passes and single decode steps) */

@@ -157,8 +157,17 @@ struct qw_model {
     uint32_t* d_btok = nullptr;          // [ROWS_MAX]
     uint32_t* d_bout = nullptr;
     size_t bout_cap = 0;                 // entries of d_bout
-    cudaGraphExec_t bgraph = nullptr;
-    struct { int B = 0, splits = 0; const void *X = nullptr, *Y = nullptr, *attp = nullptr, *logits = nullptr, *out = nullptr; } bsig;
+    // captured row-mode step graphs, by what they were captured for (kind 0: greedy batch step,
+    // kind 1: lookup verify pass) and the buffers they bake in
+    struct GraphKey {
+        int kind, B, splits;
+        const void *X, *Y, *attp, *logits, *out;
+        bool operator==(const GraphKey& o) const {
+            return kind == o.kind && B == o.B && splits == o.splits && X == o.X && Y == o.Y && attp == o.attp &&
+                   logits == o.logits && out == o.out;
+        }
+    };
+    std::vector<std::pair<GraphKey, cudaGraphExec_t>> graphs;
     unsigned epoch = 0;
     int S = 0, part_cap = 0, xs_cap = 0, xloc_cap = 0;
     u64* d_trace = nullptr;      // phase timeline of the most recent launch's first step, if enabled
@@ -450,7 +459,7 @@ void qw_free(qw_model* m) {
     cudaFree(m->pf.ahi);
     cudaFree(m->pf.alo);
     cudaFree(m->pf.attp);
-    if (m->bgraph) cudaGraphExecDestroy(m->bgraph);
+    for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);
     cudaFree(m->d_rows);
     cudaFree(m->d_btok);
     cudaFree(m->d_bout);
@@ -710,41 +719,39 @@ qw::pf::Weights weights_of(const qw_model* m) {
                            (int)cf.kv_heads, (int)cf.vocab, cf.eps};
 }
 
-// The graph of one greedy batch step (row-mode forward + argmax_rows into `out`), captured on the
-// model's stream the first time a configuration is used and replayed for every step after.
-int batch_graph(qw_model* m, int B, int splits, uint32_t* out, int* ew) {
-    auto& g = m->bsig;
-    if (m->bgraph && g.B == B && g.splits == splits && g.X == m->pf.X && g.Y == m->pf.Y && g.attp == m->pf.attp &&
-        g.logits == m->d_pf_logits && g.out == out)
-        return QW_OK;
-    if (m->bgraph) {
-        cudaGraphExecDestroy(m->bgraph);
-        m->bgraph = nullptr;
+// The graph of one row-mode step over B rows, captured on the model's stream the first time a
+// configuration is used and replayed after: kind 0 = greedy batch step (forward + argmax_rows,
+// tokens recorded into `out`, rows advanced); kind 1 = lookup verify pass (forward + argmax_each
+// into `out`).
+int row_graph(qw_model* m, int kind, int B, int splits, uint32_t* out, int* ew, cudaGraphExec_t& exec) {
+    const qw_model::GraphKey key{kind, B, splits, m->pf.X, m->pf.Y, m->pf.attp, m->d_pf_logits, out};
+    for (auto& g : m->graphs)
+        if (g.first == key) {
+            exec = g.second;
+            return QW_OK;
+        }
+    if (m->graphs.size() >= 32) {  // buffers moved or many shapes: start over
+        for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);
+        m->graphs.clear();
     }
     cudaStream_t s = m->stream;
     QW_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
     std::string err;
     int rc = qw::pf::run_rows(weights_of(m), m->d_rows, B, splits, m->d_btok, m->d_pf_logits, m->pf, ew, s, err);
-    if (!rc) rc = qw::pf::argmax_rows(m->d_pf_logits, (int)m->cfg.vocab, B, m->d_rows, m->d_btok, out, s, err);
+    if (!rc)
+        rc = kind == 0 ? qw::pf::argmax_rows(m->d_pf_logits, (int)m->cfg.vocab, B, m->d_rows, m->d_btok, out, s, err)
+                       : qw::pf::argmax_each(m->d_pf_logits, (int)m->cfg.vocab, B, out, s, err);
     cudaGraph_t graph = nullptr;
     const cudaError_t ce = cudaStreamEndCapture(s, &graph);
     if (rc) {
         if (graph) cudaGraphDestroy(graph);
         return set_err(rc, err);
     }
-    if (ce != cudaSuccess) return cuda_err(ce, "cudaStreamEndCapture (batch step)");
-    cudaGraphExec_t exec = nullptr;
+    if (ce != cudaSuccess) return cuda_err(ce, "cudaStreamEndCapture (row step)");
     const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
     cudaGraphDestroy(graph);
-    if (ie != cudaSuccess) return cuda_err(ie, "cudaGraphInstantiate (batch step)");
-    m->bgraph = exec;
-    g.B = B;
-    g.splits = splits;
-    g.X = m->pf.X;
-    g.Y = m->pf.Y;
-    g.attp = m->pf.attp;
-    g.logits = m->d_pf_logits;
-    g.out = out;
+    if (ie != cudaSuccess) return cuda_err(ie, "cudaGraphInstantiate (row step)");
+    m->graphs.emplace_back(key, exec);
     return QW_OK;
 }
 
@@ -759,10 +766,11 @@ int batch_decode_launch(qw_model* m, qw_cache* const* caches, size_t B, const si
     if (int e = ensure_batch(m, B, splits, steps * B)) return e;
     int* ew = qw::device_err_word_for(m->device);
     if (!ew) return set_err(QW_ERR_NOMEM, "error word allocation failed");
-    if (int e = batch_graph(m, (int)B, splits, m->d_bout, ew)) return e;
+    cudaGraphExec_t g = nullptr;
+    if (int e = row_graph(m, 0, (int)B, splits, m->d_bout, ew, g)) return e;
     QW_CUDA(cudaMemsetAsync(ew, 0, sizeof(int), s));
     QW_CUDA(cudaMemcpyAsync(m->d_rows, rows.data(), B * sizeof(qw::pf::RowView), cudaMemcpyHostToDevice, s));
-    for (size_t i = 0; i < steps; i++) QW_CUDA(cudaGraphLaunch(m->bgraph, s));
+    for (size_t i = 0; i < steps; i++) QW_CUDA(cudaGraphLaunch(g, s));
     return QW_OK;
 }
 
@@ -837,7 +845,10 @@ namespace {
 
 // Prompt lookup (the draft source of the reference's proposed speculation, README.md:109-111): the
 // longest n-gram, max_ngram down to 1 tokens, that ends the history and also occurs earlier; the
-// tokens that followed its most recent earlier occurrence, at most k of them, are the draft.
+// k tokens that followed its most recent earlier occurrence are the draft. Where that continuation
+// runs into the present (the occurrence overlaps the end of the history, as in a repeated token
+// or phrase), it continues from the draft itself, like an overlapping copy: the text is assumed to
+// keep repeating with the same period.
 size_t lookup_draft(const std::vector<uint32_t>& h, size_t max_ngram, size_t k, std::vector<uint32_t>& draft) {
     draft.clear();
     const size_t L = h.size();
@@ -845,14 +856,20 @@ size_t lookup_draft(const std::vector<uint32_t>& h, size_t max_ngram, size_t k, 
     for (size_t n = std::min(max_ngram, L - 1); n >= 1; n--) {
         for (size_t i = L - n; i-- > 0;) {  // occurrences starting at i, latest first, each followed by a token
             if (std::equal(h.begin() + (long)i, h.begin() + (long)(i + n), h.end() - (long)n)) {
-                const size_t cnt = std::min(k, L - (i + n));
-                draft.assign(h.begin() + (long)(i + n), h.begin() + (long)(i + n + cnt));
-                return cnt;
+                for (size_t j = 0; j < k; j++) {
+                    const size_t q = i + n + j;
+                    draft.push_back(q < L ? h[q] : draft[q - L]);
+                }
+                return k;
             }
         }
     }
     return 0;
 }
+
+// drafts shorter than this are not worth a verify pass (a pass over the weights for B rows costs
+// about two single-token decode steps); the token goes through the decode kernel instead
+constexpr size_t LOOKUP_MIN_DRAFT = 2;
 
 }  // namespace
 
@@ -869,15 +886,15 @@ int qw_decode_lookup(qw_model* m, qw_cache* c, const uint32_t* context, size_t c
     if (first >= m->cfg.vocab) return set_err(QW_ERR_ARG, "token id >= vocab_size");
     QW_CUDA(cudaSetDevice(m->device));
     if (int e = ensure_token_capacity(m, 2)) return e;
-    // (attention scratch sized for the last position a verify pass can start at)
-    if (int e = ensure_prefill(m, draft_max + 1, start_pos + steps, true)) return e;
-    if (!m->d_btok) QW_CUDA(cudaMalloc(&m->d_btok, qw::pf::ROWS_MAX * 4));
+    // verify passes run in row mode (row t = the pass's t-th token at pos + t of this one cache),
+    // as captured graphs; their attention splits cover the last position a pass can reach
+    const int splits = (int)((start_pos + steps - 1) / qw::pf::ROW_SPLIT + 1);
+    if (int e = ensure_batch(m, draft_max + 1, splits, 0)) return e;
     int* ew = qw::device_err_word_for(m->device);
     if (!ew) return set_err(QW_ERR_NOMEM, "error word allocation failed");
     cudaStream_t s = m->stream;
     QW_CUDA(cudaMemsetAsync(ew, 0, sizeof(int), s));
-    const qw::pf::Weights w = weights_of(m);
-    const qw::pf::CacheView cv{c->d_k, c->d_v, c->d_rope, (int)c->max_seq};
+    std::vector<qw::pf::RowView> rows;
     std::vector<uint32_t> hist(context, context + context_len);
     hist.push_back(first);
     std::vector<uint32_t> draft, ids, got(draft_max + 1);
@@ -888,7 +905,7 @@ int qw_decode_lookup(qw_model* m, qw_cache* c, const uint32_t* context, size_t c
         const size_t remaining = steps - emitted;
         lookup_draft(hist, max_ngram, std::min<size_t>(draft_max, remaining - 1), draft);
         size_t take;
-        if (draft.empty()) {
+        if (draft.size() < LOOKUP_MIN_DRAFT) {
             // no draft: one token through the persistent decode kernel
             m->h_stage[0] = cur;
             QW_CUDA(cudaMemcpyAsync(m->d_tok, m->h_stage, 4, cudaMemcpyHostToDevice, s));
@@ -902,11 +919,15 @@ int qw_decode_lookup(qw_model* m, qw_cache* c, const uint32_t* context, size_t c
             ids.assign(1, cur);
             ids.insert(ids.end(), draft.begin(), draft.end());
             const size_t n = ids.size();
-            QW_CUDA(cudaMemcpyAsync(m->d_pf_ids, ids.data(), n * 4, cudaMemcpyHostToDevice, s));
-            std::string err;
-            if (int e = qw::pf::run(w, cv, m->d_pf_ids, (int)n, (int)pos, m->d_pf_logits, m->pf, ew, s, err)) return set_err(e, err);
-            if (int e = qw::pf::argmax_each(m->d_pf_logits, (int)m->cfg.vocab, (int)n, m->d_btok, s, err)) return set_err(e, err);
-            QW_CUDA(cudaMemcpyAsync(got.data(), m->d_btok, n * 4, cudaMemcpyDeviceToHost, s));
+            rows.resize(n);
+            for (size_t t = 0; t < n; t++)
+                rows[t] = qw::pf::RowView{c->d_k, c->d_v, c->d_rope, (int)c->max_seq, (int)(pos + t), (int)(pos + t), 0};
+            cudaGraphExec_t g = nullptr;
+            if (int e = row_graph(m, 1, (int)n, splits, m->d_pf_ids, ew, g)) return e;
+            QW_CUDA(cudaMemcpyAsync(m->d_rows, rows.data(), n * sizeof(qw::pf::RowView), cudaMemcpyHostToDevice, s));
+            QW_CUDA(cudaMemcpyAsync(m->d_btok, ids.data(), n * 4, cudaMemcpyHostToDevice, s));
+            QW_CUDA(cudaGraphLaunch(g, s));
+            QW_CUDA(cudaMemcpyAsync(got.data(), m->d_pf_ids, n * 4, cudaMemcpyDeviceToHost, s));
             int h = 0;
             QW_CUDA(cudaMemcpyAsync(&h, ew, sizeof(int), cudaMemcpyDeviceToHost, s));
             QW_CUDA(cudaStreamSynchronize(s));
