@@ -542,11 +542,11 @@ __global__ void __launch_bounds__(AT_THREADS) attention(const float* Q, float* a
 // Combines the splits of each split tile: per row, M = max of the splits' running maxima, then
 // out = sum_j o_j e^(m_j - M) / sum_j l_j e^(m_j - M), splits in order. Grid (split tiles, KV heads,
 // row groups of 4); warp w takes row 4 * blockIdx.z + w, lane the dims 4 lane .. 4 lane + 3.
-template <int G>
+template <int G, int QT>
 __global__ void __launch_bounds__(128) attention_merge(float* att, const float* part, int n, int start, int NQ, int slots) {
     pdl_wait();
     pdl_trigger();
-    constexpr int QT = AttTile<G>::QT, R = QT * G;
+    constexpr int R = QT * G;
     const int g = blockIdx.y, lane = threadIdx.x & 31, r = blockIdx.z * 4 + (threadIdx.x >> 5);
     int tile = (n + QT - 1) / QT - 1, slot = 0, k = blockIdx.x, nsp = 1;
     for (; tile >= 0; tile--) {
@@ -595,14 +595,316 @@ int launch_attention(const float* Q, float* att, const float* Kc, const float* V
     for (int t = (n + AttTile<G>::QT - 1) / AttTile<G>::QT - 1; t >= 0; t--)
         split_tiles += tile_splits(t, AttTile<G>::QT, n, start) > 1;
     if (split_tiles)
-        launch(attention_merge<G>, dim3(split_tiles, NKV, AttTile<G>::QT * G / 4), dim3(128), 0, s, att, part, n, start, NQ,
-               pl.slots);
+        launch(attention_merge<G, AttTile<G>::QT>, dim3(split_tiles, NKV, AttTile<G>::QT * G / 4), dim3(128), 0, s, att, part,
+               n, start, NQ, pl.slots);
     return QW_OK;
 }
 
+// ---------------------------------------------------------------------------------------------
+// Causal GQA attention for the prefill on the tensor cores (tcgen05), for G = 1, 2 or 4 query heads
+// per KV head. A CTA takes 128 query rows (128 / G tokens x G heads of one KV head) and walks the
+// same 64-position chunks and position-range splits as the CUDA-core kernel above:
+//   S = Q . K^T   (M = 128 rows, N = 64 positions, K = 128 dims) into TMEM columns 0..63
+//   online softmax: thread = row reads its 64 scores from TMEM, masks positions after its own,
+//                   updates its running max / sum, writes P to shared memory and rescales its
+//                   row of O in TMEM (tcgen05.ld / tcgen05.st)
+//   O += P . V    (M = 128, N = 128 dims, K = 64 positions) into TMEM columns 64..191
+// Q, K, V (f32 in memory) and P are split into bf16 hi/lo halves as they are written to shared
+// memory in the 128-byte-swizzle K-major layout (V transposed: dims x positions); each product is
+// hi.hi + hi.lo + lo.hi, so scores and outputs keep about 16 bits of every f32 operand. One
+// thread issues the MMAs and commits them to an mbarrier per product; every wait is bounded.
+constexpr int TA_THREADS = 128;
+constexpr uint32_t TA_TMEM_COLS = 256, TA_S_COL = 0, TA_O_COL = 64;
+constexpr int TA_Q = 0, TA_QLO = 32768;                  // Q: 2 K blocks x [128 rows x 128 B] per half
+constexpr int TA_K = 65536, TA_KLO = TA_K + 16384;        // K chunk: 2 K blocks x [64 rows x 128 B] per half
+constexpr int TA_V = TA_K + 32768, TA_VLO = TA_V + 16384; // V^T chunk: [128 dims x 64 positions] per half
+constexpr int TA_P = TA_V + 32768, TA_PLO = TA_P + 16384; // P: [128 rows x 64 positions] per half
+constexpr int TA_SMEM = TA_P + 32768 + 1024;
+
+__device__ __forceinline__ uint32_t ta_sw128(int r, int c) {  // (row, column) of a [rows][64] bf16 swizzled tile
+    return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((((c >> 3) ^ r) & 7) << 4) + (c & 7) * 2);
+}
+__device__ __forceinline__ void ta_split(uint8_t* hi, uint8_t* lo, uint32_t off, float v) {
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    *reinterpret_cast<__nv_bfloat16*>(hi + off) = h;
+    *reinterpret_cast<__nv_bfloat16*>(lo + off) = __float2bfloat16_rn(v - __bfloat162float(h));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+        ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+          "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+          "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+          "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+template <int G>
+__global__ void __launch_bounds__(TA_THREADS, 1)
+attention_tc(const float* Q, float* att, const float* Kc, const float* Vc, int n, int start, int NQ, size_t head_stride_l,
+             int max_seq, float scale, float* part, int slots, int* err) {
+    constexpr int QT = 128 / G;
+    extern __shared__ __align__(1024) uint8_t ta_raw[];
+    __shared__ uint64_t bar_s, bar_o;
+    __shared__ uint32_t tmem_base;
+    __shared__ volatile int abort_flag;
+    pdl_wait();
+    pdl_trigger();
+    uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ta_raw) + 1023) & ~uintptr_t(1023));
+    const int g = blockIdx.y, tid = threadIdx.x, warp = tid >> 5;
+    // work item -> (tile, split), as attention<G>
+    int tile = (n + QT - 1) / QT - 1, item = blockIdx.x, slot = 0, nsp = 1;
+    for (; tile >= 0; tile--) {
+        nsp = tile_splits(tile, QT, n, start);
+        if (item < nsp) break;
+        item -= nsp;
+        if (nsp > 1) slot += nsp;
+    }
+    if (tile < 0) return;  // (the grid holds exactly the plan's items)
+    slot = nsp > 1 ? slot + item : -1;
+    const int nch = tile_chunks(tile, QT, n, start);
+    const int c_begin = nch * item / nsp, c_end = nch * (item + 1) / nsp;
+    const int t0 = tile * QT, ntok = min(QT, n - t0);
+    const int last = min(start + t0 + ntok - 1, c_end * PC - 1);
+
+    if (tid == 0) {
+        mbar_init(&bar_s, 1);
+        mbar_init(&bar_o, 1);
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_u32(&tmem_base)), "r"(TA_TMEM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    // Q tile: row r = token t0 + r / G, head g * G + r % G; 8 rows' loads in flight per batch
+    // (the shared-memory stores in between would otherwise serialise every global load)
+#pragma unroll 1
+    for (int i0 = tid; i0 < 128 * 32; i0 += 8 * TA_THREADS) {
+        float4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int i = i0 + u * TA_THREADS, r = i >> 5;
+            v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (r / G < ntok)
+                v[u] = __ldg(reinterpret_cast<const float4*>(Q + (size_t)(t0 + r / G) * NQ * 128 + (size_t)(g * G + r % G) * 128) +
+                             (i & 31));
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int i = i0 + u * TA_THREADS, r = i >> 5, d0 = (i & 31) * 4;
+            const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int d = d0 + j;
+                ta_split(sm + TA_Q + (d >> 6) * 16384, sm + TA_QLO + (d >> 6) * 16384, ta_sw128(r, d & 63), e[j]);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base, tS = tmem + TA_S_COL, tO = tmem + TA_O_COL;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const uint32_t idesc_s = tc::idesc_bf16_f32(128, 64), idesc_o = tc::idesc_bf16_f32(128, 128);
+    const float* kb = Kc + head_stride_l + (size_t)g * max_seq * 128;
+    const float* vb = Vc + head_stride_l + (size_t)g * max_seq * 128;
+    const int pos_r = start + t0 + tid / G;  // thread tid owns query row tid
+    float m_run = -INFINITY, l_run = 0.f;
+    int chunk = 0;
+    bool ok = true;
+    for (int p0 = c_begin * PC; p0 <= last; p0 += PC, chunk++) {
+        const int np = min(PC, last + 1 - p0);
+        // the previous chunk's P.V must be done before K, V and P are rewritten and O is rescaled
+        if (chunk > 0 && tid == 0) ok = tc::bounded_wait(&bar_o, (chunk - 1) & 1, &abort_flag);
+        if (!__syncthreads_and(ok && !abort_flag)) {
+            ok = false;
+            break;
+        }
+        // K and V rows of the chunk: 8 iterations' loads in flight per batch
+#pragma unroll 1
+        for (int i0 = tid; i0 < PC * 32; i0 += 8 * TA_THREADS) {
+            float4 kv[8], vv[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int i = i0 + u * TA_THREADS, p = i >> 5;
+                kv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                vv[u] = kv[u];
+                if (p < np) {
+                    kv[u] = __ldcg(reinterpret_cast<const float4*>(kb + (size_t)(p0 + p) * 128) + (i & 31));
+                    vv[u] = __ldcg(reinterpret_cast<const float4*>(vb + (size_t)(p0 + p) * 128) + (i & 31));
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int i = i0 + u * TA_THREADS, p = i >> 5, d0 = (i & 31) * 4;
+                const float ke[4] = {kv[u].x, kv[u].y, kv[u].z, kv[u].w}, ve[4] = {vv[u].x, vv[u].y, vv[u].z, vv[u].w};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int d = d0 + j;
+                    ta_split(sm + TA_K + (d >> 6) * 8192, sm + TA_KLO + (d >> 6) * 8192, ta_sw128(p, d & 63), ke[j]);
+                    ta_split(sm + TA_V, sm + TA_VLO, ta_sw128(d, p), ve[j]);
+                }
+            }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < 8; kk++) {
+                const int blk = kk >> 2, w = kk & 3;
+                const uint64_t qh = tc::smem_desc_k128(smem_u32(sm + TA_Q + blk * 16384)) + 2 * w;
+                const uint64_t ql = tc::smem_desc_k128(smem_u32(sm + TA_QLO + blk * 16384)) + 2 * w;
+                const uint64_t kh = tc::smem_desc_k128(smem_u32(sm + TA_K + blk * 8192)) + 2 * w;
+                const uint64_t kl = tc::smem_desc_k128(smem_u32(sm + TA_KLO + blk * 8192)) + 2 * w;
+                tc::mma_bf16(tS, qh, kh, idesc_s, kk > 0);
+                tc::mma_bf16(tS, qh, kl, idesc_s, 1u);
+                tc::mma_bf16(tS, ql, kh, idesc_s, 1u);
+            }
+            tc::mma_commit(&bar_s);
+            ok = tc::bounded_wait(&bar_s, chunk & 1, &abort_flag);
+        }
+        if (!__syncthreads_and(ok && !abort_flag)) {
+            ok = false;
+            break;
+        }
+        tc_fence_after();
+        // softmax over this chunk for row tid
+        uint32_t sr[64];
+        tc::tmem_ld32(tS + lane_base, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
+        tc::tmem_ld32(tS + lane_base + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 64; c++) {
+            const bool live = c < np && p0 + c <= pos_r;
+            const float v = live ? __uint_as_float(sr[c]) * scale : -INFINITY;
+            sr[c] = __float_as_uint(v);
+            mx = fmaxf(mx, v);
+        }
+        const float mn = fmaxf(m_run, mx);
+        const float corr = m_run == -INFINITY ? 0.f : __expf(m_run - mn);
+        float sum = 0.f;
+#pragma unroll
+        for (int c = 0; c < 64; c++) {
+            const float v = __uint_as_float(sr[c]);
+            const float e = v == -INFINITY ? 0.f : __expf(v - mn);
+            sum += e;
+            ta_split(sm + TA_P, sm + TA_PLO, ta_sw128(tid, c), e);
+        }
+        l_run = l_run * corr + sum;
+        m_run = mn;
+        if (chunk > 0) {  // O row *= corr
+#pragma unroll 1
+            for (int cb = 0; cb < 128; cb += 32) {
+                uint32_t o[32];
+                tc::tmem_ld32(tO + lane_base + cb, o);
+#pragma unroll
+                for (int j = 0; j < 32; j++) o[j] = __float_as_uint(__uint_as_float(o[j]) * corr);
+                tmem_st32(tO + lane_base + cb, o);
+            }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) {
+                const uint64_t ph = tc::smem_desc_k128(smem_u32(sm + TA_P)) + 2 * kk;
+                const uint64_t pl = tc::smem_desc_k128(smem_u32(sm + TA_PLO)) + 2 * kk;
+                const uint64_t vh = tc::smem_desc_k128(smem_u32(sm + TA_V)) + 2 * kk;
+                const uint64_t vl = tc::smem_desc_k128(smem_u32(sm + TA_VLO)) + 2 * kk;
+                tc::mma_bf16(tO, ph, vh, idesc_o, (chunk > 0 || kk > 0) ? 1u : 0u);
+                tc::mma_bf16(tO, ph, vl, idesc_o, 1u);
+                tc::mma_bf16(tO, pl, vh, idesc_o, 1u);
+            }
+            tc::mma_commit(&bar_o);
+        }
+    }
+    // the last chunk's P.V, then O -> output
+    if (ok && chunk > 0 && tid == 0) ok = tc::bounded_wait(&bar_o, (chunk - 1) & 1, &abort_flag);
+    ok = __syncthreads_and(ok && !abort_flag);
+    tc_fence_after();
+    if (ok && chunk > 0) {
+        const int tl = tid / G, h = tid % G;
+        if (slot >= 0) {
+            float* dst = part + (((size_t)g * slots + slot) * 128 + tid) * PPITCH;
+#pragma unroll 1
+            for (int cb = 0; cb < 128; cb += 32) {
+                uint32_t o[32];
+                tc::tmem_ld32(tO + lane_base + cb, o);
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<float4*>(dst + cb + j) = make_float4(__uint_as_float(o[j]), __uint_as_float(o[j + 1]),
+                                                                        __uint_as_float(o[j + 2]), __uint_as_float(o[j + 3]));
+            }
+            dst[128] = m_run;
+            dst[129] = l_run;
+        } else {
+            const float inv = 1.0f / l_run;
+            float* dst = att + (size_t)(t0 + tl) * NQ * 128 + (size_t)(g * G + h) * 128;
+#pragma unroll 1
+            for (int cb = 0; cb < 128; cb += 32) {
+                uint32_t o[32];
+                tc::tmem_ld32(tO + lane_base + cb, o);
+                if (tl < ntok)
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4)
+                        *reinterpret_cast<float4*>(dst + cb + j) =
+                            make_float4(__uint_as_float(o[j]) * inv, __uint_as_float(o[j + 1]) * inv,
+                                        __uint_as_float(o[j + 2]) * inv, __uint_as_float(o[j + 3]) * inv);
+            }
+        }
+    }
+    if (!ok && tid == 0) {
+        atomicExch(err, 1);
+        // MMAs issued before the abort must finish before their TMEM is freed (bounded waits)
+        const uint64_t w0 = globaltimer_ns();
+        while (!mbar_try_wait(&bar_s, chunk & 1) && globaltimer_ns() - w0 < (uint64_t)tc::WAIT_LIMIT_NS) {
+        }
+        const uint64_t w1 = globaltimer_ns();
+        while (chunk > 0 && !mbar_try_wait(&bar_o, (chunk - 1) & 1) && globaltimer_ns() - w1 < (uint64_t)tc::WAIT_LIMIT_NS) {
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TA_TMEM_COLS) : "memory");
+    }
+}
+
+template <int G>
+int launch_attention_tc(const float* Q, float* att, const float* Kc, const float* Vc, int n, int start, int NQ, int NKV,
+                        size_t hsl, int max_seq, float scale, float* part, size_t part_cap, int* err, cudaStream_t s) {
+    constexpr int QT = 128 / G;
+    if (cudaFuncSetAttribute(attention_tc<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, TA_SMEM) != cudaSuccess)
+        return QW_ERR_CUDA;
+    const AttPlan pl = att_plan(QT, n, start);
+    if ((size_t)NKV * pl.slots * 128 * PPITCH > part_cap) return QW_ERR_ARG;
+    launch(attention_tc<G>, dim3(pl.items, NKV), dim3(TA_THREADS), TA_SMEM, s, Q, att, Kc, Vc, n, start, NQ, hsl, max_seq,
+           scale, part, pl.slots, err);
+    int split_tiles = 0;
+    for (int t = (n + QT - 1) / QT - 1; t >= 0; t--) split_tiles += tile_splits(t, QT, n, start) > 1;
+    if (split_tiles)
+        launch(attention_merge<G, QT>, dim3(split_tiles, NKV, 128 / 4), dim3(128), 0, s, att, part, n, start, NQ, pl.slots);
+    return QW_OK;
+}
+
+
 // floats of attention partials a pass over n tokens from `start` needs (G = query heads per KV head)
 size_t attention_partial_floats(int n, int start, int NQ, int NKV) {
-    const int G = NQ / NKV, QT = G == 1 ? AttTile<1>::QT : G == 2 ? AttTile<2>::QT : AttTile<3>::QT;
+    const int G = NQ / NKV;
+    const int QT = (G == 1 || G == 2 || G == 4) ? 128 / G : AttTile<3>::QT;  // tensor-core tiles, else CUDA-core
     return (size_t)NKV * att_plan(QT, n, start).slots * QT * G * PPITCH;
 }
 
@@ -904,9 +1206,14 @@ static int forward_pass(const Weights& w, const CacheView& c, const RowView* row
             launch(row_merge, dim3(n, (NQ + 3) / 4), dim3(128), 0, s, sc.attp, rows, NQ, splits, sc.ahi, sc.alo);
         } else {
             const size_t hsl = (size_t)l * NKV * c.max_seq * 128;
-            rc = G == 1 ? launch_attention<1>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, sc.attp, sc.attp_cap, s)
-               : G == 2 ? launch_attention<2>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, sc.attp, sc.attp_cap, s)
-                        : launch_attention<3>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, sc.attp, sc.attp_cap, s);
+            rc = G == 1 ? launch_attention_tc<1>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, sc.attp,
+                                                 sc.attp_cap, err_word, s)
+               : G == 2 ? launch_attention_tc<2>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, sc.attp,
+                                                 sc.attp_cap, err_word, s)
+               : G == 4 ? launch_attention_tc<4>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, sc.attp,
+                                                 sc.attp_cap, err_word, s)
+                        : launch_attention<3>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, sc.attp,
+                                              sc.attp_cap, s);
             if (rc) {
                 err = rc == QW_ERR_ARG ? "prefill attention partial buffer too small"
                                        : "cannot raise the prefill attention kernel's shared-memory limit";
