@@ -613,7 +613,7 @@ int launch_attention(const float* Q, float* att, const float* Kc, const float* V
 // memory in the 128-byte-swizzle K-major layout (V transposed: dims x positions); each product is
 // hi.hi + hi.lo + lo.hi, so scores and outputs keep about 16 bits of every f32 operand. One
 // thread issues the MMAs and commits them to an mbarrier per product; every wait is bounded.
-constexpr int TA_THREADS = 128;
+constexpr int TA_THREADS = 256;  // 8 warps: warps w and w + 4 share TMEM lanes 32 (w % 4) .., split by columns
 constexpr uint32_t TA_TMEM_COLS = 256, TA_S_COL = 0, TA_O_COL = 64;
 constexpr int TA_Q = 0, TA_QLO = 32768;                  // Q: 2 K blocks x [128 rows x 128 B] per half
 constexpr int TA_K = 65536, TA_KLO = TA_K + 16384;        // K chunk: 2 K blocks x [64 rows x 128 B] per half
@@ -629,6 +629,29 @@ __device__ __forceinline__ void ta_split(uint8_t* hi, uint8_t* lo, uint32_t off,
     *reinterpret_cast<__nv_bfloat16*>(hi + off) = h;
     *reinterpret_cast<__nv_bfloat16*>(lo + off) = __float2bfloat16_rn(v - __bfloat162float(h));
 }
+// 4 consecutive columns (8 bytes per half) of a swizzled tile row, c0 a multiple of 4
+__device__ __forceinline__ void ta_split4(uint8_t* hi, uint8_t* lo, uint32_t off, float4 v) {
+    const __nv_bfloat162 h01 = __floats2bfloat162_rn(v.x, v.y), h23 = __floats2bfloat162_rn(v.z, v.w);
+    const float2 f01 = __bfloat1622float2(h01), f23 = __bfloat1622float2(h23);
+    const __nv_bfloat162 l01 = __floats2bfloat162_rn(v.x - f01.x, v.y - f01.y), l23 = __floats2bfloat162_rn(v.z - f23.x, v.w - f23.y);
+    *reinterpret_cast<uint2*>(hi + off) = make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+    *reinterpret_cast<uint2*>(lo + off) = make_uint2(*reinterpret_cast<const uint32_t*>(&l01), *reinterpret_cast<const uint32_t*>(&l23));
+}
+// 8 consecutive columns (one 16-byte swizzle chunk per half) of a swizzled tile row
+__device__ __forceinline__ void ta_split8(uint8_t* hi, uint8_t* lo, uint32_t off, const float* v) {
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const __nv_bfloat162 hh = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+        const float2 f = __bfloat1622float2(hh);
+        const __nv_bfloat162 ll = __floats2bfloat162_rn(v[2 * j] - f.x, v[2 * j + 1] - f.y);
+        h[j] = *reinterpret_cast<const uint32_t*>(&hh);
+        l[j] = *reinterpret_cast<const uint32_t*>(&ll);
+    }
+    *reinterpret_cast<uint4*>(hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(lo + off) = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -654,10 +677,11 @@ attention_tc(const float* Q, float* att, const float* Kc, const float* Vc, int n
     __shared__ uint64_t bar_s, bar_o;
     __shared__ uint32_t tmem_base;
     __shared__ volatile int abort_flag;
+    __shared__ float xmax[2][128], xsum[2][128];  // per row: the two score-column halves' max and sum
     pdl_wait();
     pdl_trigger();
     uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ta_raw) + 1023) & ~uintptr_t(1023));
-    const int g = blockIdx.y, tid = threadIdx.x, warp = tid >> 5;
+    const int g = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // work item -> (tile, split), as attention<G>
     int tile = (n + QT - 1) / QT - 1, item = blockIdx.x, slot = 0, nsp = 1;
     for (; tile >= 0; tile--) {
@@ -700,23 +724,20 @@ attention_tc(const float* Q, float* att, const float* Kc, const float* Vc, int n
 #pragma unroll
         for (int u = 0; u < 8; u++) {
             const int i = i0 + u * TA_THREADS, r = i >> 5, d0 = (i & 31) * 4;
-            const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int d = d0 + j;
-                ta_split(sm + TA_Q + (d >> 6) * 16384, sm + TA_QLO + (d >> 6) * 16384, ta_sw128(r, d & 63), e[j]);
-            }
+            ta_split4(sm + TA_Q + (d0 >> 6) * 16384, sm + TA_QLO + (d0 >> 6) * 16384, ta_sw128(r, d0 & 63), v[u]);
         }
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_base, tS = tmem + TA_S_COL, tO = tmem + TA_O_COL;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    // warp w reads TMEM lanes 32 (w % 4) .. (its query rows) and column half w / 4 of S and O
+    const int row = 32 * (warp & 3) + lane, half = warp >> 2;
+    const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
     const uint32_t idesc_s = tc::idesc_bf16_f32(128, 64), idesc_o = tc::idesc_bf16_f32(128, 128);
     const float* kb = Kc + head_stride_l + (size_t)g * max_seq * 128;
     const float* vb = Vc + head_stride_l + (size_t)g * max_seq * 128;
-    const int pos_r = start + t0 + tid / G;  // thread tid owns query row tid
+    const int pos_r = start + t0 + row / G;
     float m_run = -INFINITY, l_run = 0.f;
     int chunk = 0;
     bool ok = true;
@@ -728,30 +749,29 @@ attention_tc(const float* Q, float* att, const float* Kc, const float* Vc, int n
             ok = false;
             break;
         }
-        // K and V rows of the chunk: 8 iterations' loads in flight per batch
-#pragma unroll 1
-        for (int i0 = tid; i0 < PC * 32; i0 += 8 * TA_THREADS) {
+        {
+            // K and V rows of the chunk: warp w takes positions 8 w + (lane & 7), lane group lane >> 3
+            // dims 4 (lane >> 3) + 16 u, u < 8 (8 rows x 64 contiguous bytes per load). K goes out as
+            // 8-byte row pieces, V^T as single elements (dims x positions).
+            const int p = 8 * warp + (lane & 7), dg = lane >> 3;
             float4 kv[8], vv[8];
 #pragma unroll
             for (int u = 0; u < 8; u++) {
-                const int i = i0 + u * TA_THREADS, p = i >> 5;
                 kv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
                 vv[u] = kv[u];
                 if (p < np) {
-                    kv[u] = __ldcg(reinterpret_cast<const float4*>(kb + (size_t)(p0 + p) * 128) + (i & 31));
-                    vv[u] = __ldcg(reinterpret_cast<const float4*>(vb + (size_t)(p0 + p) * 128) + (i & 31));
+                    kv[u] = __ldcg(reinterpret_cast<const float4*>(kb + (size_t)(p0 + p) * 128) + dg + 4 * u);
+                    vv[u] = __ldcg(reinterpret_cast<const float4*>(vb + (size_t)(p0 + p) * 128) + dg + 4 * u);
                 }
             }
 #pragma unroll
             for (int u = 0; u < 8; u++) {
-                const int i = i0 + u * TA_THREADS, p = i >> 5, d0 = (i & 31) * 4;
-                const float ke[4] = {kv[u].x, kv[u].y, kv[u].z, kv[u].w}, ve[4] = {vv[u].x, vv[u].y, vv[u].z, vv[u].w};
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const int d = d0 + j;
-                    ta_split(sm + TA_K + (d >> 6) * 8192, sm + TA_KLO + (d >> 6) * 8192, ta_sw128(p, d & 63), ke[j]);
-                    ta_split(sm + TA_V, sm + TA_VLO, ta_sw128(d, p), ve[j]);
-                }
+                const int d0 = 4 * (dg + 4 * u);
+                ta_split4(sm + TA_K + (d0 >> 6) * 8192, sm + TA_KLO + (d0 >> 6) * 8192, ta_sw128(p, d0 & 63), kv[u]);
+                ta_split(sm + TA_V, sm + TA_VLO, ta_sw128(d0, p), vv[u].x);
+                ta_split(sm + TA_V, sm + TA_VLO, ta_sw128(d0 + 1, p), vv[u].y);
+                ta_split(sm + TA_V, sm + TA_VLO, ta_sw128(d0 + 2, p), vv[u].z);
+                ta_split(sm + TA_V, sm + TA_VLO, ta_sw128(d0 + 3, p), vv[u].w);
             }
         }
         fence_proxy_async_smem();
@@ -778,33 +798,38 @@ attention_tc(const float* Q, float* att, const float* Kc, const float* Vc, int n
             break;
         }
         tc_fence_after();
-        // softmax over this chunk for row tid
-        uint32_t sr[64];
-        tc::tmem_ld32(tS + lane_base, *reinterpret_cast<uint32_t(*)[32]>(&sr[0]));
-        tc::tmem_ld32(tS + lane_base + 32, *reinterpret_cast<uint32_t(*)[32]>(&sr[32]));
+        // softmax for row `row` over this chunk; this warp holds score columns 32 half .. + 31
+        uint32_t sr[32];
+        tc::tmem_ld32(tS + lane_base + 32 * half, sr);
         float mx = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 64; c++) {
+        for (int j = 0; j < 32; j++) {
+            const int c = 32 * half + j;
             const bool live = c < np && p0 + c <= pos_r;
-            const float v = live ? __uint_as_float(sr[c]) * scale : -INFINITY;
-            sr[c] = __float_as_uint(v);
+            const float v = live ? __uint_as_float(sr[j]) * scale : -INFINITY;
+            sr[j] = __float_as_uint(v);
             mx = fmaxf(mx, v);
         }
-        const float mn = fmaxf(m_run, mx);
+        xmax[half][row] = mx;
+        __syncthreads();
+        const float mn = fmaxf(m_run, fmaxf(xmax[0][row], xmax[1][row]));
         const float corr = m_run == -INFINITY ? 0.f : __expf(m_run - mn);
         float sum = 0.f;
 #pragma unroll
-        for (int c = 0; c < 64; c++) {
-            const float v = __uint_as_float(sr[c]);
-            const float e = v == -INFINITY ? 0.f : __expf(v - mn);
-            sum += e;
-            ta_split(sm + TA_P, sm + TA_PLO, ta_sw128(tid, c), e);
+        for (int c8 = 0; c8 < 32; c8 += 8) {  // one 16-byte swizzle chunk of P per half
+            float e[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const float v = __uint_as_float(sr[c8 + j]);
+                e[j] = v == -INFINITY ? 0.f : __expf(v - mn);
+                sum += e[j];
+            }
+            ta_split8(sm + TA_P, sm + TA_PLO, ta_sw128(row, 32 * half + c8), e);
         }
-        l_run = l_run * corr + sum;
-        m_run = mn;
-        if (chunk > 0) {  // O row *= corr
+        xsum[half][row] = sum;
+        if (chunk > 0) {  // this warp's half of the O row *= corr
 #pragma unroll 1
-            for (int cb = 0; cb < 128; cb += 32) {
+            for (int cb = 64 * half; cb < 64 * half + 64; cb += 32) {
                 uint32_t o[32];
                 tc::tmem_ld32(tO + lane_base + cb, o);
 #pragma unroll
@@ -815,6 +840,8 @@ attention_tc(const float* Q, float* att, const float* Kc, const float* Vc, int n
         fence_proxy_async_smem();
         tc_fence_before();
         __syncthreads();
+        l_run = l_run * corr + (xsum[0][row] + xsum[1][row]);
+        m_run = mn;
         if (tid == 0) {
             tc_fence_after();
 #pragma unroll
@@ -830,16 +857,16 @@ attention_tc(const float* Q, float* att, const float* Kc, const float* Vc, int n
             tc::mma_commit(&bar_o);
         }
     }
-    // the last chunk's P.V, then O -> output
+    // the last chunk's P.V, then this warp's half of the O row -> output
     if (ok && chunk > 0 && tid == 0) ok = tc::bounded_wait(&bar_o, (chunk - 1) & 1, &abort_flag);
     ok = __syncthreads_and(ok && !abort_flag);
     tc_fence_after();
     if (ok && chunk > 0) {
-        const int tl = tid / G, h = tid % G;
+        const int tl = row / G, h = row % G;
         if (slot >= 0) {
-            float* dst = part + (((size_t)g * slots + slot) * 128 + tid) * PPITCH;
+            float* dst = part + (((size_t)g * slots + slot) * 128 + row) * PPITCH;
 #pragma unroll 1
-            for (int cb = 0; cb < 128; cb += 32) {
+            for (int cb = 64 * half; cb < 64 * half + 64; cb += 32) {
                 uint32_t o[32];
                 tc::tmem_ld32(tO + lane_base + cb, o);
 #pragma unroll
@@ -847,13 +874,15 @@ attention_tc(const float* Q, float* att, const float* Kc, const float* Vc, int n
                     *reinterpret_cast<float4*>(dst + cb + j) = make_float4(__uint_as_float(o[j]), __uint_as_float(o[j + 1]),
                                                                         __uint_as_float(o[j + 2]), __uint_as_float(o[j + 3]));
             }
-            dst[128] = m_run;
-            dst[129] = l_run;
+            if (half == 0) {
+                dst[128] = m_run;
+                dst[129] = l_run;
+            }
         } else {
             const float inv = 1.0f / l_run;
             float* dst = att + (size_t)(t0 + tl) * NQ * 128 + (size_t)(g * G + h) * 128;
 #pragma unroll 1
-            for (int cb = 0; cb < 128; cb += 32) {
+            for (int cb = 64 * half; cb < 64 * half + 64; cb += 32) {
                 uint32_t o[32];
                 tc::tmem_ld32(tO + lane_base + cb, o);
                 if (tl < ntok)
