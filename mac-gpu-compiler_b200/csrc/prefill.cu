@@ -325,7 +325,7 @@ __global__ void qkv_post(const float* Y, int nparts, int n, int start, int NQ, i
 // writes its unnormalised output and running max / sum to a partial slot, and attention_merge
 // combines the splits of a tile in split order. Work items are numbered longest tiles first.
 constexpr int PC = 64;                 // positions per chunk
-constexpr int CMAX = 4;                // most chunks one CTA processes
+constexpr int CMAX = 3;                // most chunks one CTA processes
 constexpr int AT_THREADS = 256;
 constexpr int KPAD = 132;              // K row pitch in floats (bank spread for the score loads)
 constexpr int PPITCH = 132;            // partial row: 128 output dims, running max, running sum, pad
