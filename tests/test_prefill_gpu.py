@@ -24,7 +24,7 @@ def _need_gpu():
         pytest.skip("no CUDA device")
 
 
-# n = 300 and 600 reach query tiles whose positions span more than one attention split (256
+# n = 300 and 600 reach query tiles whose positions span more than one attention split (192
 # positions), so those cases also check the split merge
 @pytest.mark.parametrize("geometry,n", [("tiny", 40), ("mid", 130), ("qwen3-0.6b", 64), ("mid", 300), ("tiny", 600)])
 def test_prefill_matches_token_by_token_oracle(geometry, n):
