@@ -55,7 +55,7 @@ constexpr int HD = 128;                       // head_dim (the reference's atten
 constexpr int ATT_P = SLOT_BYTES / (2 * HD * 4);  // cached positions per attention ring slot (24)
 constexpr int MAX_G = 3;                      // query heads per KV head
 constexpr int MAX_S = 18;                     // attention chunks per KV head
-constexpr int MIN_CHUNK = 32;                 // fewest positions per attention chunk
+constexpr int MIN_CHUNK = 32;                 // default fewest positions per attention chunk (DecodeParams::min_chunk)
 constexpr uint32_t LM_PREFETCH_BYTES = 256u * 1024;  // lm_head bytes per CTA warmed into L2 ahead of use
 constexpr int APART_STRIDE = HD + 4;          // words per attention partial: acc[128], m, l, pad
 constexpr int ATT_WST = HD + 4;               // floats per (warp, head) softmax state staged in part: acc[128], m, l, pad
@@ -122,6 +122,7 @@ struct DecodeParams {
     int xloc_cap;                // floats in the shared residual-rows buffer
     long long timeout_ns;
     int poll_ns;                 // back-off between unsuccessful polling rounds of tagged words (0 = none)
+    int min_chunk;               // fewest positions per attention chunk (larger: fewer chunk CTAs to merge)
 };
 
 // static row partition of a GEMV phase for one CTA
@@ -198,7 +199,7 @@ __device__ inline AttnItem attn_item(const DecodeParams& p, int cta, int pos) {
     AttnItem a;
     const int n_t = pos + 1;
     int chunk = (n_t + p.S - 1) / p.S;
-    if (chunk < MIN_CHUNK) chunk = MIN_CHUNK;
+    if (chunk < p.min_chunk) chunk = p.min_chunk;
     a.S_eff = (n_t + chunk - 1) / chunk;
     a.g = cta / p.S;
     a.s = cta % p.S;

@@ -174,6 +174,7 @@ struct qw_model {
     size_t dyn_smem = 0;
     long long timeout_ns = 0;
     int poll_ns = 0;
+    int min_chunk = MIN_CHUNK;
 };
 
 // A cache never dereferences its model after qw_cache_new: it keeps what it needs (device,
@@ -263,6 +264,7 @@ int launch_decode(qw_model* m, qw_cache* c, const uint32_t* tok_in, uint32_t* to
     p.xloc_cap = m->xloc_cap;
     p.timeout_ns = m->timeout_ns;
     p.poll_ns = m->poll_ns;
+    p.min_chunk = m->min_chunk;
     void* args[] = {&p};
     cudaError_t e = cudaLaunchCooperativeKernel((const void*)decode_kernel, dim3(m->nctas), dim3(NTHREADS), args,
                                                 m->dyn_smem, s);
@@ -327,6 +329,7 @@ int qw_load(const char* path, int device, qw_model** out) {
     m->wbytes = f.weight_bytes_per_token();
     m->timeout_ns = timeout_ns_from_env();
     if (const char* e = std::getenv("QW_POLL_NS")) m->poll_ns = std::max(0, std::min(10000, std::atoi(e)));
+    if (const char* e = std::getenv("QW_MIN_CHUNK")) m->min_chunk = std::max(1, std::min(1 << 20, std::atoi(e)));
     int nctas = prop.multiProcessorCount;
     if (const char* e = std::getenv("QW_CTAS")) nctas = std::max(1, std::min(nctas, std::atoi(e)));
     // Buffers are reused across phases on the premise that every CTA contributes to every GEMV
