@@ -191,7 +191,7 @@ def run_batch(args, world: int, rank: int, local: int, pg) -> None:
     import torch
     import cuda_inference as ci
     c = CONFIGS["box8"]
-    n_prompt, n_dec, B = c["prompt"], c["decode"], c["batch"]
+    n_prompt, n_dec, B = c["prompt"], c["decode"], args.rows or c["batch"]
     path = randmodel.make_model("qwen3-0.6b", 0)
     model = ci.CudaModel.load_model(path, device=local)
     cfg = model.config
@@ -268,7 +268,8 @@ def run_batch(args, world: int, rank: int, local: int, pg) -> None:
             "ms_per_batch_token_step": group_s / n_dec * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "bf16", "accumulate": "f32 (split-bf16 activations)", "data": "synthetic",
-            "config": {"workload": c["label"], "model": "Qwen3-0.6B geometry, random-init bf16 (seed 0)",
+            "config": {"workload": c["label"] if B == c["batch"] else c["label"].replace("8 at a time", f"{B} at a time"),
+                       "model": "Qwen3-0.6B geometry, random-init bf16 (seed 0)",
                        "global_batch": c["sequences"], "per_gpu_batch": B, "seq_len": n_prompt + n_dec,
                        "parallelism": f"replicas x{world}, {len(seqs)} sequences on rank 0 in groups of {B}, no collective",
                        "l2": "inputs larger than L2: 1.19 GB of weights streamed per batch step",
@@ -489,6 +490,7 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="ai130", choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--rows", type=int, default=0, help="box8: sequences decoded together per GPU (default 8, at most 16)")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args, args.config)

@@ -155,6 +155,7 @@ struct qw_model {
     // captured graph of one step with the configuration it was captured for
     qw::pf::RowView* d_rows = nullptr;   // [ROWS_MAX]
     uint32_t* d_btok = nullptr;          // [ROWS_MAX]
+    qw::pf::ArgmaxScratch* d_am = nullptr;
     uint32_t* d_bout = nullptr;
     size_t bout_cap = 0;                 // entries of d_bout
     // captured row-mode step graphs, by what they were captured for (kind 0: greedy batch step,
@@ -465,6 +466,7 @@ void qw_free(qw_model* m) {
     for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);
     cudaFree(m->d_rows);
     cudaFree(m->d_btok);
+    cudaFree(m->d_am);
     cudaFree(m->d_bout);
     cudaFree(m->d_pf_ids);
     cudaFree(m->d_pf_logits);
@@ -704,6 +706,10 @@ int batch_rows(qw_model* m, qw_cache* const* caches, size_t B, const size_t* pos
 int ensure_batch(qw_model* m, size_t B, int splits, size_t out_entries) {
     if (!m->d_rows) QW_CUDA(cudaMalloc(&m->d_rows, qw::pf::ROWS_MAX * sizeof(qw::pf::RowView)));
     if (!m->d_btok) QW_CUDA(cudaMalloc(&m->d_btok, qw::pf::ROWS_MAX * 4));
+    if (!m->d_am) {
+        QW_CUDA(cudaMalloc(&m->d_am, sizeof(qw::pf::ArgmaxScratch)));
+        QW_CUDA(cudaMemset(m->d_am, 0, sizeof(qw::pf::ArgmaxScratch)));
+    }
     if (out_entries > m->bout_cap) {
         uint32_t* d = nullptr;
         const size_t cap = std::max(out_entries, 2 * m->bout_cap);
@@ -742,8 +748,8 @@ int row_graph(qw_model* m, int kind, int B, int splits, uint32_t* out, int* ew, 
     std::string err;
     int rc = qw::pf::run_rows(weights_of(m), m->d_rows, B, splits, m->d_btok, m->d_pf_logits, m->pf, ew, s, err);
     if (!rc)
-        rc = kind == 0 ? qw::pf::argmax_rows(m->d_pf_logits, (int)m->cfg.vocab, B, m->d_rows, m->d_btok, out, s, err)
-                       : qw::pf::argmax_each(m->d_pf_logits, (int)m->cfg.vocab, B, out, s, err);
+        rc = kind == 0 ? qw::pf::argmax_rows(m->d_pf_logits, (int)m->cfg.vocab, B, m->d_rows, m->d_btok, out, m->d_am, s, err)
+                       : qw::pf::argmax_each(m->d_pf_logits, (int)m->cfg.vocab, B, out, m->d_am, s, err);
     cudaGraph_t graph = nullptr;
     const cudaError_t ce = cudaStreamEndCapture(s, &graph);
     if (rc) {

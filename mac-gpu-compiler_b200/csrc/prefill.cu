@@ -1086,21 +1086,27 @@ __device__ __forceinline__ bool am_wins(float av, unsigned ai, float bv, unsigne
     return av > bv || (av == bv && ai < bi);
 }
 
-constexpr int AR_THREADS = 1024;
+constexpr int AR_THREADS = 256;
 
-// One block per row: next token = argmax of the row's logits, recorded at d_out[(pos - start) * B
-// + b]; the row then advances to pos + 1 (the next step's input position).
-__global__ void __launch_bounds__(AR_THREADS) argmax_rows_kernel(const float* logits, int V, int B, RowView* rows,
-                                                                 uint32_t* tok, uint32_t* out) {
+// Argmax of `rows` rows of V logits, AR_PARTS blocks per row (grid (rows, AR_PARTS)): block p
+// takes elements p, p + AR_PARTS*..., in its share and writes its best (value, index); the last
+// block of a row to finish (a ticket per row, reset by that block) picks the best of the parts,
+// applies the CPU rule's NaN-at-index-0 case and stores the token. Row mode (rv != null): the
+// token feeds the row's next step (tok[b]), is recorded at out[(pos - start) * rows + b], and the
+// row advances to pos + 1. Otherwise out[b] = token.
+__global__ void __launch_bounds__(AR_THREADS) argmax_rows_kernel(const float* logits, int V, int nrows, RowView* rv,
+                                                                 uint32_t* tok, uint32_t* out, ArgmaxScratch* sc) {
     pdl_wait();
     pdl_trigger();
     __shared__ float sv[AR_THREADS / 32];
     __shared__ unsigned si[AR_THREADS / 32];
-    const int b = blockIdx.x;
+    __shared__ int is_last;
+    const int b = blockIdx.x, part = blockIdx.y;
     const float* x = logits + (size_t)b * V;
+    const int per = (V + AR_PARTS - 1) / AR_PARTS, i0 = part * per, i1 = min(V, i0 + per);
     float bv = -INFINITY;
     unsigned bi = AM_NONE;
-    for (int i = threadIdx.x; i < V; i += AR_THREADS) {
+    for (int i = i0 + threadIdx.x; i < i1; i += AR_THREADS) {
         const float v = x[i];
         if (!isnan(v) && am_wins(v, (unsigned)i, bv, bi)) {
             bv = v;
@@ -1126,56 +1132,40 @@ __global__ void __launch_bounds__(AR_THREADS) argmax_rows_kernel(const float* lo
                 bv = sv[w];
                 bi = si[w];
             }
-        // a NaN at index 0 sticks, and with nothing comparable the CPU argmax stays at 0
-        const unsigned t = (isnan(x[0]) || bi == AM_NONE) ? 0u : bi;
+        sc->val[b][part] = bv;
+        sc->idx[b][part] = bi;
+        __threadfence();
+        is_last = atomicAdd(&sc->ticket[b], 1u) == AR_PARTS - 1;
+    }
+    __syncthreads();
+    if (!is_last || threadIdx.x != 0) return;
+    __threadfence();
+    bv = -INFINITY;
+    bi = AM_NONE;
+    for (int q = 0; q < AR_PARTS; q++) {
+        const float v = __ldcg(&sc->val[b][q]);
+        const unsigned i = __ldcg(&sc->idx[b][q]);
+        if (am_wins(v, i, bv, bi)) {
+            bv = v;
+            bi = i;
+        }
+    }
+    sc->ticket[b] = 0u;
+    // a NaN at index 0 sticks, and with nothing comparable the CPU argmax stays at 0
+    const unsigned t = (isnan(x[0]) || bi == AM_NONE) ? 0u : bi;
+    if (rv) {
         tok[b] = t;
-        RowView& rv = rows[b];
-        if (out) out[(size_t)(rv.pos - rv.start) * B + b] = t;
-        rv.pos += 1;
+        RowView& r = rv[b];
+        if (out) out[(size_t)(r.pos - r.start) * nrows + b] = t;
+        r.pos += 1;
+    } else {
+        out[b] = t;
     }
 }
 
-// d_out[t] = argmax of row t of d_logits ([n][V]) with the reference CPU rule; one block per row
-__global__ void __launch_bounds__(AR_THREADS) argmax_each_kernel(const float* logits, int V, uint32_t* out) {
-    pdl_wait();
-    pdl_trigger();
-    __shared__ float sv[AR_THREADS / 32];
-    __shared__ unsigned si[AR_THREADS / 32];
-    const float* x = logits + (size_t)blockIdx.x * V;
-    float bv = -INFINITY;
-    unsigned bi = AM_NONE;
-    for (int i = threadIdx.x; i < V; i += AR_THREADS) {
-        const float v = x[i];
-        if (!isnan(v) && am_wins(v, (unsigned)i, bv, bi)) {
-            bv = v;
-            bi = (unsigned)i;
-        }
-    }
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
-        const unsigned oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
-        if (am_wins(ov, oi, bv, bi)) {
-            bv = ov;
-            bi = oi;
-        }
-    }
-    if ((threadIdx.x & 31) == 0) {
-        sv[threadIdx.x >> 5] = bv;
-        si[threadIdx.x >> 5] = bi;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int w = 1; w < AR_THREADS / 32; w++)
-            if (am_wins(sv[w], si[w], bv, bi)) {
-                bv = sv[w];
-                bi = si[w];
-            }
-        out[blockIdx.x] = (isnan(x[0]) || bi == AM_NONE) ? 0u : bi;
-    }
-}
-
-int argmax_each(const float* d_logits, int V, int n, uint32_t* d_out, cudaStream_t s, std::string& err) {
-    launch(argmax_each_kernel, dim3(n), dim3(AR_THREADS), 0, s, d_logits, V, d_out);
+int argmax_each(const float* d_logits, int V, int n, uint32_t* d_out, ArgmaxScratch* sc, cudaStream_t s, std::string& err) {
+    launch(argmax_rows_kernel, dim3(n, AR_PARTS), dim3(AR_THREADS), 0, s, d_logits, V, n, (RowView*)nullptr,
+           (uint32_t*)nullptr, d_out, sc);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         err = std::string("argmax launch failed: ") + cudaGetErrorString(e);
@@ -1186,9 +1176,9 @@ int argmax_each(const float* d_logits, int V, int n, uint32_t* d_out, cudaStream
 
 size_t row_partial_floats(int B, int NQ, int splits) { return (size_t)B * NQ * splits * PPITCH; }
 
-int argmax_rows(const float* d_logits, int V, int B, RowView* d_rows, uint32_t* d_tok, uint32_t* d_out, cudaStream_t s,
-                std::string& err) {
-    launch(argmax_rows_kernel, dim3(B), dim3(AR_THREADS), 0, s, d_logits, V, B, d_rows, d_tok, d_out);
+int argmax_rows(const float* d_logits, int V, int B, RowView* d_rows, uint32_t* d_tok, uint32_t* d_out, ArgmaxScratch* sc,
+                cudaStream_t s, std::string& err) {
+    launch(argmax_rows_kernel, dim3(B, AR_PARTS), dim3(AR_THREADS), 0, s, d_logits, V, B, d_rows, d_tok, d_out, sc);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         err = std::string("argmax launch failed: ") + cudaGetErrorString(e);

@@ -89,13 +89,22 @@ size_t row_partial_floats(int B, int NQ, int splits);
 int run_rows(const Weights& w, const RowView* d_rows, int B, int splits, const uint32_t* d_tok, float* d_logits,
              Scratch& sc, int* err_word, cudaStream_t s, std::string& err);
 
+// device scratch of the row argmax: per row, the best (value, index) of each of its AR_PARTS
+// blocks and an arrival ticket (zero between launches)
+constexpr int AR_PARTS = 16;
+struct ArgmaxScratch {
+    float val[ROWS_MAX][AR_PARTS];
+    unsigned idx[ROWS_MAX][AR_PARTS];
+    unsigned ticket[ROWS_MAX];
+};
+
 // Greedy step end for B rows: d_tok[b] = argmax(d_logits[b]) (the reference CPU rule),
 // d_out[(pos - start) * B + b] = the same token, then pos += 1. Stream-ordered; capturable.
-int argmax_rows(const float* d_logits, int V, int B, RowView* d_rows, uint32_t* d_tok, uint32_t* d_out, cudaStream_t s,
-                std::string& err);
+int argmax_rows(const float* d_logits, int V, int B, RowView* d_rows, uint32_t* d_tok, uint32_t* d_out, ArgmaxScratch* sc,
+                cudaStream_t s, std::string& err);
 
-// d_out[t] = argmax(d_logits[t]) for t < n (the reference CPU rule). Stream-ordered.
-int argmax_each(const float* d_logits, int V, int n, uint32_t* d_out, cudaStream_t s, std::string& err);
+// d_out[t] = argmax(d_logits[t]) for t < n <= ROWS_MAX (the reference CPU rule). Stream-ordered.
+int argmax_each(const float* d_logits, int V, int n, uint32_t* d_out, ArgmaxScratch* sc, cudaStream_t s, std::string& err);
 
 }  // namespace pf
 }  // namespace qw
