@@ -463,6 +463,7 @@ void qw_free(qw_model* m) {
     cudaFree(m->pf.ahi);
     cudaFree(m->pf.alo);
     cudaFree(m->pf.attp);
+    cudaFree(m->pf.att_tickets);
     for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);
     cudaFree(m->d_rows);
     cudaFree(m->d_btok);
@@ -598,6 +599,7 @@ int ensure_prefill(qw_model* m, size_t n, size_t start, bool logits, size_t row_
         sc.ycap = m->pf.ycap;
         sc.attp = m->pf.attp;
         sc.attp_cap = m->pf.attp_cap;
+        sc.att_tickets = m->pf.att_tickets;
         m->pf = sc;
         m->d_pf_ids = ids;
     }
@@ -709,6 +711,11 @@ int ensure_batch(qw_model* m, size_t B, int splits, size_t out_entries) {
     if (!m->d_am) {
         QW_CUDA(cudaMalloc(&m->d_am, sizeof(qw::pf::ArgmaxScratch)));
         QW_CUDA(cudaMemset(m->d_am, 0, sizeof(qw::pf::ArgmaxScratch)));
+    }
+    if (!m->pf.att_tickets) {
+        const size_t nb = (size_t)qw::pf::ROWS_MAX * m->cfg.kv_heads * 4;
+        QW_CUDA(cudaMalloc(&m->pf.att_tickets, nb));
+        QW_CUDA(cudaMemset(m->pf.att_tickets, 0, nb));
     }
     if (out_entries > m->bout_cap) {
         uint32_t* d = nullptr;

@@ -169,6 +169,15 @@ __device__ __forceinline__ void split_store(float v, uint16_t* hi, uint16_t* lo,
     lo[i] = __bfloat16_as_ushort(__float2bfloat16_rn(v - __bfloat162float(h)));
 }
 
+// four consecutive values split into bf16 hi/lo at hi[i..i+3], lo[i..i+3] (i a multiple of 4)
+__device__ __forceinline__ void store_split4(uint16_t* hi, uint16_t* lo, size_t i, float4 v) {
+    const __nv_bfloat162 h01 = __floats2bfloat162_rn(v.x, v.y), h23 = __floats2bfloat162_rn(v.z, v.w);
+    const float2 f01 = __bfloat1622float2(h01), f23 = __bfloat1622float2(h23);
+    const __nv_bfloat162 l01 = __floats2bfloat162_rn(v.x - f01.x, v.y - f01.y), l23 = __floats2bfloat162_rn(v.z - f23.x, v.w - f23.y);
+    *reinterpret_cast<uint2*>(hi + i) = make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+    *reinterpret_cast<uint2*>(lo + i) = make_uint2(*reinterpret_cast<const uint32_t*>(&l01), *reinterpret_cast<const uint32_t*>(&l23));
+}
+
 // X[t] = f32(embed[ids[t]]) (cpu_inference.rs:109-111)
 __global__ void embed_rows(const uint32_t* ids, int H, const uint16_t* embed, float* X) {
     pdl_wait();
@@ -202,16 +211,12 @@ __global__ void __launch_bounds__(ROW_THREADS) norm_split(float* X, int H, const
     for (int i = threadIdx.x; i < H; i += ROW_THREADS) {
         float v = x[i];
         const float* p = parts + (size_t)t * H + i;
-        int z = 0;
-        for (; z + 4 <= nparts; z += 4) {  // four slice loads in flight, added in slice order
-            const float a = p[z * part_stride], b = p[(z + 1) * part_stride], c = p[(z + 2) * part_stride],
-                        d = p[(z + 3) * part_stride];
-            v += a;
-            v += b;
-            v += c;
-            v += d;
-        }
-        for (; z < nparts; z++) v += p[z * part_stride];
+        float pv[KSPLIT_MAX];  // every slice's load in flight at once, then added in slice order
+#pragma unroll
+        for (int z = 0; z < KSPLIT_MAX; z++) pv[z] = z < nparts ? p[z * part_stride] : 0.f;
+#pragma unroll
+        for (int z = 0; z < KSPLIT_MAX; z++)
+            if (z < nparts) v += pv[z];
         if (nparts) x[i] = v;
         ss = fmaf(v, v, ss);
     }
@@ -941,8 +946,8 @@ int grid_for(size_t total) { return (int)std::min<size_t>((total + 255) / 256, 1
 
 // ---------------------------------------------------------------------------------------------
 // Row mode (a decode batch): row b is one sequence's single token at its own position in its own
-// cache. Attention is per (row, KV head, split of ROW_SPLIT positions) — flash-decoding — and a
-// merge per (row, q head) combines the splits and writes the o_proj input halves directly.
+// cache. Attention is per (row, KV head, split of ROW_SPLIT positions) — flash-decoding — and the
+// last split CTA of each (row, KV head) combines the splits into the o_proj input halves.
 
 constexpr int RA_WARPS = 8;            // warp w takes positions p0 + w + 8 j, j < ROW_SPLIT / 8
 constexpr int RA_THREADS = RA_WARPS * 32;
@@ -951,11 +956,14 @@ constexpr int RA_PER_WARP = ROW_SPLIT / RA_WARPS;
 // One (row b, KV head g, split z): the G query heads of g against positions
 // [z * ROW_SPLIT, min((z + 1) * ROW_SPLIT, pos + 1)) of the row's cache; writes (unnormalised
 // output, running max, running sum) per head to part[((b * NQ + head) * splits + z) * PPITCH].
-// Same math as cpu_inference.rs:143-161 (scores scaled by 1/sqrt(128), softmax, sum of p . v),
-// with the softmax done online.
+// The last of the row's live splits to finish (a ticket per (row, KV head), reset by that CTA)
+// combines them in split order and writes the o_proj GEMM's input halves for the G heads. Same
+// math as cpu_inference.rs:143-161 (scores scaled by 1/sqrt(128), softmax, sum of p . v), with the
+// softmax done online.
 template <int G>
 __global__ void __launch_bounds__(RA_THREADS) row_attention(const float* Q, const RowView* rows, int NQ, int NKV, int layer,
-                                                            float scale, float* part, int splits) {
+                                                            float scale, float* part, int splits, unsigned* tickets,
+                                                            uint16_t* ahi, uint16_t* alo) {
     pdl_wait();
     pdl_trigger();
     __shared__ float sm_o[RA_WARPS][G][128];
@@ -1041,40 +1049,36 @@ __global__ void __launch_bounds__(RA_THREADS) row_attention(const float* Q, cons
             dst[129] = L;
         }
     }
-}
-
-// Per (row b, q head): combine the row's live splits in split order and write the normalised
-// attention output as the o_proj GEMM's bf16 hi/lo halves at [b][head * 128 + d]. One warp per
-// head, 4 heads per block.
-__global__ void __launch_bounds__(128) row_merge(const float* part, const RowView* rows, int NQ, int splits, uint16_t* hi,
-                                                 uint16_t* lo) {
-    pdl_wait();
-    pdl_trigger();
-    const int b = blockIdx.x, head = blockIdx.y * 4 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (head >= NQ) return;
-    const int live = rows[b].pos / ROW_SPLIT + 1;
-    const float* base = part + ((size_t)b * NQ + head) * splits * PPITCH;
-    float M = -INFINITY;
-    for (int z = 0; z < live; z++) M = fmaxf(M, base[(size_t)z * PPITCH + 128]);
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    float L = 0.f;
-    for (int z = 0; z < live; z++) {
-        const float* pz = base + (size_t)z * PPITCH;
-        const float mz = pz[128];
-        const float f = mz == -INFINITY ? 0.f : __expf(mz - M);
-        const float4 v = reinterpret_cast<const float4*>(pz)[lane];
-        acc.x = fmaf(v.x, f, acc.x);
-        acc.y = fmaf(v.y, f, acc.y);
-        acc.z = fmaf(v.z, f, acc.z);
-        acc.w = fmaf(v.w, f, acc.w);
-        L = fmaf(pz[129], f, L);
+    __shared__ int is_last;
+    const int live = rv.pos / ROW_SPLIT + 1;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) is_last = atomicAdd(&tickets[b * NKV + g], 1u) == (unsigned)(live - 1);
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    for (int h = warp; h < G; h += RA_WARPS) {
+        const float* base = part + ((size_t)b * NQ + g * G + h) * splits * PPITCH;
+        float M = -INFINITY;
+        for (int j = 0; j < live; j++) M = fmaxf(M, __ldcg(base + (size_t)j * PPITCH + 128));
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        float L = 0.f;
+        for (int j = 0; j < live; j++) {
+            const float* pj = base + (size_t)j * PPITCH;
+            const float mj = __ldcg(pj + 128);
+            const float f = mj == -INFINITY ? 0.f : __expf(mj - M);
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(pj) + lane);
+            acc.x = fmaf(v.x, f, acc.x);
+            acc.y = fmaf(v.y, f, acc.y);
+            acc.z = fmaf(v.z, f, acc.z);
+            acc.w = fmaf(v.w, f, acc.w);
+            L = fmaf(__ldcg(pj + 129), f, L);
+        }
+        const float inv = 1.0f / L;
+        store_split4(ahi, alo, (size_t)b * NQ * 128 + (size_t)(g * G + h) * 128 + 4 * lane,
+                     make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv));
     }
-    const float inv = 1.0f / L;
-    const size_t i0 = (size_t)b * NQ * 128 + (size_t)head * 128 + 4 * lane;
-    split_store(acc.x * inv, hi, lo, i0);
-    split_store(acc.y * inv, hi, lo, i0 + 1);
-    split_store(acc.z * inv, hi, lo, i0 + 2);
-    split_store(acc.w * inv, hi, lo, i0 + 3);
+    if (threadIdx.x == 0) tickets[b * NKV + g] = 0u;  // ready for the next layer
 }
 
 // argmax order: larger value wins, ties to the lower index, NaN never wins (the reference CPU rule,
@@ -1219,10 +1223,15 @@ static int forward_pass(const Weights& w, const CacheView& c, const RowView* row
                 return QW_ERR_ARG;
             }
             const dim3 ag(n, NKV, splits);
-            if (G == 1) launch(row_attention<1>, dim3(ag), dim3(RA_THREADS), 0, s, sc.Q, rows, NQ, NKV, l, scale, sc.attp, splits);
-            else if (G == 2) launch(row_attention<2>, dim3(ag), dim3(RA_THREADS), 0, s, sc.Q, rows, NQ, NKV, l, scale, sc.attp, splits);
-            else launch(row_attention<3>, dim3(ag), dim3(RA_THREADS), 0, s, sc.Q, rows, NQ, NKV, l, scale, sc.attp, splits);
-            launch(row_merge, dim3(n, (NQ + 3) / 4), dim3(128), 0, s, sc.attp, rows, NQ, splits, sc.ahi, sc.alo);
+            if (G == 1)
+                launch(row_attention<1>, dim3(ag), dim3(RA_THREADS), 0, s, sc.Q, rows, NQ, NKV, l, scale, sc.attp, splits,
+                       sc.att_tickets, sc.ahi, sc.alo);
+            else if (G == 2)
+                launch(row_attention<2>, dim3(ag), dim3(RA_THREADS), 0, s, sc.Q, rows, NQ, NKV, l, scale, sc.attp, splits,
+                       sc.att_tickets, sc.ahi, sc.alo);
+            else
+                launch(row_attention<3>, dim3(ag), dim3(RA_THREADS), 0, s, sc.Q, rows, NQ, NKV, l, scale, sc.attp, splits,
+                       sc.att_tickets, sc.ahi, sc.alo);
         } else {
             const size_t hsl = (size_t)l * NKV * c.max_seq * 128;
             rc = G == 1 ? launch_attention_tc<1>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, sc.attp,

@@ -64,6 +64,7 @@ struct Scratch {
     float* attp = nullptr;     // attention partials of split query tiles
     size_t attp_cap = 0;       // floats attp holds
     size_t ycap = 0;           // floats Y holds
+    unsigned* att_tickets = nullptr;  // row mode: [ROWS_MAX][NKV] split arrivals, zero between launches
 };
 
 // floats of Scratch::Y a pass over n rows needs (largest ksplit x n x N over the four GEMMs)
