@@ -261,6 +261,16 @@ __device__ __forceinline__ float dot8(uint4 w, const float* x) {
     return a + b;
 }
 
+// Packed-f32 form of dot8 (Blackwell's two-lane FFMA2): the 8 products are accumulated into
+// (acc.x, acc.y) in place, so a 16-byte chunk costs 8 bf16 conversions and 4 FMA instructions.
+__device__ __forceinline__ float2 dot8_acc2(uint4 w, const float* x, float2 acc) {
+    acc = __ffma2_rn(make_float2(bf16_lo(w.x), bf16_hi(w.x)), make_float2(x[0], x[1]), acc);
+    acc = __ffma2_rn(make_float2(bf16_lo(w.y), bf16_hi(w.y)), make_float2(x[2], x[3]), acc);
+    acc = __ffma2_rn(make_float2(bf16_lo(w.z), bf16_hi(w.z)), make_float2(x[4], x[5]), acc);
+    acc = __ffma2_rn(make_float2(bf16_lo(w.w), bf16_hi(w.w)), make_float2(x[6], x[7]), acc);
+    return acc;
+}
+
 // argmax ordering: larger value wins, ties to the lower index, NaN never wins (NONE_IDX = empty)
 __device__ __forceinline__ bool am_better(float av, unsigned ai, float bv, unsigned bi) {
     if (ai == NONE_IDX) return false;
@@ -692,8 +702,13 @@ public:
                         uint4 wv[4];
 #pragma unroll
                         for (int i = 0; i < 4; i++) wv[i] = wp[i * 32];
-#pragma unroll
-                        for (int i = 0; i < 4; i++) v[j] += dot8(wv[i], xr + i * 8);
+                        // two packed accumulators (chunks 0, 2 and 1, 3): 8 dependent FFMA2 each
+                        float2 e = make_float2(0.f, 0.f), o = e;
+                        e = dot8_acc2(wv[0], xr + 0, e);
+                        o = dot8_acc2(wv[1], xr + 8, o);
+                        e = dot8_acc2(wv[2], xr + 16, e);
+                        o = dot8_acc2(wv[3], xr + 24, o);
+                        v[j] = (e.x + e.y) + (o.x + o.y);
                     }
                 }
             }
