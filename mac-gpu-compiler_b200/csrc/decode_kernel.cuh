@@ -161,15 +161,22 @@ struct WarpGeo {
     int wbyte;        // byte offset of that row's segment within a piece
 };
 
-__device__ inline GemvGeo make_geo(long long rows, int K, int cta, int n, long long woff, int pair) {
+// `unit` (dividing the outputs) makes every CTA's share of outputs a whole number of units, so a
+// unit of 8 gives each CTA whole 64-byte blocks of the 8-byte hand-off words it publishes. Blocks
+// written by one CTA alone hand off faster: where CTAs' ranges share sectors, their stores and the
+// other CTAs' polls of those sectors contend (one all-CTA hand-off round of a 1024-word vector
+// measured 1.5 us with shared sectors, 0.9 us with one 64-byte block per CTA). Some CTAs may then
+// own no rows of a phase.
+__device__ inline GemvGeo make_geo(long long rows, int K, int cta, int n, long long woff, int pair, int unit = 1) {
     GemvGeo g;
     if (pair) {  // gate/up: partition pairs so each CTA owns whole (gate_i, up_i) row pairs
-        long long P = rows / 2;
-        g.r0 = (int)(2 * (P * cta / n));
-        g.r1 = (int)(2 * (P * (cta + 1) / n));
+        long long U = rows / 2 / unit;
+        g.r0 = (int)(2 * unit * (U * cta / n));
+        g.r1 = (int)(2 * unit * (U * (cta + 1) / n));
     } else {
-        g.r0 = (int)(rows * cta / n);
-        g.r1 = (int)(rows * (cta + 1) / n);
+        long long U = rows / unit;
+        g.r0 = (int)(unit * (U * cta / n));
+        g.r1 = (int)(unit * (U * (cta + 1) / n));
     }
     g.K = K;
     g.rpp = SLOT_BYTES / (2 * K);
@@ -323,10 +330,15 @@ public:
         const long long offC = qkvr * p.H;
         const long long offD = offC + (long long)p.H * qd;
         const long long offE = offD + 2LL * p.I * p.H;
-        qw_sm.geo[0] = make_geo(qkvr, p.H, c, nc, 0, 0);
-        qw_sm.geo[1] = make_geo(p.H, (int)qd, c, nc, offC, 0);
-        qw_sm.geo[2] = make_geo(2LL * p.I, p.H, c, nc, offD, 1);
-        qw_sm.geo[3] = make_geo(p.H, p.I, c, nc, offE, 0);
+        qw_sm.geo[0] = make_geo(qkvr, p.H, c, nc, 0, 0, qkvr % 8 == 0 && qkvr / 8 >= nc ? 8 : 1);
+        // q|k|v rows (A), x rows (C, E) and h values (D) in 64-byte units where the widths allow (see
+        // make_geo). Every CTA still owns rows of phase A (q|k|v units only when there are at least as
+        // many units as CTAs): the buffer-reuse argument (every phase's input is complete only after
+        // every CTA has read the previous contents) runs through phase A
+        const int ux = p.H % 8 == 0 ? 8 : 1, uh = p.I % 8 == 0 ? 8 : 1;
+        qw_sm.geo[1] = make_geo(p.H, (int)qd, c, nc, offC, 0, ux);
+        qw_sm.geo[2] = make_geo(2LL * p.I, p.H, c, nc, offD, 1, uh);
+        qw_sm.geo[3] = make_geo(p.H, p.I, c, nc, offE, 0, ux);
         qw_sm.geo[4] = make_geo(p.V, p.H, c, nc, 0, 0);
         for (int k = 0; k < 5; k++)
             for (int w = 0; w < NCW; w++) qw_sm.wgeo[k][w] = make_warp_geo(qw_sm.geo[k], w);

@@ -333,9 +333,10 @@ int qw_load(const char* path, int device, qw_model** out) {
     if (const char* e = std::getenv("QW_MIN_CHUNK")) m->min_chunk = std::max(1, std::min(1 << 20, std::atoi(e)));
     int nctas = prop.multiProcessorCount;
     if (const char* e = std::getenv("QW_CTAS")) nctas = std::max(1, std::min(nctas, std::atoi(e)));
-    // Buffers are reused across phases on the premise that every CTA contributes to every GEMV
-    // phase (so a CTA that sees a phase's complete input knows every CTA has finished reading the
-    // previous contents): every CTA must own at least one row of q|k|v, o/down and gate|up.
+    // Buffers are reused across phases on the premise that a phase's input is complete only after
+    // every CTA has finished reading the previous contents of the buffer it overwrites; the chain
+    // that guarantees it passes through phase A (q|k|v), so every CTA must own q|k|v rows (the
+    // o/down and gate|up partitions in 64-byte units may leave some CTAs without rows).
     nctas = (int)std::min<uint64_t>({(uint64_t)nctas, c.hidden, c.inter, c.heads * c.head_dim + 2 * c.kv_heads * c.head_dim});
     if ((uint64_t)nctas < c.kv_heads) { delete m; return set_err(QW_ERR_UNSUPPORTED, "fewer SMs than KV heads"); }
     m->nctas = nctas;
@@ -407,13 +408,18 @@ int qw_load(const char* path, int device, qw_model** out) {
     // scratch
     const int G = (int)(c.heads / c.kv_heads);
     auto ceil_div = [](uint64_t a, uint64_t b) { return (a + b - 1) / b; };
-    auto phase_cap = [&](uint64_t rows, uint64_t K) { return (uint64_t)seg_count((int)K) * (ceil_div(rows, nctas) + 2); };
-    uint64_t pc = std::max({phase_cap(QKVR, H), phase_cap(H, QD), phase_cap(2 * I, H) + 2, phase_cap(H, I), phase_cap(c.vocab, H)});
+    // most rows a CTA owns when rows are dealt out in units (the kernel's make_geo): x rows and h
+    // values go in units of 8 where the widths allow
+    const uint64_t ux = H % 8 == 0 ? 8 : 1, uh = I % 8 == 0 ? 8 : 1, uq = QKVR % 8 == 0 && QKVR / 8 >= (uint64_t)nctas ? 8 : 1;
+    auto max_rows = [&](uint64_t rows, uint64_t unit) { return unit * ceil_div(rows / unit, nctas); };
+    auto phase_cap = [&](uint64_t rows_per_cta, uint64_t K) { return (uint64_t)seg_count((int)K) * (rows_per_cta + 2); };
+    uint64_t pc = std::max({phase_cap(max_rows(QKVR, uq), H), phase_cap(max_rows(H, ux), QD),
+                            phase_cap(2 * max_rows(I, uh), H) + 2, phase_cap(max_rows(H, ux), I), phase_cap(ceil_div(c.vocab, nctas), H)});
     // part also stages the attention merge's partials: (S - 1) chunks x G heads x 128
     // and the 12 consumer warps' attention softmax states: NCW x G x ATT_WST
     m->part_cap = (int)align_up(std::max<uint64_t>({pc, (uint64_t)(m->S - 1) * G * HD, (uint64_t)NCW * G * ATT_WST}), 4);
     m->xs_cap = (int)align_up(std::max({H, QD, I}), 4);
-    m->xloc_cap = (int)align_up(ceil_div(H, nctas) + 2, 4);
+    m->xloc_cap = (int)align_up(max_rows(H, ux) + 2, 4);
     m->dyn_smem = (size_t)NSLOT * SLOT_BYTES + ((size_t)m->part_cap + m->xs_cap + m->xloc_cap) * 4;
     if (m->dyn_smem + sizeof(Smem) > (size_t)prop.sharedMemPerBlockOptin)
         return fail(QW_ERR_UNSUPPORTED, "model too large for the kernel's shared-memory plan (vocab or widths)");
