@@ -62,10 +62,10 @@ CONFIGS = {
 PUBLISHED_TPS = 46.37
 # DRAM traffic of the decode kernel relative to its algorithmic bytes, from one ncu capture of
 # mac-gpu-compiler_b200/profile_case.py's decode launch: a 4-token launch at positions 8..11 read
-# 4,777,293,000 B and wrote 5,276,928 B against 4,778,041,344 algorithmic bytes. The bench launch
+# 4,777,855,000 B and wrote 5,338,112 B against 4,778,041,344 algorithmic bytes. The bench launch
 # (128 tokens, ~158 GB) is too large to capture, and its traffic grows with the same weight + K/V
 # bytes per token, so roofline.traffic is that ratio times the launch's algorithmic bytes.
-NCU_TRAFFIC_RATIO = (4_777_293_000 + 5_276_928) / 4_778_041_344
+NCU_TRAFFIC_RATIO = (4_777_855_000 + 5_338_112) / 4_778_041_344
 
 
 def kv_bytes_at(cfg, pos: int) -> int:
