@@ -178,6 +178,18 @@ __device__ __forceinline__ void store_split4(uint16_t* hi, uint16_t* lo, size_t 
     *reinterpret_cast<uint2*>(lo + i) = make_uint2(*reinterpret_cast<const uint32_t*>(&l01), *reinterpret_cast<const uint32_t*>(&l23));
 }
 
+// v + p[0] + p[stride] + ... over n <= NS slices, added in slice order
+template <int NS>
+__device__ __forceinline__ float add_slices(float v, const float* p, int n, size_t stride) {
+    float pv[NS];
+#pragma unroll
+    for (int z = 0; z < NS; z++) pv[z] = z < n ? p[z * stride] : 0.f;
+#pragma unroll
+    for (int z = 0; z < NS; z++)
+        if (z < n) v += pv[z];
+    return v;
+}
+
 // X[t] = f32(embed[ids[t]]) (cpu_inference.rs:109-111)
 __global__ void embed_rows(const uint32_t* ids, int H, const uint16_t* embed, float* X) {
     pdl_wait();
@@ -211,12 +223,23 @@ __global__ void __launch_bounds__(ROW_THREADS) norm_split(float* X, int H, const
     for (int i = threadIdx.x; i < H; i += ROW_THREADS) {
         float v = x[i];
         const float* p = parts + (size_t)t * H + i;
-        float pv[KSPLIT_MAX];  // every slice's load in flight at once, then added in slice order
-#pragma unroll
-        for (int z = 0; z < KSPLIT_MAX; z++) pv[z] = z < nparts ? p[z * part_stride] : 0.f;
-#pragma unroll
-        for (int z = 0; z < KSPLIT_MAX; z++)
-            if (z < nparts) v += pv[z];
+        // slices added in slice order: four loads in flight per round for a prefill's few slices,
+        // every slice's load at once for the row mode's many (16 predicated loads per element
+        // would slow the prefill's 512-row passes)
+        if (nparts > 4) {
+            v = add_slices<KSPLIT_MAX>(v, p, nparts, part_stride);
+        } else {
+            int z = 0;
+            for (; z + 4 <= nparts; z += 4) {
+                const float a = p[z * part_stride], b = p[(z + 1) * part_stride], c = p[(z + 2) * part_stride],
+                            d = p[(z + 3) * part_stride];
+                v += a;
+                v += b;
+                v += c;
+                v += d;
+            }
+            for (; z < nparts; z++) v += p[z * part_stride];
+        }
         if (nparts) x[i] = v;
         ss = fmaf(v, v, ss);
     }
