@@ -58,6 +58,28 @@ def test_cuda_matches_cpu(geometry, n):
     print(f"{geometry}: max |cpu - gpu| = {worst:.3e}")
 
 
+@pytest.mark.parametrize("ctas", [100, 37])
+def test_uneven_row_partition(ctas, monkeypatch):
+    """Fewer CTAs than SMs (QW_CTAS, read at load): the 64-byte output units then fall unevenly
+    (100 CTAs: 8 or 16 x rows each; 37 CTAs: phase rows spanning more ring pieces than the ring
+    holds), and forward() and decode() must still match the oracle."""
+    monkeypatch.setenv("QW_CTAS", str(ctas))
+    cpu, gpu, cc, gc, ids, worst = _parity(randmodel.make_model("mid", 0), 12, max_seq=24)
+    assert gpu.num_ctas == ctas
+    logits = gpu.forward(ids[-1], len(ids), gc)
+    expected = cpu.forward(ids[-1], len(ids), cc)
+    assert float(np.abs(expected - logits).max()) < MAX_ABS_DIFF
+    tok = co.argmax(logits)
+    got = gpu.decode(tok, len(ids) + 1, 4, gc)
+    for i, t in enumerate(got):
+        ref = cpu.forward(tok, len(ids) + 1 + i, cc)
+        if co.top2_margin(ref) < MARGIN:
+            break
+        assert t == co.argmax(ref), f"step {i}"
+        tok = t
+    print(f"{ctas} CTAs: max |cpu - gpu| = {worst:.3e}")
+
+
 def test_kv_cache_matches_oracle(mid_model_path):
     cpu, gpu, cc, gc, ids, _ = _parity(mid_model_path, 12, seed=3, max_seq=20)
     n = len(ids)
