@@ -212,6 +212,10 @@ __device__ float block_sum(float v, float* red) {
 // X[t] += the nparts split-K slices of the previous projection (residual add, cpu_inference.rs:
 // 163-164, :171-172; slices summed in order), then A_hi/A_lo[t] = split(rmsnorm(X[t]) * gain)
 // (cpu_inference.rs:189-194)
+// MANY: up to KSPLIT_MAX slices with every load in flight (row mode); else up to 4 per round (a
+// prefill's few slices). Separate kernels, so the prefill's keeps the smaller register footprint
+// (two 1024-thread blocks per SM).
+template <bool MANY>
 __global__ void __launch_bounds__(ROW_THREADS) norm_split(float* X, int H, const uint16_t* gain, float eps, uint16_t* hi,
                                                           uint16_t* lo, const float* parts, int nparts, size_t part_stride) {
     pdl_wait();
@@ -223,10 +227,8 @@ __global__ void __launch_bounds__(ROW_THREADS) norm_split(float* X, int H, const
     for (int i = threadIdx.x; i < H; i += ROW_THREADS) {
         float v = x[i];
         const float* p = parts + (size_t)t * H + i;
-        // slices added in slice order: four loads in flight per round for a prefill's few slices,
-        // every slice's load at once for the row mode's many (16 predicated loads per element
-        // would slow the prefill's 512-row passes)
-        if (nparts > 4) {
+        // slices added in slice order
+        if (MANY) {
             v = add_slices<KSPLIT_MAX>(v, p, nparts, part_stride);
         } else {
             int z = 0;
@@ -1216,6 +1218,9 @@ int argmax_rows(const float* d_logits, int V, int B, RowView* d_rows, uint32_t* 
 
 // One forward pass over n rows: prefill (rows == null; token t at position start + t of cache c)
 // or row mode (rows != null; token t at rows[t].pos of its own cache, `splits` attention splits).
+typedef void (*NormSplitFn)(float*, int, const uint16_t*, float, uint16_t*, uint16_t*, const float*, int, size_t);
+inline NormSplitFn norm_kernel(int nparts) { return nparts > 4 ? norm_split<true> : norm_split<false>; }
+
 static int forward_pass(const Weights& w, const CacheView& c, const RowView* rows, int splits, const uint32_t* d_ids, int n,
                         int start, float* d_logits, Scratch& sc, int* err_word, cudaStream_t s, std::string& err) {
     const int H = w.H, I = w.I, NQ = w.NQ, NKV = w.NKV, QD = NQ * 128, KVD = NKV * 128, QKVR = QD + 2 * KVD;
@@ -1234,7 +1239,8 @@ static int forward_pass(const Weights& w, const CacheView& c, const RowView* row
         const uint16_t* nrm = w.layer_n + (size_t)l * w.norm_stride;
         int rc;
         // A: (the previous layer's down_proj slices into X) rmsnorm -> q|k|v
-        launch(norm_split, dim3(n), dim3(ROW_THREADS), 0, s, sc.X, H, nrm, w.eps, sc.ahi, sc.alo, sc.Y, l == 0 ? 0 : ks_d, nH);
+        launch(norm_kernel(l == 0 ? 0 : ks_d), dim3(n), dim3(ROW_THREADS), 0, s, sc.X, H, nrm, w.eps, sc.ahi, sc.alo, sc.Y,
+               l == 0 ? 0 : ks_d, nH);
         if ((rc = tc::gemm(sc.ahi, sc.alo, H, W, H, sc.Y, QKVR, n, QKVR, H, err_word, s, err, ks_qkv))) return rc;
         // B: q/k norm + RoPE, K/V into the cache, attention -> o_proj input halves
         const int items = n * (NQ + 2 * NKV);
@@ -1275,7 +1281,7 @@ static int forward_pass(const Weights& w, const CacheView& c, const RowView* row
         // C: o_proj (its slices go into X in the next norm)
         if ((rc = tc::gemm(sc.ahi, sc.alo, QD, W + (size_t)QKVR * H, QD, sc.Y, H, n, H, QD, err_word, s, err, ks_o))) return rc;
         // D: residual + rmsnorm -> gate|up -> silu(gate) * up
-        launch(norm_split, dim3(n), dim3(ROW_THREADS), 0, s, sc.X, H, nrm + H, w.eps, sc.ahi, sc.alo, sc.Y, ks_o, nH);
+        launch(norm_kernel(ks_o), dim3(n), dim3(ROW_THREADS), 0, s, sc.X, H, nrm + H, w.eps, sc.ahi, sc.alo, sc.Y, ks_o, nH);
         const uint16_t* Wgu = W + (size_t)QKVR * H + (size_t)H * QD;
         if ((rc = tc::gemm(sc.ahi, sc.alo, H, Wgu, H, sc.Y, 2 * I, n, 2 * I, H, err_word, s, err, ks_gu))) return rc;
         launch(silu_split, dim3(grid_for((size_t)n * I)), dim3(256), 0, s, sc.Y, (size_t)n * I, sc.ahi, sc.alo, ks_gu);
@@ -1285,7 +1291,7 @@ static int forward_pass(const Weights& w, const CacheView& c, const RowView* row
     }
     // the last down_proj's slices go into X with the final norm; without logits, add them alone
     if (d_logits) {
-        launch(norm_split, dim3(n), dim3(ROW_THREADS), 0, s, sc.X, H, w.final_norm, w.eps, sc.ahi, sc.alo, sc.Y, ks_d, nH);
+        launch(norm_kernel(ks_d), dim3(n), dim3(ROW_THREADS), 0, s, sc.X, H, w.final_norm, w.eps, sc.ahi, sc.alo, sc.Y, ks_d, nH);
         int rc;
         if ((rc = tc::gemm(sc.ahi, sc.alo, H, w.lm_head, H, d_logits, w.V, n, w.V, H, err_word, s, err, 1))) return rc;
     } else {
