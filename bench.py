@@ -470,11 +470,12 @@ def run_reference(args, cfg_name: str) -> None:
     print(json.dumps({
         "impl": "reference",
         "metric": ("Qwen3-0.6B bf16 batched prefill tok/s (512-token prompt, per-position logits)" if cfg_name == "prefill"
-                   else "Qwen3-0.6B bf16 decode tok/s @bs1"),
+                   else "Qwen3-0.6B bf16 decode tok/s @bs1 & % of HBM roofline; box tok/s at 1-8 GPUs"),
         "value": v, "unit": "tok/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "dtype": "bf16", "data": "synthetic",
         "config": {"workload": c["label"], "model": "Qwen3-0.6B geometry, random-init bf16 (seed 0)",
+                   "global_batch": c.get("sequences", 1), "seq_len": c["prompt"] + c["decode"],
                    "engine": "CPU oracle: C++ restatement of metal_infrence_engine/src/cpu_inference.rs "
                              "(the Rust original needs cargo, absent on these machines)"},
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": co.threads(), "kind": "port", "sample": sample},
