@@ -218,6 +218,12 @@ __device__ float block_sum(float v, float* red) {
 template <bool MANY>
 __global__ void __launch_bounds__(ROW_THREADS) norm_split(float* X, int H, const uint16_t* gain, float eps, uint16_t* hi,
                                                           uint16_t* lo, const float* parts, int nparts, size_t part_stride) {
+    // rows of at most ROW_THREADS elements: one per thread, its gain fetched before waiting for the
+    // kernels that produce X and the slices (the gains do not depend on them), its value kept in a
+    // register for the output pass
+    const bool one = H <= ROW_THREADS;
+    float g1 = 0.f, v1 = 0.f;
+    if (one && (int)threadIdx.x < H) g1 = bf16f(gain[threadIdx.x]);
     pdl_wait();
     pdl_trigger();
     __shared__ float red[ROW_THREADS / 32];
@@ -244,9 +250,14 @@ __global__ void __launch_bounds__(ROW_THREADS) norm_split(float* X, int H, const
         }
         if (nparts) x[i] = v;
         ss = fmaf(v, v, ss);
+        v1 = v;
     }
     const float sc = rsqrtf(block_sum(ss, red) / (float)H + eps);
-    for (int i = threadIdx.x; i < H; i += ROW_THREADS) split_store(x[i] * sc * bf16f(gain[i]), hi, lo, (size_t)t * H + i);
+    if (one) {
+        if ((int)threadIdx.x < H) split_store(v1 * sc * g1, hi, lo, (size_t)t * H + threadIdx.x);
+    } else {
+        for (int i = threadIdx.x; i < H; i += ROW_THREADS) split_store(x[i] * sc * bf16f(gain[i]), hi, lo, (size_t)t * H + i);
+    }
 }
 
 // A_hi/A_lo = split(src) over n rows of K
@@ -291,13 +302,11 @@ __global__ void silu_split(const float* Y, size_t n_inter, uint16_t* hi, uint16_
 // token t is row t, at rows[t].pos of its own cache.
 __global__ void qkv_post(const float* Y, int nparts, int n, int start, int NQ, int NKV, const uint16_t* qn,
                          const uint16_t* kn, float eps, CacheView c, const RowView* rows, int layer, float* Q) {
-    pdl_wait();
-    pdl_trigger();
     const int warps = blockDim.x >> 5;
     const int item = blockIdx.x * warps + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     const int per_tok = NQ + 2 * NKV;
-    if (item >= n * per_tok) return;
-    const int t = item / per_tok, hh = item - t * per_tok;
+    const bool live = item < n * per_tok;
+    const int t = live ? item / per_tok : 0, hh = live ? item - t * per_tok : 0;
     int pos = start + t, max_seq = c.max_seq;
     float *Kc = c.k, *Vc = c.v;
     const float2* rope = c.rope;
@@ -309,6 +318,23 @@ __global__ void qkv_post(const float* Y, int nparts, int n, int start, int NQ, i
         Vc = rv.v;
         rope = rv.rope;
     }
+    // the head-norm gains and the RoPE row do not depend on earlier kernels (a row's position was
+    // set by the previous step's argmax, which every later kernel of the chain waited for): fetch
+    // them before waiting for the projection's output
+    const int d0 = lane * 4;
+    float gv[4] = {0.f, 0.f, 0.f, 0.f};
+    float2 cs[4] = {};
+    if (live && hh < NQ + NKV) {
+        const uint16_t* gw = hh < NQ ? qn : kn;
+        const float2* rr = rope + (size_t)pos * 64;
+        for (int j = 0; j < 4; j++) {
+            gv[j] = bf16f(gw[d0 + j]);
+            cs[j] = rr[(d0 + j) & 63];
+        }
+    }
+    pdl_wait();
+    pdl_trigger();
+    if (!live) return;
     const size_t head_stride_l = (size_t)layer * NKV * max_seq * 128;
     const int QKVR = per_tok * 128;
     const size_t ps = (size_t)n * QKVR;
@@ -325,18 +351,14 @@ __global__ void qkv_post(const float* Y, int nparts, int n, int start, int NQ, i
         reinterpret_cast<float4*>(Vc + head_stride_l + ((size_t)g * max_seq + pos) * 128)[lane] = v;
         return;
     }
-    const uint16_t* gw = hh < NQ ? qn : kn;
     float ss = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
     const float s = rsqrtf(ss / 128.0f + eps);
-    const int d0 = lane * 4;
     float e[4] = {v.x, v.y, v.z, v.w}, o4[4];
-    for (int j = 0; j < 4; j++) e[j] = e[j] * s * bf16f(gw[d0 + j]);
-    const float2* rr = rope + (size_t)pos * 64;
+    for (int j = 0; j < 4; j++) e[j] = e[j] * s * gv[j];
     for (int j = 0; j < 4; j++) {
         const float other = __shfl_xor_sync(0xFFFFFFFFu, e[j], 16);  // element d +- 64
-        const float2 cs = rr[(d0 + j) & 63];
-        o4[j] = lane < 16 ? e[j] * cs.x - other * cs.y : e[j] * cs.x + other * cs.y;
+        o4[j] = lane < 16 ? e[j] * cs[j].x - other * cs[j].y : e[j] * cs[j].x + other * cs[j].y;
     }
     const float4 out = make_float4(o4[0], o4[1], o4[2], o4[3]);
     if (hh < NQ) reinterpret_cast<float4*>(Q + (size_t)t * NQ * 128 + (size_t)hh * 128)[lane] = out;
@@ -989,12 +1011,12 @@ template <int G>
 __global__ void __launch_bounds__(RA_THREADS) row_attention(const float* Q, const RowView* rows, int NQ, int NKV, int layer,
                                                             float scale, float* part, int splits, unsigned* tickets,
                                                             uint16_t* ahi, uint16_t* alo) {
-    pdl_wait();
-    pdl_trigger();
     __shared__ float sm_o[RA_WARPS][G][128];
     __shared__ float sm_m[RA_WARPS][G], sm_l[RA_WARPS][G];
     const int b = blockIdx.x, g = blockIdx.y, z = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // the row views were last written by the previous step's argmax, which every kernel since
+    // waited for, so they (and this split's K/V range) are known before waiting for qkv_post
     const RowView rv = rows[b];
     const int p_begin = z * ROW_SPLIT;
     if (p_begin > rv.pos) return;  // past this row's positions (the merge reads only live splits)
@@ -1002,6 +1024,15 @@ __global__ void __launch_bounds__(RA_THREADS) row_attention(const float* Q, cons
     const size_t head_off = ((size_t)layer * NKV + g) * rv.max_seq * 128;
     const float* kb = rv.k + head_off;
     const float* vb = rv.v + head_off;
+    // warm L2 with the split's K/V rows while the previous kernel finishes; the loads themselves
+    // come after the wait (qkv_post writes this step's rows, and in a multi-position pass other
+    // rows' positions too)
+    if (threadIdx.x == 0) {
+        bulk_prefetch_l2(kb + (size_t)p_begin * 128, (uint32_t)(p_end - p_begin) * 512u);
+        bulk_prefetch_l2(vb + (size_t)p_begin * 128, (uint32_t)(p_end - p_begin) * 512u);
+    }
+    pdl_wait();
+    pdl_trigger();
     float4 q[G], o[G];
     float m[G], l[G];
 #pragma unroll
