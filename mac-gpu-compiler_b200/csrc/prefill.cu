@@ -106,13 +106,22 @@ int gemm(const uint16_t* a_hi, const uint16_t* a_lo, int lda, const uint16_t* b,
         if ((rc = make_map_bf16(&mh, a_hi, (uint64_t)M, (uint64_t)K, (uint64_t)lda, SK_NB, err))) return rc;
         if ((rc = make_map_bf16(&ml, a_lo, (uint64_t)M, (uint64_t)K, (uint64_t)lda, SK_NB, err))) return rc;
         if ((rc = make_map_bf16(&mb, b, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, BN, err))) return rc;
-        if (cudaFuncSetAttribute(gemm_skinny_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM_BYTES) !=
-            cudaSuccess) {
+        // a launch of many waves (the lm_head: 1187 tiles) runs two 4-stage CTAs per SM
+        const bool wide = (long long)((N + BN - 1) / BN) * ksplit > 2 * 148;
+        if (cudaFuncSetAttribute(gemm_skinny_kernel<SK_STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM_BYTES) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(gemm_skinny_kernel<SK_STAGES_WIDE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 SK_SMEM_BYTES_WIDE) != cudaSuccess) {
             err = "cannot raise the skinny GEMM kernel's shared-memory limit";
             return QW_ERR_CUDA;
         }
         GemmArgs args{y, M, N, K, ldy, err_word, (long long)M * ldy};
-        launch(gemm_skinny_kernel, dim3((N + BN - 1) / BN, 1, ksplit), dim3(THREADS), SK_SMEM_BYTES, s, mh, ml, mb, args);
+        if (wide)
+            launch(gemm_skinny_kernel<SK_STAGES_WIDE>, dim3((N + BN - 1) / BN, 1, ksplit), dim3(THREADS), SK_SMEM_BYTES_WIDE, s, mh,
+                   ml, mb, args);
+        else
+            launch(gemm_skinny_kernel<SK_STAGES>, dim3((N + BN - 1) / BN, 1, ksplit), dim3(THREADS), SK_SMEM_BYTES, s, mh, ml, mb,
+                   args);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) {
             err = std::string("GEMM launch failed: ") + cudaGetErrorString(e);

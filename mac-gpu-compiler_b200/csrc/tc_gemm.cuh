@@ -281,14 +281,20 @@ constexpr int SK_TILE_W = BN * BK * 2;             // 16 KB weight tile (128 row
 constexpr int SK_TILE_X = SK_NB * BK * 2;          // 2 KB activation half tile (16 rows x 64)
 constexpr int SK_STAGE_BYTES = SK_TILE_W + 2 * SK_TILE_X;
 constexpr int SK_SMEM_BYTES = SK_STAGES * SK_STAGE_BYTES + 1024;
+constexpr int SK_STAGES_WIDE = 4;                  // stages of a many-wave launch (two CTAs per SM)
+constexpr int SK_SMEM_BYTES_WIDE = SK_STAGES_WIDE * SK_STAGE_BYTES + 1024;
 constexpr int SK_TMEM_COLS = 32;                   // smallest allocation; columns 0..15 used
 
 // Y[M][ldy] (M <= 16) = (X_hi + X_lo)[M][K] . W[N][K]^T; CTA = 128 weight rows x one K range
+// STG ring stages: 8 for a layer's one-wave launches (the most weights in flight per SM); 4 for
+// many-wave launches (the lm_head), where two CTAs per SM let one stream while the other fills or
+// drains its pipeline
+template <int STG>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_skinny_kernel(const __grid_constant__ CUtensorMap map_xhi, const __grid_constant__ CUtensorMap map_xlo,
                    const __grid_constant__ CUtensorMap map_w, const GemmArgs args) {
     extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
-    __shared__ uint64_t full[SK_STAGES], empty[SK_STAGES], done;
+    __shared__ uint64_t full[STG], empty[STG], done;
     __shared__ uint32_t tmem_base;
     __shared__ volatile int abort_flag;
     uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
@@ -300,7 +306,7 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap map_xhi, const __grid_con
     float* const y = args.y + (long long)blockIdx.z * args.split_stride;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < SK_STAGES; s++) {
+        for (int s = 0; s < STG; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
@@ -322,7 +328,7 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap map_xhi, const __grid_con
 
     if (warp == 0 && lane == 0) {
         // weight tiles of the first stages before waiting for the previous kernel, activations after
-        const int pre = nkb < SK_STAGES ? nkb : SK_STAGES;
+        const int pre = nkb < STG ? nkb : STG;
         for (int kb = 0; kb < pre; kb++) {
             mbar_arrive_expect_tx(&full[kb], SK_STAGE_BYTES);
             tma_load_2d(ring + kb * SK_STAGE_BYTES, &map_w, (kb0 + kb) * BK, n0, &full[kb]);
@@ -336,8 +342,8 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap map_xhi, const __grid_con
         }
         issued_kb = pre;
         for (int kb = pre; kb < nkb; kb++) {
-            const int s = kb % SK_STAGES;
-            if (!bounded_wait(&empty[s], ((kb / SK_STAGES) - 1) & 1, &abort_flag)) break;
+            const int s = kb % STG;
+            if (!bounded_wait(&empty[s], ((kb / STG) - 1) & 1, &abort_flag)) break;
             uint8_t* st = ring + s * SK_STAGE_BYTES;
             mbar_arrive_expect_tx(&full[s], SK_STAGE_BYTES);
             tma_load_2d(st, &map_w, (kb0 + kb) * BK, n0, &full[s]);
@@ -347,8 +353,8 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap map_xhi, const __grid_con
         }
     } else if (warp == 1 && lane == 0) {
         for (int kb = 0; kb < nkb; kb++) {
-            const int s = kb % SK_STAGES;
-            if (!bounded_wait(&full[s], (kb / SK_STAGES) & 1, &abort_flag)) break;
+            const int s = kb % STG;
+            if (!bounded_wait(&full[s], (kb / STG) & 1, &abort_flag)) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t st = smem_u32(ring + s * SK_STAGE_BYTES);
             const uint64_t dw = smem_desc_k128(st), dhi = smem_desc_k128(st + SK_TILE_W),
@@ -378,9 +384,9 @@ gemm_skinny_kernel(const __grid_constant__ CUtensorMap map_xhi, const __grid_con
     }
     if (!ok && threadIdx.x == 0) atomicExch(args.err, 1);
     if (!ok && warp == 0 && lane == 0) {
-        for (int kb = issued_kb - SK_STAGES > 0 ? issued_kb - SK_STAGES : 0; kb < issued_kb; kb++) {
+        for (int kb = issued_kb - STG > 0 ? issued_kb - STG : 0; kb < issued_kb; kb++) {
             const uint64_t t0 = globaltimer_ns();
-            while (!mbar_try_wait(&full[kb % SK_STAGES], (kb / SK_STAGES) & 1))
+            while (!mbar_try_wait(&full[kb % STG], (kb / STG) & 1))
                 if (globaltimer_ns() - t0 > (uint64_t)WAIT_LIMIT_NS) break;
         }
     }
