@@ -132,13 +132,18 @@ int gemm(const uint16_t* a_hi, const uint16_t* a_lo, int lda, const uint16_t* b,
     if ((rc = make_map_bf16(&mh, a_hi, (uint64_t)M, (uint64_t)K, (uint64_t)lda, BM, err))) return rc;
     if ((rc = make_map_bf16(&ml, a_lo, (uint64_t)M, (uint64_t)K, (uint64_t)lda, BM, err))) return rc;
     if ((rc = make_map_bf16(&mb, b, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, BN, err))) return rc;
-    if (cudaFuncSetAttribute(gemm_bf16x2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess) {
+    if (cudaFuncSetAttribute(gemm_bf16x2_kernel<STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(gemm_bf16x2_kernel<STAGES_WIDE>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES_WIDE) !=
+            cudaSuccess) {
         err = "cannot raise the GEMM kernel's shared-memory limit";
         return QW_ERR_CUDA;
     }
     GemmArgs args{y, M, N, K, ldy, err_word, (long long)M * ldy};
     dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, ksplit);
-    launch(gemm_bf16x2_kernel, dim3(grid), dim3(THREADS), SMEM_BYTES, s, mh, ml, mb, args);
+    if ((long long)grid.x * grid.y * grid.z > 148)
+        launch(gemm_bf16x2_kernel<STAGES_WIDE>, dim3(grid), dim3(THREADS), SMEM_BYTES_WIDE, s, mh, ml, mb, args);
+    else
+        launch(gemm_bf16x2_kernel<STAGES>, dim3(grid), dim3(THREADS), SMEM_BYTES, s, mh, ml, mb, args);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         err = std::string("GEMM launch failed: ") + cudaGetErrorString(e);

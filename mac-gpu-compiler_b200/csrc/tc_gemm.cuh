@@ -47,6 +47,10 @@ constexpr int TILE_A = BM * BK * 2;          // bytes of one A half tile (16 KB)
 constexpr int TILE_B = BN * BK * 2;          // bytes of one B tile (16 KB)
 constexpr int STAGE_BYTES = 2 * TILE_A + TILE_B;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024;  // + alignment slack for the 1024-byte swizzle atoms
+// launches of more tiles than SMs use 2 stages, so two CTAs share an SM (TMEM 2 x 128 columns) and
+// one's MMAs overlap the other's pipeline fill and epilogue
+constexpr int STAGES_WIDE = 2;
+constexpr int SMEM_BYTES_WIDE = STAGES_WIDE * STAGE_BYTES + 1024;
 constexpr int THREADS = 128;
 constexpr int TMEM_COLS = BN;                // f32 accumulator columns
 constexpr long long WAIT_LIMIT_NS = 2000000000ll;
@@ -140,11 +144,12 @@ struct GemmArgs {
     long long split_stride;  // elements between the outputs of K splits (blockIdx.z)
 };
 
+template <int STG>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_bf16x2_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
                    const __grid_constant__ CUtensorMap map_b, const GemmArgs args) {
     extern __shared__ __align__(1024) uint8_t tc_smem_raw[];
-    __shared__ uint64_t full[STAGES], empty[STAGES], done;
+    __shared__ uint64_t full[STG], empty[STG], done;
     __shared__ uint32_t tmem_base;
     __shared__ volatile int abort_flag;
     // 1024-byte aligned ring (the 128-byte swizzle atom spans 8 rows x 128 bytes)
@@ -158,7 +163,7 @@ gemm_bf16x2_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_con
     float* const y = args.y + (long long)blockIdx.z * args.split_stride;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; s++) {
+        for (int s = 0; s < STG; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
@@ -181,23 +186,23 @@ gemm_bf16x2_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_con
     if (warp == 0 && lane == 0) {
         // the first stages' weight tiles do not depend on the previous kernel: issue them before
         // waiting for it (programmatic dependent launch), the activation tiles after
-        const int pre = nkb < STAGES ? nkb : STAGES;
+        const int pre = nkb < STG ? nkb : STG;
         for (int kb = 0; kb < pre; kb++) {
-            uint8_t* st = ring + (kb % STAGES) * STAGE_BYTES;
+            uint8_t* st = ring + (kb % STG) * STAGE_BYTES;
             mbar_arrive_expect_tx(&full[kb], STAGE_BYTES);
             tma_load_2d(st + 2 * TILE_A, &map_b, (kb0 + kb) * BK, n0, &full[kb]);
         }
         pdl_wait();
         pdl_trigger();
         for (int kb = 0; kb < pre; kb++) {
-            uint8_t* st = ring + (kb % STAGES) * STAGE_BYTES;
+            uint8_t* st = ring + (kb % STG) * STAGE_BYTES;
             tma_load_2d(st, &map_ahi, (kb0 + kb) * BK, m0, &full[kb]);
             tma_load_2d(st + TILE_A, &map_alo, (kb0 + kb) * BK, m0, &full[kb]);
         }
         issued_kb = pre;
         for (int kb = pre; kb < nkb; kb++) {
-            const int s = kb % STAGES;
-            if (!bounded_wait(&empty[s], ((kb / STAGES) - 1) & 1, &abort_flag)) break;
+            const int s = kb % STG;
+            if (!bounded_wait(&empty[s], ((kb / STG) - 1) & 1, &abort_flag)) break;
             uint8_t* st = ring + s * STAGE_BYTES;
             mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
             tma_load_2d(st, &map_ahi, (kb0 + kb) * BK, m0, &full[s]);
@@ -207,8 +212,8 @@ gemm_bf16x2_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_con
         }
     } else if (warp == 1 && lane == 0) {
         for (int kb = 0; kb < nkb; kb++) {
-            const int s = kb % STAGES;
-            if (!bounded_wait(&full[s], (kb / STAGES) & 1, &abort_flag)) break;
+            const int s = kb % STG;
+            if (!bounded_wait(&full[s], (kb / STG) & 1, &abort_flag)) break;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t st = smem_u32(ring + s * STAGE_BYTES);
             const uint64_t dhi = smem_desc_k128(st), dlo = smem_desc_k128(st + TILE_A), db = smem_desc_k128(st + 2 * TILE_A);
@@ -253,9 +258,9 @@ gemm_bf16x2_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_con
     if (!ok && threadIdx.x == 0) atomicExch(args.err, 1);
     // after an abort, the TMA copies still in flight must land before the CTA exits
     if (!ok && warp == 0 && lane == 0) {
-        for (int kb = issued_kb - STAGES > 0 ? issued_kb - STAGES : 0; kb < issued_kb; kb++) {
+        for (int kb = issued_kb - STG > 0 ? issued_kb - STG : 0; kb < issued_kb; kb++) {
             const uint64_t t0 = globaltimer_ns();
-            while (!mbar_try_wait(&full[kb % STAGES], (kb / STAGES) & 1))
+            while (!mbar_try_wait(&full[kb % STG], (kb / STG) & 1))
                 if (globaltimer_ns() - t0 > (uint64_t)WAIT_LIMIT_NS) break;
         }
     }
