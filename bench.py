@@ -1,6 +1,6 @@
-"""Benchmark: batch-1 Qwen3-0.6B bf16 greedy decode on B200 (BASELINE.json `metric`).
+"""Benchmark: batch-1 Qwen3-0.6B bf16 greedy decode on B200 (the benchmark metric: decode tok/s at batch 1 and the HBM roofline fraction).
 
-Workload (the configuration the reference's headline tok/s is quoted on,
+Workload (configs[0], the configuration the reference's headline tok/s is quoted on,
 metal_infrence_engine/README.md:15-24): the Qwen3-0.6B geometry with seeded random-init bf16
 weights, a 130-id seeded prompt fed token by token, then 128 greedy decode steps at positions
 130..257, batch 1, f32 KV cache. One bench STEP = one 128-token greedy decode from the prefilled

@@ -82,7 +82,7 @@ size_t qw_cache_max_seq(const qw_cache* cache); /* MetalKVCache::max_seq (metal_
  * cache, copy vocab_size f32 logits to `logits_out` (host). Synchronous. */
 int qw_forward(qw_model* model, qw_cache* cache, uint32_t token, size_t pos, float* logits_out);
 
-/* Batched prefill (the reference feeds a prompt token by token through
+/* Batched prefill (the 512-token prompt workload; the reference feeds a prompt token by token through
  * forward, metal_inference.rs:286-291, src/bin/bench.rs:166-191): one pass over ids[0..n) at
  * positions start_pos .. start_pos+n-1 whose projections run as tcgen05 tensor-core GEMMs over all
  * n tokens. Writes their K/V into the cache exactly where n forward calls would; with logits_out
@@ -95,7 +95,7 @@ int qw_prefill(qw_model* model, qw_cache* cache, const uint32_t* ids, size_t n, 
 int qw_prefill_device(qw_model* model, qw_cache* cache, const uint32_t* d_ids, size_t n, size_t start_pos,
                       float* d_logits, void* stream);
 
-/* Batch decode (its per-GPU batch-8 variant): B independent sequences, each
+/* Batch decode (the box workload's per-GPU batch-8 variant): B independent sequences, each
  * with its own cache, advance one token per step together, so each step streams the weights once
  * for all B (the reference decodes one sequence per engine, metal_inference.rs:286-387). Every
  * projection is a tcgen05 GEMM over the B rows; attention runs per row over the row's own cache.

@@ -1,4 +1,4 @@
-// Batched prefill: the tcgen05 GEMM's host side (tensor maps, launch) and
+// Batched prefill (the 512-token prompt workload, configs[3]): the tcgen05 GEMM's host side (tensor maps, launch) and
 // the standalone entry point qw_gemm_bf16x2 (see tc_gemm.cuh for the kernel).
 #include <cuda.h>
 #include <cuda_bf16.h>

@@ -1,4 +1,4 @@
-"""the isolated bf16 GEMV microbenchmark.
+"""Benchmark config 3: the isolated bf16 GEMV microbenchmark.
 
 y = W x with W bf16 ~ N(0, 0.02) [rows x cols], x f32 ~ N(0, 1), at the decode step's shapes:
 q [2048x1024], k+v [1024x1024]... o [1024x2048], fused gate+up [6144x1024], down [1024x3072] and

@@ -8,7 +8,7 @@ written by ``csrc/randmodel.cpp`` (built into ``librandmodel.so``); this module 
 Hugging Face keys needed to load the same directory with ``transformers``.
 
 Named geometries:
-  qwen3-0.6b  the BASELINE model: hidden 1024, 28 layers, 16/8 heads, head_dim 128,
+  qwen3-0.6b  the benchmark model: hidden 1024, 28 layers, 16/8 heads, head_dim 128,
               SwiGLU 3072, vocab 151936, tied embedding, RoPE theta 1e6, eps 1e-6
   mid         the same per-layer shapes with 3 layers and a ragged vocab (10007)
   tiny        a small model for fast CPU checks (hidden 256, 2 layers, vocab 1000)

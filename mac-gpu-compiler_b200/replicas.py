@@ -4,7 +4,7 @@ the data path.
 Batch-1 decode of one sequence is not split across GPUs (a per-layer all-reduce would cost more
 than the 1.2 GB weight read it saves). The box runs one process per GPU instead: every rank loads
 its own copy of the weights and decodes its own share of the independent sequences
-(64 sequences of a 130-id prompt plus 128 greedy steps). The only
+(the box workload, configs[4]: 64 sequences of a 130-id prompt plus 128 greedy steps). The only
 cross-rank traffic is host-side bookkeeping around the timed region: a barrier before it, the
 max of the ranks' device times after it, and the gathered token counts.
 

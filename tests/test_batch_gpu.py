@@ -1,4 +1,4 @@
-"""Batch decode (qw_forward_batch / qw_decode_batch, BASELINE configs[4]'s per-GPU batch variant)
+"""Batch decode (qw_forward_batch / qw_decode_batch, the box workload's per-GPU batch variant)
 against the CPU oracle, through the C ABI.
 
 B independent sequences, each with its own prompt length and cache, step together. The rules are

@@ -1,4 +1,4 @@
-"""Standalone kernels through the C ABI: the decode kernel's GEMV machinery at BASELINE config 3's
+"""Standalone kernels through the C ABI: the decode kernel's GEMV machinery at benchmark config 3's
 shapes against float64 accumulation, the argmax rule bit-exact against the oracle's
 (tests/common/mod.rs:17-22), and the streaming-read probe (tests/read_bandwidth.rs:122-124)."""
 from __future__ import annotations

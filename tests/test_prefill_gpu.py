@@ -1,4 +1,4 @@
-"""Batched prefill (qw_prefill) against the reference CPU engine's token-by-token
+"""Batched prefill (qw_prefill, the 512-token prompt workload) against the reference CPU engine's token-by-token
 prefill (the oracle, cpu_inference.rs:100-179): every position's logits within 1e-2 max-abs, the
 K/V cache filled at the same slots (indexing exact, values within the f32 tolerance of the
 reordered arithmetic), and a greedy decode continuing from a prefilled cache producing the same
