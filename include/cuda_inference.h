@@ -187,6 +187,15 @@ int qw_read_trace(qw_model* model, uint64_t* out, size_t capacity);
 int qw_gemv_bf16(int device, const uint16_t* d_w, const float* d_x, float* d_y, size_t rows, size_t cols,
                  void* stream);
 
+/* The same GEMV over `count` matrices of one shape stored back to back (d_w [count][rows][cols],
+ * d_y [count][rows], one x) in ONE launch: every CTA owns the same rows of each matrix as in
+ * qw_gemv_bf16 and streams matrix after matrix, the way the decode kernel streams layer after layer.
+ * It measures the steady-state streaming rate of a layer-sized shape, which a single launch of a
+ * few MB cannot show (the reference's tests/read_bandwidth.rs:69-141 likewise
+ * times many passes back to back). count >= 1. */
+int qw_gemv_bf16_seq(int device, const uint16_t* d_w, const float* d_x, float* d_y, size_t rows, size_t cols,
+                     size_t count, void* stream);
+
 /* *d_out = first index of the largest element (tests/common/mod.rs:17-22: ties to the lowest
  * index, a NaN at index 0 gives 0, other NaNs never win; the GPU argmax of
  * shaders/inference.metal:300-321). d_workspace holds qw_argmax_workspace_size(n) bytes. */

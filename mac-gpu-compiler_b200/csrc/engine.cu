@@ -650,7 +650,7 @@ int qw_prefill(qw_model* m, qw_cache* c, const uint32_t* ids, size_t n, size_t s
     if (int e = ensure_prefill(m, n, start_pos, logits_out != nullptr)) return e;
     int* ew = qw::device_err_word_for(m->device);
     if (!ew) return set_err(QW_ERR_NOMEM, "error word allocation failed");
-    QW_CUDA(cudaMemsetAsync(ew, 0, sizeof(int), m->stream));
+    QW_CUDA(cudaMemsetAsync(ew, 0, 2 * sizeof(int), m->stream));
     QW_CUDA(cudaMemcpyAsync(m->d_pf_ids, ids, n * 4, cudaMemcpyHostToDevice, m->stream));
     const ModelConfig& cf = m->cfg;
     qw::pf::Weights w{m->d_layer_w, m->d_layer_n, m->d_final_norm, m->d_embed, m->d_lm_head, m->layer_stride, m->norm_stride,
@@ -661,10 +661,10 @@ int qw_prefill(qw_model* m, qw_cache* c, const uint32_t* ids, size_t n, size_t s
                             m->stream, err))
         return set_err(e, err);
     if (logits_out) QW_CUDA(cudaMemcpyAsync(logits_out, m->d_pf_logits, n * cf.vocab * 4, cudaMemcpyDeviceToHost, m->stream));
-    int h = 0;
-    QW_CUDA(cudaMemcpyAsync(&h, ew, sizeof(int), cudaMemcpyDeviceToHost, m->stream));
+    int h[2] = {0, 0};
+    QW_CUDA(cudaMemcpyAsync(h, ew, sizeof h, cudaMemcpyDeviceToHost, m->stream));
     QW_CUDA(cudaStreamSynchronize(m->stream));
-    if (h) return set_err(QW_ERR_DEVICE_TIMEOUT, "prefill: a GEMM pipeline wait expired on the device");
+    if (h[0]) return set_err(QW_ERR_DEVICE_TIMEOUT, "prefill: a GEMM pipeline wait expired on the device");
     return QW_OK;
 }
 
@@ -678,7 +678,7 @@ int qw_prefill_device(qw_model* m, qw_cache* c, const uint32_t* d_ids, size_t n,
     int* ew = qw::device_err_word_for(m->device);
     if (!ew) return set_err(QW_ERR_NOMEM, "error word allocation failed");
     cudaStream_t s = pick_stream(m, stream);
-    QW_CUDA(cudaMemsetAsync(ew, 0, sizeof(int), s));
+    QW_CUDA(cudaMemsetAsync(ew, 0, 2 * sizeof(int), s));
     const ModelConfig& cf = m->cfg;
     qw::pf::Weights w{m->d_layer_w, m->d_layer_n, m->d_final_norm, m->d_embed, m->d_lm_head, m->layer_stride, m->norm_stride,
                       (int)cf.hidden, (int)cf.inter, (int)cf.layers, (int)cf.heads, (int)cf.kv_heads, (int)cf.vocab, cf.eps};
@@ -790,7 +790,7 @@ int batch_decode_launch(qw_model* m, qw_cache* const* caches, size_t B, const si
     if (!ew) return set_err(QW_ERR_NOMEM, "error word allocation failed");
     cudaGraphExec_t g = nullptr;
     if (int e = row_graph(m, 0, (int)B, splits, m->d_bout, ew, g)) return e;
-    QW_CUDA(cudaMemsetAsync(ew, 0, sizeof(int), s));
+    QW_CUDA(cudaMemsetAsync(ew, 0, 2 * sizeof(int), s));
     QW_CUDA(cudaMemcpyAsync(m->d_rows, rows.data(), B * sizeof(qw::pf::RowView), cudaMemcpyHostToDevice, s));
     for (size_t i = 0; i < steps; i++) QW_CUDA(cudaGraphLaunch(g, s));
     return QW_OK;
@@ -811,7 +811,7 @@ int qw_forward_batch(qw_model* m, qw_cache* const* caches, size_t B, const uint3
     int* ew = qw::device_err_word_for(m->device);
     if (!ew) return set_err(QW_ERR_NOMEM, "error word allocation failed");
     cudaStream_t s = m->stream;
-    QW_CUDA(cudaMemsetAsync(ew, 0, sizeof(int), s));
+    QW_CUDA(cudaMemsetAsync(ew, 0, 2 * sizeof(int), s));
     QW_CUDA(cudaMemcpyAsync(m->d_rows, rows.data(), B * sizeof(qw::pf::RowView), cudaMemcpyHostToDevice, s));
     QW_CUDA(cudaMemcpyAsync(m->d_btok, tokens, B * 4, cudaMemcpyHostToDevice, s));
     std::string err;
@@ -915,7 +915,7 @@ int qw_decode_lookup(qw_model* m, qw_cache* c, const uint32_t* context, size_t c
     int* ew = qw::device_err_word_for(m->device);
     if (!ew) return set_err(QW_ERR_NOMEM, "error word allocation failed");
     cudaStream_t s = m->stream;
-    QW_CUDA(cudaMemsetAsync(ew, 0, sizeof(int), s));
+    QW_CUDA(cudaMemsetAsync(ew, 0, 2 * sizeof(int), s));
     std::vector<qw::pf::RowView> rows;
     std::vector<uint32_t> hist(context, context + context_len);
     hist.push_back(first);
@@ -1049,12 +1049,14 @@ int qw_sync(qw_model* m, void* stream) {
     QW_CUDA(cudaStreamSynchronize(pick_stream(m, stream)));
     if (int e = check_device_err(m)) return e;
     // the prefill GEMMs report an expired pipeline wait through the device's shared error word
+    // (word 0) and an input id >= vocab_size in device memory (word 1, read as row 0 instead)
     if (int* ew = qw::device_err_word_for(m->device)) {
-        int h = 0;
-        QW_CUDA(cudaMemcpy(&h, ew, sizeof(int), cudaMemcpyDeviceToHost));
-        if (h) {
-            QW_CUDA(cudaMemset(ew, 0, sizeof(int)));
-            return set_err(QW_ERR_DEVICE_TIMEOUT, "prefill: a GEMM pipeline wait expired on the device");
+        int h[2] = {0, 0};
+        QW_CUDA(cudaMemcpy(h, ew, sizeof h, cudaMemcpyDeviceToHost));
+        if (h[0] || h[1]) {
+            QW_CUDA(cudaMemset(ew, 0, sizeof h));
+            if (h[0]) return set_err(QW_ERR_DEVICE_TIMEOUT, "prefill: a GEMM pipeline wait expired on the device");
+            return set_err(QW_ERR_ARG, "device: an input token id >= vocab_size (row 0 was used instead)");
         }
     }
     return QW_OK;

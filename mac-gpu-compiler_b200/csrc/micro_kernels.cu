@@ -24,8 +24,10 @@ int set_error(int code, const char* msg);
 
 namespace {
 
+// y[m] = W[m] x for m < count (matrices [count][rows][cols] back to back); count = 1 is the plain GEMV
 __global__ void __launch_bounds__(NTHREADS, 1)
-gemv_kernel(const __grid_constant__ DecodeParams p, const uint16_t* w, const float* x, float* y, int rows, int cols) {
+gemv_kernel(const __grid_constant__ DecodeParams p, const uint16_t* w, const float* x, float* y, int rows, int cols,
+            int count) {
     if (threadIdx.x == 0) {
         for (int i = 0; i < NSLOT; i++) {
             mbar_init(&qw_sm.full[i], 1);
@@ -42,17 +44,22 @@ gemv_kernel(const __grid_constant__ DecodeParams p, const uint16_t* w, const flo
     }
     __syncthreads();
     const GemvGeo& g = qw_sm.geo[0];
+    const size_t mat = (size_t)rows * cols;
     if (Decoder::warp() == NCW) {
         if (Decoder::lane() == 0) {
-            Decoder::gemv_produce(g, w);
+            for (int m = 0; m < count; m++) Decoder::gemv_produce(g, w + m * mat);
             Decoder::drain();
         }
         return;
     }
     for (int i = Decoder::tid(); i < cols; i += NCT) Decoder::xs()[xperm(i)] = x[i];
     named_bar_sync(1, NCT);
-    Decoder::gemv_consume<EPI_PART>(g);
-    for (int i = Decoder::tid(); i < g.r1 - g.r0; i += NCT) y[g.r0 + i] = Decoder::row_value(g, i);
+    for (int m = 0; m < count; m++) {
+        Decoder::gemv_consume<EPI_PART>(g);
+        float* ym = y + (size_t)m * rows;
+        for (int i = Decoder::tid(); i < g.r1 - g.r0; i += NCT) ym[g.r0 + i] = Decoder::row_value(g, i);
+        named_bar_sync(1, NCT);  // the next matrix's sums overwrite part()
+    }
 }
 
 // argmax with the reference CPU rule, in two levels inside one launch (last-block reduction)
@@ -182,7 +189,12 @@ int sm_count(int device) {
 extern "C" {
 
 int qw_gemv_bf16(int device, const uint16_t* d_w, const float* d_x, float* d_y, size_t rows, size_t cols, void* stream) {
-    if (!d_w || !d_x || !d_y || rows == 0) return set_error(QW_ERR_ARG, "bad gemv arguments");
+    return qw_gemv_bf16_seq(device, d_w, d_x, d_y, rows, cols, 1, stream);
+}
+
+int qw_gemv_bf16_seq(int device, const uint16_t* d_w, const float* d_x, float* d_y, size_t rows, size_t cols,
+                     size_t count, void* stream) {
+    if (!d_w || !d_x || !d_y || rows == 0 || count == 0 || count >= (1u << 20)) return set_error(QW_ERR_ARG, "bad gemv arguments");
     if (cols == 0 || cols > 12288 || seg_count((int)cols) == 0)
         return set_error(QW_ERR_UNSUPPORTED, "cols must split into 1, 2, 3, 4, 6 or 12 segments of 256-1024 columns");
     if (rows >= (1u << 30)) return set_error(QW_ERR_ARG, "rows too large");
@@ -208,7 +220,8 @@ int qw_gemv_bf16(int device, const uint16_t* d_w, const float* d_x, float* d_y, 
     if (smem + sizeof(Smem) > 227 * 1024) return set_error(QW_ERR_UNSUPPORTED, "rows too large for one launch");
     if (cudaFuncSetAttribute(gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return set_error(QW_ERR_CUDA, "cannot raise the gemv kernel's shared-memory limit");
-    gemv_kernel<<<n, NTHREADS, smem, static_cast<cudaStream_t>(stream)>>>(p, d_w, d_x, d_y, (int)rows, (int)cols);
+    gemv_kernel<<<n, NTHREADS, smem, static_cast<cudaStream_t>(stream)>>>(p, d_w, d_x, d_y, (int)rows, (int)cols,
+                                                                          (int)count);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_error(QW_ERR_CUDA, cudaGetErrorString(e));
     return QW_OK;

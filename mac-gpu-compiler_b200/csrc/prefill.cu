@@ -205,11 +205,19 @@ __device__ __forceinline__ float add_slices(float v, const float* p, int n, size
 }
 
 // X[t] = f32(embed[ids[t]]) (cpu_inference.rs:109-111)
-__global__ void embed_rows(const uint32_t* ids, int H, const uint16_t* embed, float* X) {
+// X[t] = embed[ids[t]] (cpu_inference.rs:109-111). An id >= V (device memory the host did not
+// check: qw_prefill_device, or a device first token of a batch decode) is never read through: the
+// row is taken from id 0 and err[1] is set, which the host reports as QW_ERR_ARG.
+__global__ void embed_rows(const uint32_t* ids, int H, int V, const uint16_t* embed, float* X, int* err) {
     pdl_wait();
     pdl_trigger();
     const int t = blockIdx.x;
-    const uint16_t* e = embed + (size_t)ids[t] * H;
+    uint32_t id = ids[t];
+    if (id >= (uint32_t)V) {
+        if (threadIdx.x == 0) atomicExch(err + 1, 1);
+        id = 0;
+    }
+    const uint16_t* e = embed + (size_t)id * H;
     for (int i = threadIdx.x; i < H; i += blockDim.x) X[(size_t)t * H + i] = bf16f(e[i]);
 }
 
@@ -1274,7 +1282,7 @@ static int forward_pass(const Weights& w, const CacheView& c, const RowView* row
         err = "GEMM output scratch too small";
         return QW_ERR_ARG;
     }
-    launch(embed_rows, dim3(n), dim3(256), 0, s, d_ids, H, w.embed, sc.X);
+    launch(embed_rows, dim3(n), dim3(256), 0, s, d_ids, H, w.V, w.embed, sc.X, err_word);
     const int G = NQ / NKV;
     const float scale = 1.0f / sqrtf(128.0f);
     const int ks_qkv = ksplit_for(n, QKVR, H), ks_o = ksplit_for(n, H, QD), ks_gu = ksplit_for(n, 2 * I, H),

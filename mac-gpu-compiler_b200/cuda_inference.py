@@ -107,6 +107,7 @@ def lib() -> ctypes.CDLL:
             "qw_set_trace": (i32, [vp, i32]),
             "qw_read_trace": (i32, [vp, ctypes.POINTER(ctypes.c_uint64), sz]),
             "qw_gemv_bf16": (i32, [i32, vp, vp, vp, sz, sz, vp]),
+            "qw_gemv_bf16_seq": (i32, [i32, vp, vp, vp, sz, sz, sz, vp]),
             "qw_argmax_workspace_size": (sz, [sz]),
             "qw_argmax_f32": (i32, [i32, vp, sz, vp, vp, vp]),
             "qw_argmax_f32_noalloc": (i32, [i32, vp, sz, vp, vp]),
@@ -294,6 +295,11 @@ class CudaKVCache:
 # ---- standalone kernels ----------------------------------------------------------------------
 def gemv_bf16(device: int, d_w: int, d_x: int, d_y: int, rows: int, cols: int, stream: int = 0) -> None:
     _check(lib().qw_gemv_bf16(device, d_w, d_x, d_y, rows, cols, stream or None))
+
+
+def gemv_bf16_seq(device: int, d_w: int, d_x: int, d_y: int, rows: int, cols: int, count: int, stream: int = 0) -> None:
+    """y[m] = W[m] x for `count` back-to-back matrices in one launch (see qw_gemv_bf16_seq)."""
+    _check(lib().qw_gemv_bf16_seq(device, d_w, d_x, d_y, rows, cols, count, stream or None))
 
 
 def argmax_workspace_size(n: int) -> int:

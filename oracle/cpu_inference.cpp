@@ -21,6 +21,7 @@
 #include <cstdio>
 #include <cstring>
 #include <fcntl.h>
+#include <functional>
 #include <map>
 #include <memory>
 #include <stdexcept>
@@ -474,6 +475,132 @@ int oracle_forward(const OracleModel* m, OracleCache* cache, uint32_t token, siz
         g_err = e.what();
         return -1;
     }
+}
+
+// Model::forward (cpu_inference.rs:100-179) for n consecutive tokens at positions start_pos ..
+// start_pos + n - 1, computed layer by layer over all n positions instead of token by token. Every
+// value goes through the same functions in the same order as n calls of oracle_forward: a
+// position's projections are dot_bf16 of the same row and input, and its attention reads only
+// positions <= its own, whose K/V this layer has already appended. So the cache and the logits are
+// bit-identical to the token-by-token loop (tests/test_oracle.py checks this), while each weight row
+// is read once per block of positions rather than once per token: a 2048-token prompt on the
+// Qwen3-0.6B geometry takes seconds instead of minutes. That is the only reason it exists.
+// Logits are written for the positions listed in out_idx (indices into 0..n-1), row k of
+// logits_out for out_idx[k]; the cache must hold exactly start_pos positions.
+int oracle_forward_seq(const OracleModel* m, OracleCache* cache, const uint32_t* tokens, size_t n, size_t start_pos,
+                       const size_t* out_idx, size_t n_out, float* logits_out) {
+    try {
+        const Config& c = m->config;
+        const size_t H = c.hidden_size, I = c.intermediate_size, hd = c.head_dim;
+        const size_t q_dim = c.num_attention_heads * hd, kv_dim = c.num_key_value_heads * hd;
+        const size_t group = c.num_attention_heads / c.num_key_value_heads;
+        const float eps = c.rms_norm_eps;
+        if (oracle_cache_len(m, cache) != start_pos) throw std::runtime_error("cache length differs from start_pos");
+        for (size_t k = 0; k < n_out; k++)
+            if (out_idx[k] >= n) throw std::runtime_error("out_idx beyond n");
+        size_t embed_n = 0;
+        const uint16_t* embed = m->weight("model.embed_tokens.weight", &embed_n);
+        std::vector<float> x(n * H), xn(n * H), q(n * q_dim), kk(n * kv_dim), vv(n * kv_dim), att(n * q_dim),
+            proj(n * H), gate(n * I), up(n * I);
+        for (size_t t = 0; t < n; t++) {
+            const size_t row = (size_t)tokens[t] * H;
+            if (row + H > embed_n) throw std::runtime_error("token id out of range");
+            for (size_t i = 0; i < H; i++) x[t * H + i] = bf16_to_f32(embed[row + i]);
+        }
+        const size_t threads = g_threads > 0 ? (size_t)g_threads : std::max(1u, std::thread::hardware_concurrency());
+        // out[t][r] = dot_bf16(w row r, in[t]) for t < n: rows split over the threads, positions
+        // taken in blocks so a block's inputs stay cached while the thread walks its rows
+        auto seq_matvec = [&](float* out, size_t rows, const uint16_t* w, const float* in, size_t cols,
+                              const std::vector<size_t>* pick) {
+            const size_t np = pick ? pick->size() : n;
+            const size_t rows_per = (rows + threads - 1) / threads;
+            std::vector<std::thread> th;
+            for (size_t r0 = 0; r0 < rows; r0 += rows_per) {
+                const size_t r1 = std::min(rows, r0 + rows_per);
+                th.emplace_back([=] {
+                    for (size_t b0 = 0; b0 < np; b0 += 16) {
+                        const size_t b1 = std::min(np, b0 + 16);
+                        for (size_t r = r0; r < r1; r++)
+                            for (size_t b = b0; b < b1; b++) {
+                                const size_t t = pick ? (*pick)[b] : b;
+                                out[b * rows + r] = dot_bf16(w + r * cols, in + t * cols, cols);
+                            }
+                    }
+                });
+            }
+            for (auto& t : th) t.join();
+        };
+        auto parallel = [&](size_t count, const std::function<void(size_t)>& fn) {
+            std::vector<std::thread> th;
+            const size_t per = (count + threads - 1) / threads;
+            for (size_t a0 = 0; a0 < count; a0 += per) {
+                const size_t a1 = std::min(count, a0 + per);
+                th.emplace_back([=, &fn] { for (size_t a = a0; a < a1; a++) fn(a); });
+            }
+            for (auto& t : th) t.join();
+        };
+        const float scale = 1.0f / sqrtf((float)hd);
+        for (size_t l = 0; l < c.num_hidden_layers; l++) {
+            std::string p = "model.layers." + std::to_string(l) + ".";
+            auto w = [&](const char* nm) { return m->weight(p + nm); };
+            const uint16_t* ln1 = w("input_layernorm.weight");
+            for (size_t t = 0; t < n; t++) rmsnorm(&xn[t * H], &x[t * H], ln1, H, eps);
+            seq_matvec(q.data(), q_dim, w("self_attn.q_proj.weight"), xn.data(), H, nullptr);
+            seq_matvec(kk.data(), kv_dim, w("self_attn.k_proj.weight"), xn.data(), H, nullptr);
+            seq_matvec(vv.data(), kv_dim, w("self_attn.v_proj.weight"), xn.data(), H, nullptr);
+            const uint16_t* q_norm = w("self_attn.q_norm.weight");
+            const uint16_t* k_norm = w("self_attn.k_norm.weight");
+            for (size_t t = 0; t < n; t++) {
+                const size_t pos = start_pos + t;
+                for (size_t h = 0; h < q_dim; h += hd) { rmsnorm_inplace(&q[t * q_dim + h], q_norm, hd, eps); rope(&q[t * q_dim + h], hd, pos, c.rope_theta); }
+                for (size_t h = 0; h < kv_dim; h += hd) { rmsnorm_inplace(&kk[t * kv_dim + h], k_norm, hd, eps); rope(&kk[t * kv_dim + h], hd, pos, c.rope_theta); }
+                cache->k[l].insert(cache->k[l].end(), kk.begin() + t * kv_dim, kk.begin() + (t + 1) * kv_dim);
+                cache->v[l].insert(cache->v[l].end(), vv.begin() + t * kv_dim, vv.begin() + (t + 1) * kv_dim);
+            }
+            const std::vector<float>& kc = cache->k[l];
+            const std::vector<float>& vc = cache->v[l];
+            parallel(n * c.num_attention_heads, [&](size_t job) {
+                const size_t t = job / c.num_attention_heads, h = job % c.num_attention_heads;
+                const size_t pos = start_pos + t;
+                std::vector<float> scores(pos + 1);
+                const float* qh = &q[t * q_dim + h * hd];
+                const size_t kv_off = (h / group) * hd;
+                for (size_t s = 0; s <= pos; s++) scores[s] = dot(qh, &kc[s * kv_dim + kv_off], hd) * scale;
+                softmax(scores.data(), pos + 1);
+                float* o = &att[t * q_dim + h * hd];
+                std::fill(o, o + hd, 0.0f);
+                for (size_t s = 0; s <= pos; s++) {
+                    const float* vt = &vc[s * kv_dim + kv_off];
+                    for (size_t i = 0; i < hd; i++) o[i] += scores[s] * vt[i];
+                }
+            });
+            seq_matvec(proj.data(), H, w("self_attn.o_proj.weight"), att.data(), q_dim, nullptr);
+            for (size_t i = 0; i < n * H; i++) x[i] += proj[i];
+            const uint16_t* ln2 = w("post_attention_layernorm.weight");
+            for (size_t t = 0; t < n; t++) rmsnorm(&xn[t * H], &x[t * H], ln2, H, eps);
+            seq_matvec(gate.data(), I, w("mlp.gate_proj.weight"), xn.data(), H, nullptr);
+            seq_matvec(up.data(), I, w("mlp.up_proj.weight"), xn.data(), H, nullptr);
+            for (size_t i = 0; i < n * I; i++) gate[i] = silu(gate[i]) * up[i];
+            seq_matvec(proj.data(), H, w("mlp.down_proj.weight"), gate.data(), I, nullptr);
+            for (size_t i = 0; i < n * H; i++) x[i] += proj[i];
+        }
+        if (n_out) {
+            const uint16_t* fn = m->weight("model.norm.weight");
+            std::vector<size_t> pick(out_idx, out_idx + n_out);
+            for (size_t k = 0; k < n_out; k++) rmsnorm(&xn[pick[k] * H], &x[pick[k] * H], fn, H, eps);
+            seq_matvec(logits_out, c.vocab_size, m->weight("lm_head.weight"), xn.data(), H, &pick);
+        }
+        return 0;
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
+}
+
+// cpu_inference.rs:225-257  the reference's matvec on its own (bf16 weights [rows][cols], f32 x),
+// rows split over the host threads: the CPU side of the isolated GEMV microbenchmark
+void oracle_matvec(const uint16_t* w, const float* x, float* out, size_t rows, size_t cols) {
+    matvec(out, rows, w, x, cols);
 }
 
 // tests/common/mod.rs:17-22 (also bench.rs:99-104, main.rs:37-42): first strict maximum

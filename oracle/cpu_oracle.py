@@ -58,6 +58,10 @@ def lib():
         L.oracle_cache_fill.restype = ctypes.c_int
         L.oracle_forward.argtypes = [vp, vp, ctypes.c_uint32, sz, vp]
         L.oracle_forward.restype = ctypes.c_int
+        L.oracle_forward_seq.argtypes = [vp, vp, vp, sz, sz, vp, sz, vp]
+        L.oracle_forward_seq.restype = ctypes.c_int
+        L.oracle_matvec.argtypes = [vp, vp, vp, sz, sz]
+        L.oracle_matvec.restype = None
         L.oracle_argmax.argtypes = [vp, sz]
         L.oracle_argmax.restype = ctypes.c_uint32
         L.oracle_set_threads.argtypes = [ctypes.c_int]
@@ -137,6 +141,21 @@ class Model:
             raise RuntimeError(lib().oracle_last_error().decode())
         return out
 
+    def forward_seq(self, tokens, start_pos: int, cache: KVCache, out_positions=None) -> np.ndarray:
+        """``forward`` for consecutive tokens at positions start_pos.., computed layer by layer
+        over all of them; the cache and the logits are bit-identical to calling ``forward`` once per
+        token. Returns the logits of the positions in ``out_positions`` (indices into ``tokens``;
+        default: every position) as [len(out_positions)][vocab]."""
+        toks = np.ascontiguousarray(tokens, np.uint32)
+        idx = np.arange(toks.size) if out_positions is None else np.asarray(out_positions)
+        idx = np.ascontiguousarray(idx, np.uint64)
+        out = np.empty((idx.size, self.config.vocab_size), np.float32)
+        rc = lib().oracle_forward_seq(self._h, cache._h, toks.ctypes.data, toks.size, start_pos,
+                                      idx.ctypes.data, idx.size, out.ctypes.data)
+        if rc != 0:
+            raise RuntimeError(lib().oracle_last_error().decode())
+        return out
+
     def __del__(self):
         if getattr(self, "_h", None) and _lib is not None:
             _lib.oracle_free(self._h)
@@ -153,6 +172,17 @@ def top2_margin(x: np.ndarray) -> float:
     """Gap between the largest and second-largest logit (greedy-flip risk when below 1e-2)."""
     p = np.partition(np.asarray(x, np.float64), -2)[-2:]
     return float(p[1] - p[0])
+
+
+def matvec(w_bf16: np.ndarray, x: np.ndarray) -> np.ndarray:
+    """cpu_inference.rs:225-257: y = W x, W given as uint16 bf16 bit patterns [rows][cols]."""
+    w = np.ascontiguousarray(w_bf16, np.uint16)
+    xx = np.ascontiguousarray(x, np.float32)
+    rows, cols = w.shape
+    assert xx.size == cols
+    out = np.empty(rows, np.float32)
+    lib().oracle_matvec(w.ctypes.data, xx.ctypes.data, out.ctypes.data, rows, cols)
+    return out
 
 
 def set_threads(n: int) -> None:

@@ -1,6 +1,8 @@
 """The bench's reference arm (`bench.py --impl reference`) on the CPU: one JSON line on the product
-arm's metric, unit and direction, timing the CPU oracle, with the keys the bench contract names
-(cpu_baseline, e2e without host copies)."""
+arm's metric, unit, direction and config (the same `config` object the product arm prints, so the
+two lines describe the same workload), timing the CPU oracle the way the reference's own bench
+times its CPU engine, with the keys the bench contract names (cpu_baseline, e2e without host
+copies)."""
 from __future__ import annotations
 
 import json
@@ -8,22 +10,55 @@ import subprocess
 import sys
 from pathlib import Path
 
+import pytest
+
 ROOT = Path(__file__).resolve().parents[1]
-PRODUCT_METRIC = "Qwen3-0.6B bf16 decode tok/s @bs1 & % of HBM roofline; box tok/s at 1-8 GPUs"
+sys.path.insert(0, str(ROOT))
+
+import bench  # noqa: E402
 
 
-def test_reference_arm_prints_the_product_metric(full_model_path):
-    out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1", "--warmup", "1"],
-                         capture_output=True, text=True, timeout=600, cwd=ROOT)
+def _reference_line(*extra):
+    out = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "2", "--warmup", "1",
+                          *extra], capture_output=True, text=True, timeout=900, cwd=ROOT)
     assert out.returncode == 0, out.stderr[-2000:]
     lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
     assert len(lines) == 1, out.stdout
-    d = json.loads(lines[0])
+    return json.loads(lines[0])
+
+
+def _common(d, metric, unit):
     assert d["impl"] == "reference"
-    assert d["metric"] == PRODUCT_METRIC
-    assert d["unit"] == "tok/s" and d["higher_is_better"] is True
-    assert d["value"] > 0 and d["steps"] == 1 and d["warmup"] == 1
+    assert d["metric"] == metric
+    assert d["unit"] == unit and d["higher_is_better"] is True
+    assert d["value"] > 0 and d["steps"] == 2 and d["warmup"] == 1
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["value"] == d["value"]
     assert d["cpu_baseline"]["cores"] >= 1 and d["cpu_baseline"]["sample"]
-    assert d["e2e"] == {"value": d["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
-    assert d["config"]["workload"].startswith("configs[0]")
+    assert d["e2e"] == {"value": d["value"], "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_decode_line(full_model_path):
+    d = _reference_line()
+    _common(d, bench.DECODE_METRIC, "tok/s")
+    assert d["config"] == bench.workload_config("ai130", 1)
+    # timed like bench.rs: decode positions right after the real 130-id prompt
+    assert "positions 130.." in d["cpu_baseline"]["sample"]
+
+
+@pytest.mark.parametrize("cfg", ["prefill", "gemv"])
+def test_reference_arm_other_configs(cfg, full_model_path):
+    d = _reference_line("--config", cfg)
+    if cfg == "prefill":
+        _common(d, bench.PREFILL_METRIC, "tok/s")
+        assert "positions 0.." in d["cpu_baseline"]["sample"]
+    else:
+        _common(d, bench.GEMV_METRIC, "GB/s")
+        assert set(d["shapes"]) == set(bench.GEMV_SHAPES)
+    assert d["config"] == bench.workload_config(cfg, 1)
+
+
+def test_workload_config_is_engine_free():
+    for name in bench.CONFIGS:
+        c = bench.workload_config(name, 4)
+        assert c["workload"].startswith("configs[")
+        assert "engine" not in c and "impl" not in c

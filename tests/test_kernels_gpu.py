@@ -36,6 +36,25 @@ def test_gemv_matches_f64(rows, cols):
     assert err < 1e-4, err
 
 
+@pytest.mark.parametrize("rows,cols,count", [(2048, 1024, 9), (1024, 2048, 5), (1024, 3072, 3), (37, 768, 4)])
+def test_gemv_seq_matches_single_launches(rows, cols, count):
+    """qw_gemv_bf16_seq (count stacked matrices in one launch) gives, bit for bit, what one
+    qw_gemv_bf16 launch per matrix gives (same rows per CTA, same reduction order), and matches f64."""
+    g = torch.Generator().manual_seed(rows + 13 * cols + count)
+    w = (torch.randn(count, rows, cols, generator=g) * 0.02).to(torch.bfloat16)
+    x = torch.randn(cols, generator=g)
+    wd, xd = w.cuda(), x.cuda()
+    ys = torch.full((count, rows), float("nan"), device="cuda")
+    ci.gemv_bf16_seq(0, wd.data_ptr(), xd.data_ptr(), ys.data_ptr(), rows, cols, count)
+    y1 = torch.full((count, rows), float("nan"), device="cuda")
+    for m in range(count):
+        ci.gemv_bf16(0, wd[m].data_ptr(), xd.data_ptr(), y1[m].data_ptr(), rows, cols)
+    torch.cuda.synchronize()
+    assert torch.equal(ys, y1)
+    ref = torch.einsum("mrc,c->mr", w.double(), x.double())
+    assert (ys.cpu().double() - ref).abs().max().item() < 1e-4
+
+
 def _gpu_argmax(x: np.ndarray) -> int:
     xd = torch.from_numpy(x).cuda()
     out = torch.zeros(1, dtype=torch.int32, device="cuda")

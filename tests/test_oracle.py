@@ -77,3 +77,27 @@ def test_oracle_load_errors(tmp_path):
     (tmp_path / "config.json").write_text("{}")
     with pytest.raises(OSError):
         co.Model.load_model(bad)
+
+
+@pytest.mark.parametrize("geometry,n,start", [("tiny", 37, 0), ("tiny", 20, 9), ("mid", 6, 0)])
+def test_forward_seq_is_bit_identical_to_token_by_token(geometry, n, start, request):
+    """The layer-major multi-position forward (used to get long-prompt oracle references in
+    seconds) must reproduce the token-by-token loop exactly: logits and cache, bit for bit."""
+    path = request.getfixturevalue(f"{geometry}_model_path")
+    m = co.Model.load_model(path)
+    import randmodel
+    ids = randmodel.prompt_ids(start + n, m.config.vocab_size, seed=4)
+    c1, c2 = co.KVCache(m), co.KVCache(m)
+    want = [m.forward(t, p, c1) for p, t in enumerate(ids)]
+    if start:
+        m.forward_seq(ids[:start], 0, c2, out_positions=[])
+    pick = list(range(0, n, 3)) + [n - 1]
+    got = m.forward_seq(ids[start:], start, c2, out_positions=pick)
+    for row, i in enumerate(pick):
+        assert np.array_equal(got[row], want[start + i]), i
+    for l in range(m.config.num_hidden_layers):
+        k1, v1 = c1.layer(l)
+        k2, v2 = c2.layer(l)
+        assert np.array_equal(k1, k2) and np.array_equal(v1, v2)
+    with pytest.raises(RuntimeError):      # the cache must hold exactly start_pos positions
+        m.forward_seq(ids[:2], 3, c2)

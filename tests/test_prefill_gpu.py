@@ -88,3 +88,22 @@ def test_prefill_argument_errors(tiny_model_path):
     with pytest.raises(ci.QwError) as e:
         m.prefill([1, m.config.vocab_size], 0, cache)   # token id out of range
     assert e.value.code == ci.QW_ERR_ARG
+
+
+def test_prefill_device_bad_id_is_reported(tiny_model_path):
+    """qw_prefill_device reads its ids from device memory, which the host cannot check: an id >=
+    vocab_size is never used as an embedding row (row 0 is read instead) and the next qw_sync
+    reports QW_ERR_ARG; the handle keeps working afterwards."""
+    m = ci.CudaModel.load_model(tiny_model_path)
+    cache = ci.CudaKVCache(m, 16)
+    V = m.config.vocab_size
+    d_ids = torch.tensor([3, V + 7, 5, -1], dtype=torch.int32, device="cuda")   # -1: 0xFFFFFFFF as uint32
+    torch.cuda.synchronize()
+    m.prefill_device(cache, d_ids.data_ptr(), 4, 0)
+    with pytest.raises(ci.QwError) as e:
+        m.sync()
+    assert e.value.code == ci.QW_ERR_ARG
+    m.sync()                                                 # the report was cleared
+    ids = [3, 1, 5, 2]
+    lg = m.prefill(ids, 0, ci.CudaKVCache(m, 16))
+    assert np.isfinite(lg).all()
