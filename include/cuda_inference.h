@@ -166,6 +166,16 @@ int qw_cache_read(qw_cache* cache, size_t layer, size_t n, float* k_out, float* 
 /* Streaming-SM count the decode kernel uses (one CTA per SM). */
 int qw_num_ctas(const qw_model* model);
 
+/* Which decode kernel runs qw_forward / qw_decode for this model (no reference counterpart: the
+ * reference has one Metal pipeline per op). QW_DECODER_GRID, the default: one CTA per SM over the
+ * whole GPU, every shape. QW_DECODER_CLUSTER, when the environment sets QW_DECODER=cluster at
+ * load: 8 thread-block clusters of 8 CTAs, one per KV head, exchanging activations through
+ * distributed shared memory (the Qwen3-0.6B layer shape only). Both compute the same function
+ * (cpu_inference.rs:100-179). */
+#define QW_DECODER_GRID 0
+#define QW_DECODER_CLUSTER 1
+int qw_decoder_kind(const qw_model* model);
+
 /* The model's own cudaStream_t (what qw_forward/qw_decode run on), e.g. to bracket them with
  * events. */
 void* qw_model_stream(const qw_model* model);
@@ -211,7 +221,9 @@ int qw_argmax_f32(int device, const float* d_x, size_t n, uint32_t* d_out, void*
  * stream capture). n must be in [1, QW_ARGMAX_NOALLOC_MAX_N]; larger n returns QW_ERR_ARG. All
  * calls on a device share the array, which keeps the last call's contents (the call clears what
  * must start at zero itself): two calls that overlap on the GPU — on different streams, or from
- * different threads — race and give wrong results; keep them ordered on one stream. */
+ * different threads — race and give wrong results; keep them ordered on one stream. The looked-up
+ * address is kept for the life of the process: a cudaDeviceReset on that device invalidates it
+ * (and every handle of this library on the device), so do not reset a device this library uses. */
 #define QW_ARGMAX_NOALLOC_MAX_N 4294967295ull
 int qw_argmax_f32_noalloc(int device, const float* d_x, size_t n, uint32_t* d_out, void* stream);
 

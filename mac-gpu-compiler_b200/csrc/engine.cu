@@ -20,6 +20,7 @@
 #include <vector>
 
 #include "../../include/cuda_inference.h"
+#include "cluster_decode.cuh"
 #include "decode_kernel.cuh"
 #include "model_file.h"
 #include "prefill.h"
@@ -122,7 +123,11 @@ struct qw_model {
     uint64_t id = 0;  // unique per load, so a cache can tell its model from a later one at the same address
     int device = 0;
     cudaStream_t stream = nullptr;
-    int nctas = 0;
+    int nctas = 0;    // grid of the decode kernel in use
+    int kind = 0;     // QW_DECODER_GRID (decode_kernel.cuh) or QW_DECODER_CLUSTER (cluster_decode.cuh)
+    bool cl_coop = true;          // cluster launches also ask for co-residency (cooperative) until refused
+    uint16_t* d_clw = nullptr;    // cluster kernel: o_proj and down_proj repacked per (layer, cluster, rank)
+    u64 *d_po = nullptr, *d_pd = nullptr;  // cluster kernel: [8][hidden] partial residual updates (tagged words)
     ModelConfig cfg;
     uint64_t wbytes = 0;
     // weights
@@ -176,6 +181,7 @@ struct qw_model {
     long long timeout_ns = 0;
     int poll_ns = 0;
     int min_chunk = MIN_CHUNK;
+    int stall_cta = -1;          // QW_TEST_STALL_CTA: consumed by the next launch only (timeout test hook)
 };
 
 // A cache never dereferences its model after qw_cache_new: it keeps what it needs (device,
@@ -217,8 +223,94 @@ int ensure_token_capacity(qw_model* m, size_t n) {
     return QW_OK;
 }
 
+// The epoch of the next launch. Tagged hand-off words carry the low 12 bits of it, so a word left by
+// a launch 4096 launches earlier (e.g. a longer decode, whose later steps' words nothing has
+// overwritten since) could carry a tag that matches again: whenever those bits wrap, the tagged
+// buffers are cleared first (stream-ordered, before the launch).
+int next_epoch(qw_model* m, cudaStream_t s) {
+    const unsigned e = ++m->epoch;
+    if ((e & 0xFFFu) == 0 && e != 0) {
+        // the grid kernel's tagged buffers (x, q|k|v, att, h, attention partials) lead the scratch block
+        const size_t tagged_bytes = (size_t)(reinterpret_cast<uint8_t*>(m->d_am_val) - m->d_scratch);
+        QW_CUDA(cudaMemsetAsync(m->d_scratch, 0, tagged_bytes, s));
+        QW_CUDA(cudaMemsetAsync(m->d_po, 0, (size_t)cl::NKV * m->cfg.hidden * 8, s));
+        QW_CUDA(cudaMemsetAsync(m->d_pd, 0, (size_t)cl::NKV * m->cfg.hidden * 8, s));
+    }
+    return QW_OK;
+}
+
+// the cluster decode kernel (cluster_decode.cuh): 8 clusters of 16 CTAs, one per KV head
+int launch_cluster(qw_model* m, qw_cache* c, const uint32_t* tok_in, uint32_t* tok_out, bool stream_to_host,
+                   float* logits, size_t start_pos, size_t steps, cudaStream_t s) {
+    const ModelConfig& g = m->cfg;
+    cl::Params p{};
+    p.layer_w = m->d_layer_w;
+    p.o_blk = m->d_clw;
+    p.d_blk = m->d_clw + (size_t)g.layers * cl::NKV * cl::CL * cl::XO * cl::OK;
+    p.layer_n = m->d_layer_n;
+    p.final_norm = m->d_final_norm;
+    p.embed = m->d_embed;
+    p.lm_head = m->d_lm_head;
+    p.kc = c->d_k;
+    p.vc = c->d_v;
+    p.rope = c->d_rope;
+    p.po = m->d_po;
+    p.pd = m->d_pd;
+    p.am_val = m->d_am_val;
+    p.am_idx = m->d_am_idx;
+    p.nan0 = m->d_nan0;
+    p.flags = m->d_flags;
+    p.err = m->d_err;
+    p.logits = logits;
+    p.trace = m->d_trace;
+    p.tok_in = tok_in;
+    p.tok_out = tok_out;
+    p.host_tok = stream_to_host ? m->h_tok_dev : nullptr;
+    p.host_count = stream_to_host ? m->h_count_dev : nullptr;
+    p.layer_stride = m->layer_stride;
+    p.norm_stride = m->norm_stride;
+    p.L = (int)g.layers;
+    p.V = (int)g.vocab;
+    p.max_seq = (int)c->max_seq;
+    p.start_pos = (int)start_pos;
+    p.steps = (int)steps;
+    p.eps = g.eps;
+    p.scale = 1.0f / sqrtf((float)g.head_dim);  // cpu_inference.rs:144
+    p.timeout_ns = m->timeout_ns;
+    p.stall_cta = m->stall_cta;
+    m->stall_cta = -1;
+    if (int e = next_epoch(m, s)) return e;
+    p.epoch = m->epoch;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(m->nctas);
+    cfg.blockDim = dim3(cl::NTHREADS);
+    cfg.dynamicSmemBytes = cl::DYN_BYTES;
+    cfg.stream = s;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = cl::CL;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeCooperative;
+    at[1].val.cooperative = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = m->cl_coop ? 2 : 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, cl::cluster_decode_kernel, p);
+    if (e != cudaSuccess && m->cl_coop) {
+        // a driver that does not combine cooperative and cluster launches: the load-time occupancy
+        // check (every cluster fits at once on an otherwise idle GPU) stands in for it
+        (void)cudaGetLastError();
+        m->cl_coop = false;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, cl::cluster_decode_kernel, p);
+    }
+    if (e != cudaSuccess) return cuda_err(e, "cluster decode kernel launch");
+    return QW_OK;
+}
+
 int launch_decode(qw_model* m, qw_cache* c, const uint32_t* tok_in, uint32_t* tok_out, bool stream_to_host,
                   float* logits, size_t start_pos, size_t steps, cudaStream_t s) {
+    if (m->kind == QW_DECODER_CLUSTER) return launch_cluster(m, c, tok_in, tok_out, stream_to_host, logits, start_pos, steps, s);
     const ModelConfig& g = m->cfg;
     DecodeParams p{};
     p.layer_w = m->d_layer_w;
@@ -256,7 +348,8 @@ int launch_decode(qw_model* m, qw_cache* c, const uint32_t* tok_in, uint32_t* to
     p.max_seq = (int)c->max_seq;
     p.start_pos = (int)start_pos;
     p.steps = (int)steps;
-    p.epoch = ++m->epoch;
+    if (int e = next_epoch(m, s)) return e;
+    p.epoch = m->epoch;
     p.eps = g.eps;
     p.scale = 1.0f / sqrtf((float)g.head_dim);  // cpu_inference.rs:144
     p.S = m->S;
@@ -266,6 +359,8 @@ int launch_decode(qw_model* m, qw_cache* c, const uint32_t* tok_in, uint32_t* to
     p.timeout_ns = m->timeout_ns;
     p.poll_ns = m->poll_ns;
     p.min_chunk = m->min_chunk;
+    p.stall_cta = m->stall_cta;
+    m->stall_cta = -1;
     void* args[] = {&p};
     cudaError_t e = cudaLaunchCooperativeKernel((const void*)decode_kernel, dim3(m->nctas), dim3(NTHREADS), args,
                                                 m->dyn_smem, s);
@@ -286,6 +381,34 @@ int check_device_err(qw_model* m) {
 }
 
 cudaStream_t pick_stream(qw_model* m, void* s) { return s ? static_cast<cudaStream_t>(s) : m->stream; }
+
+// whether NKV clusters of 16 CTAs of the cluster kernel can be resident at once (`fit`: how many)
+bool cluster_kernel_fits(int& fit) {
+    fit = 0;
+    if (cudaFuncSetAttribute(cl::cluster_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cl::DYN_BYTES) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(cl::cluster_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return false;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(cl::NKV * cl::CL);
+    cfg.blockDim = dim3(cl::NTHREADS);
+    cfg.dynamicSmemBytes = cl::DYN_BYTES;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = cl::CL;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&fit, cl::cluster_decode_kernel, &cfg) != cudaSuccess) {
+        (void)cudaGetLastError();
+        fit = 0;
+        return false;
+    }
+    return fit >= cl::NKV;
+}
 
 }  // namespace
 
@@ -331,6 +454,8 @@ int qw_load(const char* path, int device, qw_model** out) {
     m->timeout_ns = timeout_ns_from_env();
     if (const char* e = std::getenv("QW_POLL_NS")) m->poll_ns = std::max(0, std::min(10000, std::atoi(e)));
     if (const char* e = std::getenv("QW_MIN_CHUNK")) m->min_chunk = std::max(1, std::min(1 << 20, std::atoi(e)));
+    // test hook: the first launch of this model has CTA QW_TEST_STALL_CTA skip its end-of-token flag
+    if (const char* e = std::getenv("QW_TEST_STALL_CTA")) m->stall_cta = std::atoi(e);
     int nctas = prop.multiProcessorCount;
     if (const char* e = std::getenv("QW_CTAS")) nctas = std::max(1, std::min(nctas, std::atoi(e)));
     // Buffers are reused across phases on the premise that a phase's input is complete only after
@@ -405,6 +530,52 @@ int qw_load(const char* path, int device, qw_model** out) {
             return fail(QW_ERR_CUDA, "weight upload failed");
     }
 
+    // The single-grid kernel (decode_kernel.cuh) runs every shape and is the default: on B200 one SM
+    // takes in weights at only ~40 GB/s, so reaching HBM bandwidth needs every SM streaming.
+    // QW_DECODER=cluster selects the cluster kernel (cluster_decode.cuh: 8 clusters of 8 CTAs, one per
+    // KV head, activations exchanged through distributed shared memory) for the Qwen3-0.6B layer
+    // shape; it streams on 64 SMs only, which bounds it below the grid kernel here.
+    {
+        const bool shape = H == (uint64_t)cl::H && I == (uint64_t)cl::I && c.heads == (uint64_t)cl::NQ &&
+                           c.kv_heads == (uint64_t)cl::NKV && c.head_dim == (uint64_t)cl::HD;
+        const char* dec = std::getenv("QW_DECODER");
+        if (dec && std::strcmp(dec, "cluster") == 0) {
+            if (!shape || std::getenv("QW_CTAS"))
+                return fail(QW_ERR_UNSUPPORTED, "QW_DECODER=cluster: the cluster kernel needs the Qwen3-0.6B layer "
+                                                "shape and no QW_CTAS");
+            int fit = 0;
+            if (!cluster_kernel_fits(fit))
+                return fail(QW_ERR_UNSUPPORTED, "QW_DECODER=cluster: " + std::to_string(fit) + " clusters of " +
+                                                    std::to_string(cl::CL) + " CTAs fit at once, " +
+                                                    std::to_string(cl::NKV) + " are needed");
+            m->kind = QW_DECODER_CLUSTER;
+            m->nctas = cl::NKV * cl::CL;
+        }
+    }
+    if (m->kind == QW_DECODER_CLUSTER) {
+        // o_proj and down_proj once more, as the contiguous block of each (layer, cluster g, rank r):
+        // rows [64r, 64r+64) over o's columns [256g, +256) and down's columns [384g, +384)
+        const size_t per_o = (size_t)cl::NKV * cl::CL * cl::XO * cl::OK, per_d = (size_t)cl::NKV * cl::CL * cl::XO * cl::DK;
+        if (cudaMalloc(&m->d_clw, (per_o + per_d) * c.layers * 2) != cudaSuccess)
+            return fail(QW_ERR_NOMEM, "cluster weight allocation failed");
+        std::vector<uint16_t> ob(per_o), db(per_d);
+        for (uint64_t l = 0; l < c.layers; l++) {
+            const std::string pre = "model.layers." + std::to_string(l) + ".";
+            const uint16_t* o = reinterpret_cast<const uint16_t*>(f.data(pre + "self_attn.o_proj.weight"));
+            const uint16_t* d = reinterpret_cast<const uint16_t*>(f.data(pre + "mlp.down_proj.weight"));
+            for (int g = 0; g < cl::NKV; g++)
+                for (int r = 0; r < cl::CL; r++)
+                    for (int i = 0; i < cl::XO; i++) {
+                        const size_t row = (size_t)cl::XO * r + i, blk = ((size_t)g * cl::CL + r) * cl::XO + i;
+                        std::memcpy(&ob[blk * cl::OK], o + row * QD + (size_t)cl::OK * g, cl::OK * 2);
+                        std::memcpy(&db[blk * cl::DK], d + row * I + (size_t)cl::DK * g, cl::DK * 2);
+                    }
+            if (cudaMemcpy(m->d_clw + l * per_o, ob.data(), per_o * 2, cudaMemcpyHostToDevice) != cudaSuccess ||
+                cudaMemcpy(m->d_clw + c.layers * per_o + l * per_d, db.data(), per_d * 2, cudaMemcpyHostToDevice) != cudaSuccess)
+                return fail(QW_ERR_CUDA, "cluster weight upload failed");
+        }
+    }
+
     // scratch
     const int G = (int)(c.heads / c.kv_heads);
     auto ceil_div = [](uint64_t a, uint64_t b) { return (a + b - 1) / b; };
@@ -435,7 +606,8 @@ int qw_load(const char* path, int device, qw_model** out) {
         {H * 8, (void**)&m->d_x}, {QKVR * 8, (void**)&m->d_qkv}, {QD * 8, (void**)&m->d_att},
         {I * 8, (void**)&m->d_h}, {sz_apart, (void**)&m->d_apart},
         {(size_t)nctas * 4, (void**)&m->d_am_val}, {(size_t)nctas * 4, (void**)&m->d_am_idx}, {16, (void**)&m->d_nan0},
-        {(size_t)nctas * 8, (void**)&m->d_flags}, {16, (void**)&m->d_err}, {c.vocab * 4, (void**)&m->d_logits}};
+        {(size_t)nctas * 8, (void**)&m->d_flags}, {16, (void**)&m->d_err}, {c.vocab * 4, (void**)&m->d_logits},
+        {(size_t)cl::NKV * H * 8, (void**)&m->d_po}, {(size_t)cl::NKV * H * 8, (void**)&m->d_pd}};
     size_t scratch = 0;
     for (auto& pc2 : pieces) scratch += align_up(pc2.bytes, 256);
     if (cudaMalloc(&m->d_scratch, scratch) != cudaSuccess) return fail(QW_ERR_NOMEM, "scratch allocation failed");
@@ -459,6 +631,7 @@ void qw_free(qw_model* m) {
     cudaSetDevice(m->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
     cudaFree(m->d_weights);
+    cudaFree(m->d_clw);
     cudaFree(m->d_scratch);
     cudaFree(m->d_tok);
     cudaFree(m->d_trace);
@@ -494,6 +667,8 @@ int qw_config_get(const qw_model* m, qw_config* out) {
 uint64_t qw_weight_bytes_per_token(const qw_model* m) { return m ? m->wbytes : 0; }
 
 int qw_num_ctas(const qw_model* m) { return m ? m->nctas : 0; }
+
+int qw_decoder_kind(const qw_model* m) { return m ? m->kind : -1; }
 
 void* qw_model_stream(const qw_model* m) { return m ? static_cast<void*>(m->stream) : nullptr; }
 

@@ -205,6 +205,7 @@ int qw_gemv_bf16_seq(int device, const uint16_t* d_w, const float* d_x, float* d
     const size_t rows_per = (rows + n - 1) / n;
     DecodeParams p{};
     p.err = err;
+    p.stall_cta = -1;
     p.H = (int)cols;
     p.I = 256;
     p.L = 1;

@@ -102,6 +102,7 @@ def lib() -> ctypes.CDLL:
             "qw_sync": (i32, [vp, vp]),
             "qw_cache_read": (i32, [vp, sz, sz, vp, vp]),
             "qw_num_ctas": (i32, [vp]),
+            "qw_decoder_kind": (i32, [vp]),
             "qw_model_stream": (vp, [vp]),
             "qw_trace_stride": (sz, [vp]),
             "qw_set_trace": (i32, [vp, i32]),
@@ -157,6 +158,11 @@ class CudaModel:
     @property
     def num_ctas(self) -> int:
         return int(lib().qw_num_ctas(self._h))
+
+    @property
+    def decoder_kind(self) -> str:
+        """'grid' (one CTA per SM, the default) or 'cluster' (8 clusters of 8 CTAs, QW_DECODER=cluster)."""
+        return {0: "grid", 1: "cluster"}.get(int(lib().qw_decoder_kind(self._h)), "?")
 
     @property
     def stream(self) -> int:

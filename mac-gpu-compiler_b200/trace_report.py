@@ -20,7 +20,18 @@ import cuda_inference as ci  # noqa: E402
 import randmodel  # noqa: E402
 
 TPL = 14
-INTERVALS = [  # (name, from stamp, to stamp)
+# the cluster kernel's stamps per layer (cluster_decode.cuh): 0 layer start, 1 x*ln1 in hand, 2 q|k|v
+# of the head group in hand, 3 q/k norm + RoPE done, 4 this CTA's attention partial ready,
+# 5 all 16 partials in hand, 6 attention merged, 7 o_proj rows published, 8 x*ln2 in hand,
+# 9 the cluster's h in hand, 10 down rows published, 11 residual updated and the next x pushed
+CLUSTER_INTERVALS = [
+    ("E1 wait (x*ln1 from the residual exchange)", 0, 1), ("A q|k|v GEMV + push + E2 wait", 1, 2),
+    ("B q/k norm + RoPE (+ K/V append)", 2, 3), ("B attention over own positions", 3, 4),
+    ("B partials push + E3 wait", 4, 5), ("B merge 16 partials", 5, 6), ("C o_proj rows + publish", 6, 7),
+    ("G1 residual poll + E4 push + wait", 7, 8), ("D gate|up + SiLU + E5 push + wait", 8, 9),
+    ("E down rows + publish", 9, 10), ("G2 residual poll + E1 push", 10, 11),
+]
+INTERVALS = [  # (name, from stamp, to stamp) of the grid kernel (decode_kernel.cuh)
     ("A input (gather x + rmsnorm)", 0, 1), ("A q|k|v GEMV + store", 1, 2),
     ("B wait q/k/v + norm/RoPE", 2, 3), ("B attention chunk", 3, 4), ("B merge / publish", 4, 5),
     ("C input (gather att)", 5, 6), ("C o GEMV + residual", 6, 7),
@@ -49,7 +60,8 @@ def main() -> None:
     t0 = tr[:, 0].min()
     rel = tr - t0
     rows = []
-    for name, i, j in INTERVALS:
+    kind = model.decoder_kind
+    for name, i, j in (CLUSTER_INTERVALS if kind == "cluster" else INTERVALS):
         vals = []
         for l in range(L):
             d = rel[:, l * TPL + j] - rel[:, l * TPL + i]
@@ -61,7 +73,7 @@ def main() -> None:
     layer_span = [(rel[:, l * TPL + 11].max() - (rel[:, l * TPL + 0].min())) / 1e3 for l in range(L)]
     tail = L * TPL
     out = {
-        "geometry": a.geometry, "pos": a.pos, "ctas": int(tr.shape[0]),
+        "geometry": a.geometry, "pos": a.pos, "ctas": int(tr.shape[0]), "decoder": kind,
         "token_span_us": float(rel[:, tail + 3].max()) / 1e3,
         "layers_span_us": float(rel[:, (L - 1) * TPL + 11].max()) / 1e3,
         "layer_span_us_median": float(np.median(layer_span)),
@@ -73,7 +85,7 @@ def main() -> None:
     if a.json:
         print(json.dumps(out))
         return
-    print(f"{a.geometry} pos {a.pos}: token span {out['token_span_us']:.1f} us over {out['ctas']} CTAs; "
+    print(f"{a.geometry} pos {a.pos} ({kind} decoder): token span {out['token_span_us']:.1f} us over {out['ctas']} CTAs; "
           f"layers {out['layers_span_us']:.1f} us (median layer {out['layer_span_us_median']:.2f} us); "
           f"lm_head {out['lm_head_us']:.1f} us; end barrier {out['barrier_us']:.2f} us")
     for r in rows:

@@ -185,3 +185,79 @@ def test_device_token_out_of_range_is_reported(tiny_model_path):
         gpu.sync()
     assert e.value.code == ci.QW_ERR_ARG
     assert np.isfinite(gpu.forward(1, 0, cache)).all()     # recovered
+
+
+def test_decoder_selection(full_model_path, mid_model_path, tiny_model_path, monkeypatch):
+    """The grid kernel (one CTA per SM) is the default for every shape; QW_DECODER=cluster selects
+    the cluster kernel (8 clusters x 8 CTAs) for the Qwen3-0.6B layer shape and is refused for others."""
+    for path in (full_model_path, mid_model_path, tiny_model_path):
+        m = ci.CudaModel.load_model(path)
+        assert m.decoder_kind == "grid"
+        m.close()
+    monkeypatch.setenv("QW_DECODER", "cluster")
+    for path in (full_model_path, mid_model_path):
+        m = ci.CudaModel.load_model(path)
+        assert m.decoder_kind == "cluster" and m.num_ctas == 64
+        m.close()
+    with pytest.raises(ci.QwError) as e:
+        ci.CudaModel.load_model(tiny_model_path)
+    assert e.value.code == ci.QW_ERR_UNSUPPORTED
+
+
+def test_cluster_and_grid_kernels_agree(mid_model_path, monkeypatch):
+    """The two decode kernels compute the same function with different summation orders: their
+    logits agree far inside the oracle bar, and their greedy decodes give the same tokens."""
+    gr = ci.CudaModel.load_model(mid_model_path)
+    monkeypatch.setenv("QW_DECODER", "cluster")
+    cl = ci.CudaModel.load_model(mid_model_path)
+    assert (cl.decoder_kind, gr.decoder_kind) == ("cluster", "grid")
+    ids = randmodel.prompt_ids(40, cl.config.vocab_size, seed=21)
+    c1, c2 = ci.CudaKVCache(cl, 80), ci.CudaKVCache(gr, 80)
+    worst = 0.0
+    for pos, tok in enumerate(ids):
+        a, b = cl.forward(tok, pos, c1), gr.forward(tok, pos, c2)
+        worst = max(worst, float(np.abs(a - b).max()))
+    assert worst < 1e-3, worst
+    first = co.argmax(a)
+    assert cl.decode(first, len(ids), 24, c1) == gr.decode(first, len(ids), 24, c2)
+    print(f"cluster vs grid: max |diff| = {worst:.2e}")
+
+
+def test_cluster_kernel_device_token_out_of_range(mid_model_path, monkeypatch):
+    monkeypatch.setenv("QW_DECODER", "cluster")
+    gpu = ci.CudaModel.load_model(mid_model_path)
+    assert gpu.decoder_kind == "cluster"
+    import torch
+    cache = ci.CudaKVCache(gpu, 8)
+    toks = torch.tensor([gpu.config.vocab_size + 5, 0, 0], dtype=torch.int32, device="cuda")
+    torch.cuda.synchronize()
+    gpu.decode_device(cache, toks.data_ptr(), 0, 2)
+    with pytest.raises(ci.QwError) as e:
+        gpu.sync()
+    assert e.value.code == ci.QW_ERR_ARG
+    assert np.isfinite(gpu.forward(1, 0, cache)).all()     # recovered
+
+
+@pytest.mark.parametrize("geometry,kind", [("mid", "cluster"), ("tiny", "grid")])
+def test_expired_wait_is_reported_and_the_handle_recovers(geometry, kind, monkeypatch):
+    """A bounded device wait that runs out: with the test hook QW_TEST_STALL_CTA one CTA never raises
+    its first end-of-token flag, so every CTA's barrier wait expires (QW_WAIT_TIMEOUT_MS at its 50 ms
+    floor). The launch must end on its own and report QW_ERR_DEVICE_TIMEOUT; the next calls on the
+    same handle must give the same logits as a model that never stalled."""
+    path = randmodel.make_model(geometry, 0)
+    if kind == "cluster":
+        monkeypatch.setenv("QW_DECODER", "cluster")
+    ref = ci.CudaModel.load_model(path)
+    monkeypatch.setenv("QW_TEST_STALL_CTA", "5")
+    monkeypatch.setenv("QW_WAIT_TIMEOUT_MS", "50")
+    gpu = ci.CudaModel.load_model(path)
+    assert gpu.decoder_kind == kind
+    cache = ci.CudaKVCache(gpu, 16)
+    with pytest.raises(ci.QwError) as e:
+        gpu.forward(3, 0, cache)
+    assert e.value.code == ci.QW_ERR_DEVICE_TIMEOUT
+    rc = ci.CudaKVCache(ref, 16)
+    for pos, tok in enumerate([3, 7, 11]):
+        a, b = gpu.forward(tok, pos, cache), ref.forward(tok, pos, rc)
+        assert np.array_equal(a, b), pos
+    assert gpu.decode(5, 3, 4, cache) == ref.decode(5, 3, 4, rc)

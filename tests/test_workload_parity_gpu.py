@@ -76,14 +76,31 @@ def _agree_until_low_margin(got, want, logits):
     return len(want)
 
 
-def test_decode_workload_130_plus_128_every_position(models):
-    cpu, gpu = models
+@pytest.fixture(scope="module")
+def ref130(models):
+    """The oracle's side of the 130 + 128 workload, computed once for both decode kernels."""
+    cpu, _ = models
     n_prompt, n_dec = 130, 128
     ids = randmodel.prompt_ids(n_prompt, cpu.config.vocab_size, seed=1)
     oc = co.KVCache(cpu)
     want_prompt = cpu.forward_seq(ids, 0, oc)
     first = co.argmax(want_prompt[-1])
     want_toks, want_dec = _oracle_chain(cpu, oc, first, n_prompt, n_dec)
+    last = cpu.config.num_hidden_layers - 1
+    return dict(ids=ids, want_prompt=want_prompt, first=first, want_toks=want_toks, want_dec=want_dec,
+                kv={l: oc.layer(l) for l in (0, last)})
+
+
+@pytest.mark.parametrize("decoder", ["grid", "cluster"])
+def test_decode_workload_130_plus_128_every_position(models, ref130, decoder, full_model_path, monkeypatch):
+    cpu, gpu = models
+    if decoder == "cluster":
+        monkeypatch.setenv("QW_DECODER", "cluster")
+        gpu = ci.CudaModel.load_model(full_model_path)
+    assert gpu.decoder_kind == decoder
+    ids, first = ref130["ids"], ref130["first"]
+    want_prompt, want_toks, want_dec = ref130["want_prompt"], ref130["want_toks"], ref130["want_dec"]
+    n_prompt, n_dec = len(ids), len(want_toks)
 
     # teacher-forced: the GPU is fed the oracle's tokens, logits compared at all 258 positions
     gc = ci.CudaKVCache(gpu, n_prompt + n_dec + 1)
@@ -94,9 +111,8 @@ def test_decode_workload_130_plus_128_every_position(models):
     for i, tok in enumerate(fed):
         worst = max(worst, _check(n_prompt + i, want_dec[i], gpu.forward(tok, n_prompt + i, gc), "decode"))
     # KV cache of the whole sequence against the oracle's (first and last layer)
-    for l in (0, cpu.config.num_hidden_layers - 1):
+    for l, (ko, vo) in ref130["kv"].items():
         kg, vg = gc.layer(l, n_prompt + n_dec)
-        ko, vo = oc.layer(l)
         assert np.abs(kg - ko).max() < KV_TOL and np.abs(vg - vo).max() < KV_TOL, l
 
     # free-running: one qw_decode launch of 128 steps from a forward-filled prompt cache
@@ -105,7 +121,7 @@ def test_decode_workload_130_plus_128_every_position(models):
         gpu.forward(tok, pos, fc)
     got = gpu.decode(first, n_prompt, n_dec, fc)
     agreed = _agree_until_low_margin(got, want_toks, want_dec)
-    print(f"130+128: max |cpu - gpu| = {worst:.3e} over 258 positions; decode agrees for {agreed} steps")
+    print(f"130+128 ({decoder}): max |cpu - gpu| = {worst:.3e} over 258 positions; decode agrees for {agreed} steps")
 
 
 def test_long_context_2048_plus_32(models):
