@@ -30,8 +30,10 @@
 // After the layers: lm_head rows [V*c/64, V*(c+1)/64) of CTA c, per-CTA argmax partials, one
 // grid barrier per token, and every CTA combines the partials into the next token.
 //
-// Weights stream through a 7-slot shared-memory ring filled by one producer lane with 1-D TMA bulk
+// Weights stream through an 8-slot shared-memory ring filled by one producer lane with 1-D TMA bulk
 // copies (no multicast); the next layer's rows of each CTA are warmed into L2 at the start of a layer.
+// Each CTA moves 480 KB per layer through its 192 KB ring, so the GEMVs release every ring piece as
+// soon as its data is in registers: the producer refills the ring while the phase still computes.
 // Every wait is bounded in time; on expiry the kernel records an error and stops waiting. A CTA
 // leaves only after a cluster barrier, so no peer can still be writing into its shared memory.
 #pragma once
@@ -49,7 +51,7 @@ constexpr int CL = 8;                           // CTAs per cluster
 constexpr int NCW = 12;                         // consumer warps
 constexpr int NCT = NCW * 32;
 constexpr int NTHREADS = NCT + 32;              // + producer warp
-constexpr int NSLOT = 7;
+constexpr int NSLOT = 8;
 constexpr int SLOT_BYTES = 24 * 1024;
 constexpr int HD = 128, H = 1024, NQ = 16, NKV = 8, G = 2, I = 3072;
 constexpr int QD = NQ * HD, KVD = NKV * HD, QKVR = QD + 2 * KVD;
@@ -130,18 +132,28 @@ struct Smem {
     __align__(16) float gst[NKV][XO];  // polled partial residual updates, by cluster
 };
 
-// dynamic shared memory: ring | exchange targets (written by peers) | local scratch
+// dynamic shared memory: ring | exchange targets (written by peers) | local scratch.
+// The attention's per-warp softmax states (wst) overlay xsA, xsD, qkv, hs and att: while a CTA
+// combines its warps' states, it has finished reading xsA (phase A) and qkv (q/k norm + RoPE), has
+// not yet written att (the merge comes after), and no peer can push into xsA, xsD or hs yet (each
+// of those pushes needs this CTA's o_proj or gate|up outputs first, which come later).
 struct Dyn {
     uint8_t ring[NSLOT][SLOT_BYTES];
-    float xsA[H];                      // x * ln1 (or final norm) in the GEMV's permuted layout (E1)
-    float xsD[H];                      // x * ln2 (E4)
+    union {
+        struct {
+            float xsA[H];              // x * ln1 (or final norm) in the GEMV's permuted layout (E1)
+            float xsD[H];              // x * ln2 (E4)
+            float qkv[G * HD + 2 * HD];  // q0 | q1 | k | v of the head group (E2)
+            float hs[DK];              // the cluster's 384 SiLU(gate)*up values (E5)
+            float att[OK];             // merged attention output of the head group
+        };
+        float wst[NCW][G][WST];        // per-warp softmax states (local, see above)
+    };
     float ssA[CL], ssD[CL];            // the CL senders' sums of squares of x
-    float qkv[G * HD + 2 * HD];        // q0 | q1 | k | v of the head group (E2)
     float apr[CL][APW];                // attention partials by sender (E3)
-    float hs[DK];                      // the cluster's 384 SiLU(gate)*up values (E5)
-    float att[OK];                     // merged attention output of the head group
-    float wst[NCW][G][WST];            // per-warp softmax states (local)
 };
+static_assert(sizeof(float) * (2 * H + (G + 2) * HD + DK + OK) >= sizeof(float) * NCW * G * WST,
+              "the softmax states fit in the buffers they overlay");
 
 constexpr size_t DYN_BYTES = sizeof(Dyn);
 static_assert(offsetof(Dyn, xsA) % 16 == 0 && offsetof(Dyn, qkv) % 16 == 0 && offsetof(Dyn, apr) % 16 == 0 &&
@@ -303,7 +315,6 @@ public:
             }
         }
         const int npieces = (rows + 11) / 12;
-        const bool release_here = npieces > NSLOT;
         float bv = -INFINITY;
         unsigned bi = NONE_IDX;
         uint32_t pc = it;
@@ -336,11 +347,11 @@ public:
                     }
                 }
             }
-            if (release_here) {
-                __syncwarp();
-                if (ln == 0 && ok)
-                    for (int j = 0; j < n; j++) mbar_arrive(&cl_sm.empty[(pc + j) % NSLOT]);
-            }
+            // the group's data is in registers: hand its slots back to the producer now (every warp
+            // arrives on every slot of the group; a slot is released only after its data landed)
+            __syncwarp();
+            if (ln == 0 && ok)
+                for (int j = 0; j < n; j++) mbar_arrive(&cl_sm.empty[(pc + j) % NSLOT]);
             pc += n;
             const bool hi16 = ln & 16, hi8 = ln & 8;
             float k0 = hi16 ? v[2] : v[0], k1 = hi16 ? v[3] : v[1];
@@ -386,10 +397,6 @@ public:
             if (ln == 0) { cl_sm.redv[w] = bv; cl_sm.redi[w] = bi; }
         }
         named_bar_sync(1, NCT);
-        // a phase whose pieces all fit in the ring releases them once, after its closing barrier, one
-        // lane per slot standing in for all 12 warps
-        if (!release_here && warp() == 0 && lane() < npieces && !aborted())
-            mbar_arrive_cnt(&cl_sm.empty[(pc - npieces + lane()) % NSLOT], NCW);
     }
 
     // ------------------------------------------------------------------ GEMV over 4-row units, K = 256 / 384
@@ -418,6 +425,7 @@ public:
         }
         const int npieces = (units + UPP - 1) / UPP;
         const uint32_t pc = it;
+        int released = 0;  // lane 0: pieces [0, released) this warp has handed back to the producer
         for (int u = w; u < units; u += NCW) {
             const int pj = u / UPP;
             const bool ok = wait_mbar(&cl_sm.full[(pc + pj) % NSLOT], ((pc + pj) / NSLOT) & 1, DERR_TIMEOUT_FULL);
@@ -427,6 +435,11 @@ public:
                 uint4 wv[NL];
 #pragma unroll
                 for (int i = 0; i < NL; i++) wv[i] = wp[i * 32];
+                // release every piece this warp has no further unit in (its data is in registers)
+                const int done = u + NCW < units ? (u + NCW) / UPP : npieces;
+                __syncwarp();
+                if (ln == 0)
+                    for (; released < done; released++) mbar_arrive(&cl_sm.empty[(pc + released) % NSLOT]);
                 if (K == 256) {
 #pragma unroll
                     for (int i = 0; i < 4; i++) acc[i] = dot8(wv[i], xa);
@@ -450,9 +463,12 @@ public:
             const int jj = (hi16 ? 2 : 0) + (hi8 ? 1 : 0);
             if ((ln & 7) == 0 && ok) st_relaxed_u64(out + 4 * u + jj, tagged(t, tg));
         }
+        // pieces this warp read nothing from (after an expired wait: none, the slot stays taken)
+        __syncwarp();
+        if (ln == 0 && !aborted())
+            for (; released < npieces; released++) mbar_arrive(&cl_sm.empty[(pc + released) % NSLOT]);
         it = pc + npieces;
         named_bar_sync(1, NCT);
-        if (warp() == 0 && lane() < npieces && !aborted()) mbar_arrive_cnt(&cl_sm.empty[(pc + lane()) % NSLOT], NCW);
     }
 
     // ------------------------------------------------------------------ the residual hand-off (G1, G2)

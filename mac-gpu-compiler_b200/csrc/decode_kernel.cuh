@@ -1321,20 +1321,6 @@ public:
         }
     }
 
-    // warm L2 with the cached K/V rows this CTA's attention item reads in layer l for a token at
-    // `pos` (one contiguous range per K and V: the cache is [layer][kv head][position][128])
-    __device__ __noinline__ static void prefetch_kv(int l, int pos) {
-        const DecodeParams& p = qw_sm.prm;
-        const AttnItem a = attn_item(p, cta(), pos);
-        if (!a.active) return;
-        const int tc1 = a.has_cur ? pos : a.t1;
-        if (tc1 <= a.t0) return;
-        const size_t row = (((size_t)l * p.NKV + a.g) * p.max_seq + a.t0) * HD;
-        const uint32_t bytes = (uint32_t)(tc1 - a.t0) * HD * 4u;
-        bulk_prefetch_l2(p.kc + row, bytes);
-        bulk_prefetch_l2(p.vc + row, bytes);
-    }
-
     __device__ static void prefetch_lm_head() {
         const DecodeParams& p = qw_sm.prm;
         const GemvGeo& g = gF();
@@ -1345,25 +1331,17 @@ public:
 
     __device__ static void produce() {
         prefetch_layer(vprm().layer_w);
-        prefetch_kv(0, vprm().start_pos);
         for (ls().step = 0; cur_step() < vprm().steps; ls().step = cur_step() + 1) {
             for (ls().l = 0; cur_layer() < vprm().L; ls().l = cur_layer() + 1) {
-                if (cur_layer() + 1 < vprm().L) {
-                    prefetch_layer(layer_weights(cur_layer() + 1));
-                    prefetch_kv(cur_layer() + 1, vprm().start_pos + cur_step());
-                } else {
-                    prefetch_lm_head();
-                }
+                if (cur_layer() + 1 < vprm().L) prefetch_layer(layer_weights(cur_layer() + 1));
+                else prefetch_lm_head();
                 gemv_produce(gA(), layer_weights(cur_layer()));
                 attn_produce(cur_step(), cur_layer(), vprm().start_pos + cur_step());
                 gemv_produce(gC(), layer_weights(cur_layer()));
                 gemv_produce(gD(), layer_weights(cur_layer()));
                 gemv_produce(gE(), layer_weights(cur_layer()));
             }
-            if (cur_step() + 1 < vprm().steps) {
-                prefetch_layer(vprm().layer_w);
-                prefetch_kv(0, vprm().start_pos + cur_step() + 1);
-            }
+            if (cur_step() + 1 < vprm().steps) prefetch_layer(vprm().layer_w);
             gemv_produce(gF(), vprm().lm_head);
         }
         drain();

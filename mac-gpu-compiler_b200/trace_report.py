@@ -27,7 +27,7 @@ TPL = 14
 CLUSTER_INTERVALS = [
     ("E1 wait (x*ln1 from the residual exchange)", 0, 1), ("A q|k|v GEMV + push + E2 wait", 1, 2),
     ("B q/k norm + RoPE (+ K/V append)", 2, 3), ("B attention over own positions", 3, 4),
-    ("B partials push + E3 wait", 4, 5), ("B merge 16 partials", 5, 6), ("C o_proj rows + publish", 6, 7),
+    ("B partials push + E3 wait", 4, 5), ("B merge the cluster's partials", 5, 6), ("C o_proj rows + publish", 6, 7),
     ("G1 residual poll + E4 push + wait", 7, 8), ("D gate|up + SiLU + E5 push + wait", 8, 9),
     ("E down rows + publish", 9, 10), ("G2 residual poll + E1 push", 10, 11),
 ]
