@@ -94,10 +94,16 @@ int make_map_bf16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t co
 // Y[M][ldy] = (A_hi + A_lo)[M][K] . B[N][K]^T ; A halves with row pitch lda, B with row pitch ldb
 // With ksplit > 1 the K blocks are split over ksplit CTAs per tile, each writing its partial
 // product to its own slice y + z * M * ldy (the caller sums the slices in a fixed order).
+// With silu_hi/silu_lo (M > 16, ksplit 1, N even): the SiLU epilogue of GemmArgs instead of y.
 int gemm(const uint16_t* a_hi, const uint16_t* a_lo, int lda, const uint16_t* b, int ldb, float* y, int ldy, int M, int N,
-         int K, int* err_word, cudaStream_t s, std::string& err, int ksplit) {
+         int K, int* err_word, cudaStream_t s, std::string& err, int ksplit, uint16_t* silu_hi = nullptr,
+         uint16_t* silu_lo = nullptr) {
     if (M <= 0 || N <= 0 || K <= 0 || K % BK != 0 || ksplit < 1 || ksplit > K / BK) {
         err = "gemm: M, N, K must be positive, K a multiple of 64 and 1 <= ksplit <= K / 64";
+        return QW_ERR_ARG;
+    }
+    if (silu_hi && (M <= SK_NB || ksplit != 1 || N % 2 != 0 || !silu_lo)) {
+        err = "gemm: the SiLU epilogue needs M > 16, one K split and an even N";
         return QW_ERR_ARG;
     }
     CUtensorMap mh, ml, mb;
@@ -138,7 +144,7 @@ int gemm(const uint16_t* a_hi, const uint16_t* a_lo, int lda, const uint16_t* b,
         err = "cannot raise the GEMM kernel's shared-memory limit";
         return QW_ERR_CUDA;
     }
-    GemmArgs args{y, M, N, K, ldy, err_word, (long long)M * ldy};
+    GemmArgs args{y, M, N, K, ldy, err_word, (long long)M * ldy, silu_hi, silu_lo};
     dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, ksplit);
     if ((long long)grid.x * grid.y * grid.z > 148)
         launch(gemm_bf16x2_kernel<STAGES_WIDE>, dim3(grid), dim3(THREADS), SMEM_BYTES_WIDE, s, mh, ml, mb, args);
@@ -1336,11 +1342,22 @@ static int forward_pass(const Weights& w, const CacheView& c, const RowView* row
         // D: residual + rmsnorm -> gate|up -> silu(gate) * up
         launch(norm_kernel(ks_o), dim3(n), dim3(ROW_THREADS), 0, s, sc.X, H, nrm + H, w.eps, sc.ahi, sc.alo, sc.Y, ks_o, nH);
         const uint16_t* Wgu = W + (size_t)QKVR * H + (size_t)H * QD;
-        if ((rc = tc::gemm(sc.ahi, sc.alo, H, Wgu, H, sc.Y, 2 * I, n, 2 * I, H, err_word, s, err, ks_gu))) return rc;
-        launch(silu_split, dim3(grid_for((size_t)n * I)), dim3(256), 0, s, sc.Y, (size_t)n * I, sc.ahi, sc.alo, ks_gu);
-        // E: down (its slices go into X in the next layer's norm)
         const uint16_t* Wd = Wgu + (size_t)2 * I * H;
-        if ((rc = tc::gemm(sc.ahi, sc.alo, I, Wd, I, sc.Y, H, n, H, I, err_word, s, err, ks_d))) return rc;
+        if (ks_gu == 1 && n > tc::SK_NB && (size_t)I * 2 <= (size_t)QD * 4) {
+            // SiLU * up in the gate|up GEMM's epilogue, its bf16 halves into the dead Q and att
+            // buffers (their next writers are the next layer's qkv_post and attention); the GEMM's own
+            // input halves stay in ahi/alo, which its CTAs are still reading
+            uint16_t* hh = reinterpret_cast<uint16_t*>(sc.Q);
+            uint16_t* hl = reinterpret_cast<uint16_t*>(sc.att);
+            if ((rc = tc::gemm(sc.ahi, sc.alo, H, Wgu, H, sc.Y, 2 * I, n, 2 * I, H, err_word, s, err, 1, hh, hl))) return rc;
+            // E: down (its slices go into X in the next layer's norm)
+            if ((rc = tc::gemm(hh, hl, I, Wd, I, sc.Y, H, n, H, I, err_word, s, err, ks_d))) return rc;
+        } else {
+            if ((rc = tc::gemm(sc.ahi, sc.alo, H, Wgu, H, sc.Y, 2 * I, n, 2 * I, H, err_word, s, err, ks_gu))) return rc;
+            launch(silu_split, dim3(grid_for((size_t)n * I)), dim3(256), 0, s, sc.Y, (size_t)n * I, sc.ahi, sc.alo, ks_gu);
+            // E: down (its slices go into X in the next layer's norm)
+            if ((rc = tc::gemm(sc.ahi, sc.alo, I, Wd, I, sc.Y, H, n, H, I, err_word, s, err, ks_d))) return rc;
+        }
     }
     // the last down_proj's slices go into X with the final norm; without logits, add them alone
     if (d_logits) {

@@ -142,6 +142,11 @@ struct GemmArgs {
     int ldy;
     int* err;          // kernel error word (nonzero: a wait ran out)
     long long split_stride;  // elements between the outputs of K splits (blockIdx.z)
+    // SiLU epilogue (gemm_bf16x2_kernel, one K split): instead of y, columns 2i, 2i+1 of the output
+    // (interleaved gate/up rows of B) become h = silu(gate) * up, stored as its bf16 high and low
+    // halves silu_hi/silu_lo[row][i] with row pitch N / 2 (the down GEMM's input); null: plain y
+    uint16_t* silu_hi = nullptr;
+    uint16_t* silu_lo = nullptr;
 };
 
 template <int STG>
@@ -231,7 +236,47 @@ gemm_bf16x2_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_con
     // epilogue: wait for the accumulator (bounded), then TMEM -> registers -> global
     const bool ok = bounded_wait(&done, 0, &abort_flag) && !abort_flag;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (ok) {
+    if (ok && args.silu_hi) {
+        // cpu_inference.rs:166-170, :187: h = silu(gate) * up, the same expression and split as the
+        // separate silu pass, so the values are identical to it
+        const int row = m0 + warp * 32 + lane;
+        const int ldh = args.N / 2;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+            uint32_t r[32];
+            tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, r);
+            if (row < args.M && n0 + c < args.N) {
+                const int np = (args.N - (n0 + c) < 32 ? args.N - (n0 + c) : 32) / 2;
+                const size_t h0 = (size_t)row * ldh + (size_t)((n0 + c) >> 1);
+                uint32_t hp[8], lp[8];
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    const float g = __uint_as_float(r[2 * j]), u = __uint_as_float(r[2 * j + 1]);
+                    const float v = g / (1.0f + __expf(-g)) * u;
+                    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+                    const uint32_t hb = __bfloat16_as_ushort(h);
+                    const uint32_t lb = __bfloat16_as_ushort(__float2bfloat16_rn(v - __bfloat162float(h)));
+                    if (j & 1) { hp[j >> 1] |= hb << 16; lp[j >> 1] |= lb << 16; }
+                    else { hp[j >> 1] = hb; lp[j >> 1] = lb; }
+                }
+                uint16_t* dh = args.silu_hi + h0;
+                uint16_t* dl = args.silu_lo + h0;
+                if (np == 16 && ((reinterpret_cast<uintptr_t>(dh) | reinterpret_cast<uintptr_t>(dl)) & 15) == 0) {
+                    reinterpret_cast<uint4*>(dh)[0] = make_uint4(hp[0], hp[1], hp[2], hp[3]);
+                    reinterpret_cast<uint4*>(dh)[1] = make_uint4(hp[4], hp[5], hp[6], hp[7]);
+                    reinterpret_cast<uint4*>(dl)[0] = make_uint4(lp[0], lp[1], lp[2], lp[3]);
+                    reinterpret_cast<uint4*>(dl)[1] = make_uint4(lp[4], lp[5], lp[6], lp[7]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; j++)
+                        if (j < np) {
+                            dh[j] = (uint16_t)(hp[j >> 1] >> (16 * (j & 1)));
+                            dl[j] = (uint16_t)(lp[j >> 1] >> (16 * (j & 1)));
+                        }
+                }
+            }
+        }
+    } else if (ok) {
         const int row = m0 + warp * 32 + lane;
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
