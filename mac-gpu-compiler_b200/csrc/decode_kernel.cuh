@@ -76,7 +76,8 @@ constexpr int TRACE_PER_LAYER = 14;
 
 // error codes written to DecodeParams::err[0]
 enum : int { DERR_NONE = 0, DERR_TIMEOUT_GRID = 1, DERR_TIMEOUT_FULL = 2, DERR_TIMEOUT_EMPTY = 3,
-             DERR_TIMEOUT_KV = 4, DERR_BAD_TOKEN = 5, DERR_TIMEOUT_DRAIN = 6, DERR_TIMEOUT_DATA = 7 };
+             DERR_TIMEOUT_KV = 4, DERR_BAD_TOKEN = 5, DERR_TIMEOUT_DRAIN = 6, DERR_TIMEOUT_DATA = 7,
+             DERR_SHAPE = 8 };
 
 typedef unsigned long long u64;
 
@@ -301,7 +302,15 @@ extern __shared__ __align__(128) uint8_t qw_dyn[];
 // out-of-line phase routines need, nothing sits in local memory, which on this kernel is backed
 // by an L1 of only ~24 KB (shared memory takes the rest) and would miss to L2 on the critical
 // path. It also keeps the kernel within the 128 registers a 13-warp CTA can have per thread.
-class Decoder {
+//
+// Two compile-time switches leave code out of the kernel that a launch does not need: kTrace, the
+// phase-timeline stamps (qw_set_trace), and kGeneric, the GEMV routine for phases whose rows do not
+// split into whole 1024-column segments (the Qwen3-0.6B shapes never need it). The kernel's speed
+// depends on its code size as well as on the instructions it executes: without both, the 130 + 128
+// token decode ran 2% faster (same-box A/B, 1,972 -> 2,012 tok/s). The effect is one of layout as much
+// as of size: instantiating only the 2-head attention routine in this variant made it 2% slower again.
+template <bool kTrace, bool kGeneric>
+class DecoderT {
 public:
     __device__ __forceinline__ static int tid() { return (int)threadIdx.x; }
     __device__ __forceinline__ static int warp() { return (int)(threadIdx.x >> 5); }
@@ -344,6 +353,11 @@ public:
         qw_sm.geo[4] = make_geo(p.V, p.H, c, nc, 0, 0);
         for (int k = 0; k < 5; k++)
             for (int w = 0; w < NCW; w++) qw_sm.wgeo[k][w] = make_warp_geo(qw_sm.geo[k], w);
+        if constexpr (!kGeneric) {  // the host picked the variant without the generic routine: confirm it
+            const bool part[5] = {false, true, false, true, true};  // EPI of A, C, D, E, F
+            for (int k = 0; k < 5; k++)
+                if (!full_segments(qw_sm.geo[k], part[k])) fail(DERR_SHAPE, k);
+        }
     }
 
     // phase sequence numbers within the launch -> tags (12 bits of epoch, 20 bits of sequence)
@@ -358,8 +372,14 @@ public:
 
     __device__ __forceinline__ static void stamp(int step, int idx) {
         const volatile DecodeParams& p = qw_sm.prm;
-        if (p.trace != nullptr && step == 0 && tid() == 0)
-            p.trace[(size_t)cta() * (TRACE_PER_LAYER * p.L + 4) + idx] = globaltimer_ns();
+        if constexpr (kTrace) {
+            if (p.trace != nullptr && step == 0 && tid() == 0)
+                p.trace[(size_t)cta() * (TRACE_PER_LAYER * p.L + 4) + idx] = globaltimer_ns();
+        } else {
+            (void)p;
+            (void)step;
+            (void)idx;
+        }
     }
 
 
@@ -670,6 +690,12 @@ public:
     // warp whole (gate, up) row pairs - warp w takes pair w % 6 of pieces w / 6 and w / 6 + 2 of a
     // group - and stores silu(gate) * up as out[row / 2]. The fused epilogues write their results
     // before the phase's closing barrier, so the hand-off to other CTAs starts earlier.
+    // whether gemv_full_segments covers phase g: whole 1024-column segments, at most one unit per warp
+    // per piece, and (outputs stored from the reduction lanes) one segment of 12 rows per piece
+    __host__ __device__ static bool full_segments(const GemvGeo& g, bool part) {
+        return g.cpl == 4 && g.rpp * g.segs <= NCW && (part || (g.segs == 1 && g.rpp == 12));
+    }
+
     template <int EPI>
     __device__ __noinline__ static void gemv_full_segments(const GemvGeo& gs, u64* out, uint32_t tg) {
         uint32_t& it = ring_pos();
@@ -771,13 +797,16 @@ public:
     // row sums in part() for residual_rows / lm_epilogue
     template <int EPI>
     __device__ __forceinline__ static void gemv_consume(const GemvGeo& g, u64* out = nullptr, uint32_t tg = 0) {
-        const bool full = g.cpl == 4 && g.rpp * g.segs <= NCW && (EPI == EPI_PART || (g.segs == 1 && g.rpp == 12));
-        if (full) {
-            gemv_full_segments<EPI>(g, out, tg);
+        if constexpr (kGeneric) {
+            if (full_segments(g, EPI == EPI_PART)) {
+                gemv_full_segments<EPI>(g, out, tg);
+            } else {
+                gemv_generic(g);
+                if (EPI == EPI_STORE) store_rows(out, g, tg);
+                if (EPI == EPI_SILU) silu_rows(tg);
+            }
         } else {
-            gemv_generic(g);
-            if (EPI == EPI_STORE) store_rows(out, g, tg);
-            if (EPI == EPI_SILU) silu_rows(tg);
+            gemv_full_segments<EPI>(g, out, tg);  // init_geometry checked every phase's shape
         }
     }
 
@@ -1369,5 +1398,16 @@ public:
         }
     }
 };
+
+// every phase of the model's shapes runs gemv_full_segments (kGeneric = false is then safe): rows of
+// the lm_head, o and down in whole 1024-column segments whose count divides 12, q|k|v and gate|up
+// over exactly 1024 columns
+inline bool full_segment_shapes(int H, int QD, int I) {
+    auto part_ok = [](int K) { return K % 1024 == 0 && K / 1024 >= 1 && 12 % (K / 1024) == 0; };
+    return H == 1024 && part_ok(QD) && part_ok(I);
+}
+
+// the GEMV micro-benchmark kernel's decoder: every shape, no trace
+using Decoder = DecoderT<false, true>;
 
 }  // namespace qw

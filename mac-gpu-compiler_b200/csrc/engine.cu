@@ -63,6 +63,8 @@ const char* derr_name(int code) {
         case DERR_TIMEOUT_KV: return "KV visibility wait expired";
         case DERR_BAD_TOKEN: return "input token id >= vocab_size";
         case DERR_TIMEOUT_DRAIN: return "bulk-copy drain wait expired";
+        case DERR_TIMEOUT_DATA: return "activation hand-off wait expired";
+        case DERR_SHAPE: return "decode kernel variant does not cover the model's shapes";
         default: return "unknown device error";
     }
 }
@@ -92,9 +94,13 @@ int* device_err_word_for(int device) {
 
 namespace qw {
 
-// the persistent decode kernel (device code in decode_kernel.cuh)
+// the persistent decode kernel (device code in decode_kernel.cuh), in four variants: with or without
+// the phase-timeline stamps, with or without the GEMV routine for shapes that are not whole
+// 1024-column segments (kernel_for picks one per launch)
 // 13 warps: one SM sub-partition holds 4 of them, so 16K registers / 128 threads caps it at 128 each
+template <bool kTrace, bool kGeneric>
 __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_constant__ DecodeParams p) {
+    using Decoder = DecoderT<kTrace, kGeneric>;
     if (threadIdx.x == 0) {
         for (int i = 0; i < NSLOT; i++) {
             mbar_init(&qw_sm.full[i], 1);
@@ -117,6 +123,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_kernel(const __grid_consta
     Decoder::consume();
 }
 
+// the decode kernel variant for a launch: stamps only when tracing, the generic GEMV routine only
+// for shapes that need it
+inline const void* kernel_for(bool trace, bool generic) {
+    if (trace) return generic ? (const void*)decode_kernel<true, true> : (const void*)decode_kernel<true, false>;
+    return generic ? (const void*)decode_kernel<false, true> : (const void*)decode_kernel<false, false>;
+}
+
 }  // namespace qw
 
 struct qw_model {
@@ -125,6 +138,7 @@ struct qw_model {
     cudaStream_t stream = nullptr;
     int nctas = 0;    // grid of the decode kernel in use
     int kind = 0;     // QW_DECODER_GRID (decode_kernel.cuh) or QW_DECODER_CLUSTER (cluster_decode.cuh)
+    bool generic = true;  // grid kernel: the shapes need the generic GEMV routine (full_segment_shapes)
     bool cl_coop = true;          // cluster launches also ask for co-residency (cooperative) until refused
     uint16_t* d_clw = nullptr;    // cluster kernel: o_proj and down_proj repacked per (layer, cluster, rank)
     u64 *d_po = nullptr, *d_pd = nullptr;  // cluster kernel: [8][hidden] partial residual updates (tagged words)
@@ -362,7 +376,7 @@ int launch_decode(qw_model* m, qw_cache* c, const uint32_t* tok_in, uint32_t* to
     p.stall_cta = m->stall_cta;
     m->stall_cta = -1;
     void* args[] = {&p};
-    cudaError_t e = cudaLaunchCooperativeKernel((const void*)decode_kernel, dim3(m->nctas), dim3(NTHREADS), args,
+    cudaError_t e = cudaLaunchCooperativeKernel(kernel_for(m->d_trace != nullptr, m->generic), dim3(m->nctas), dim3(NTHREADS), args,
                                                 m->dyn_smem, s);
     if (e != cudaSuccess) return cuda_err(e, "decode kernel launch");
     return QW_OK;
@@ -594,11 +608,15 @@ int qw_load(const char* path, int device, qw_model** out) {
     m->dyn_smem = (size_t)NSLOT * SLOT_BYTES + ((size_t)m->part_cap + m->xs_cap + m->xloc_cap) * 4;
     if (m->dyn_smem + sizeof(Smem) > (size_t)prop.sharedMemPerBlockOptin)
         return fail(QW_ERR_UNSUPPORTED, "model too large for the kernel's shared-memory plan (vocab or widths)");
-    if (cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->dyn_smem) != cudaSuccess)
-        return fail(QW_ERR_CUDA, "cannot raise the decode kernel's shared-memory limit");
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_kernel, NTHREADS, m->dyn_smem) != cudaSuccess || per_sm < 1)
-        return fail(QW_ERR_UNSUPPORTED, "decode kernel does not fit on an SM");
+    m->generic = !full_segment_shapes((int)H, (int)QD, (int)I);
+    for (int t = 0; t < 2; t++) {
+        const void* k = kernel_for(t == 1, m->generic);
+        if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)m->dyn_smem) != cudaSuccess)
+            return fail(QW_ERR_CUDA, "cannot raise the decode kernel's shared-memory limit");
+        int per_sm = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, NTHREADS, m->dyn_smem) != cudaSuccess || per_sm < 1)
+            return fail(QW_ERR_UNSUPPORTED, "decode kernel does not fit on an SM");
+    }
 
     struct Piece { size_t bytes; void** dst; };
     const size_t sz_apart = (size_t)c.kv_heads * m->S * G * APART_STRIDE * 8;
