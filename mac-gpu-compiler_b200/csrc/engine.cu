@@ -952,7 +952,8 @@ int row_graph(qw_model* m, int kind, int B, int splits, uint32_t* out, int* ew, 
     cudaStream_t s = m->stream;
     QW_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
     std::string err;
-    int rc = qw::pf::run_rows(weights_of(m), m->d_rows, B, splits, m->d_btok, m->d_pf_logits, m->pf, ew, s, err);
+    // kind 0 rows are distinct caches (batch_rows refuses a cache twice); a lookup pass's rows share one
+    int rc = qw::pf::run_rows(weights_of(m), m->d_rows, B, splits, kind == 0, m->d_btok, m->d_pf_logits, m->pf, ew, s, err);
     if (!rc)
         rc = kind == 0 ? qw::pf::argmax_rows(m->d_pf_logits, (int)m->cfg.vocab, B, m->d_rows, m->d_btok, out, m->d_am, s, err)
                        : qw::pf::argmax_each(m->d_pf_logits, (int)m->cfg.vocab, B, out, m->d_am, s, err);
@@ -1008,7 +1009,7 @@ int qw_forward_batch(qw_model* m, qw_cache* const* caches, size_t B, const uint3
     QW_CUDA(cudaMemcpyAsync(m->d_rows, rows.data(), B * sizeof(qw::pf::RowView), cudaMemcpyHostToDevice, s));
     QW_CUDA(cudaMemcpyAsync(m->d_btok, tokens, B * 4, cudaMemcpyHostToDevice, s));
     std::string err;
-    if (int e = qw::pf::run_rows(weights_of(m), m->d_rows, (int)B, splits, m->d_btok, m->d_pf_logits, m->pf, ew, s, err))
+    if (int e = qw::pf::run_rows(weights_of(m), m->d_rows, (int)B, splits, true, m->d_btok, m->d_pf_logits, m->pf, ew, s, err))
         return set_err(e, err);
     QW_CUDA(cudaMemcpyAsync(logits_out, m->d_pf_logits, B * m->cfg.vocab * 4, cudaMemcpyDeviceToHost, s));
     int h = 0;

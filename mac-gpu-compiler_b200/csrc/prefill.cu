@@ -323,6 +323,34 @@ __global__ void silu_split(const float* Y, size_t n_inter, uint16_t* hi, uint16_
     }
 }
 
+// One head's RMSNorm (gains gv) and rotate-half RoPE (cos/sin cs) across a warp: lane l holds
+// dimensions 4 l .. 4 l + 3 (cpu_inference.rs:134-138, :196-215)
+__device__ __forceinline__ float4 head_norm_rope(float4 v, const float (&gv)[4], const float2 (&cs)[4], float eps, int lane) {
+    float ss = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    const float s = rsqrtf(ss / 128.0f + eps);
+    float e[4] = {v.x, v.y, v.z, v.w}, o4[4];
+    for (int j = 0; j < 4; j++) e[j] = e[j] * s * gv[j];
+    for (int j = 0; j < 4; j++) {
+        const float other = __shfl_xor_sync(0xFFFFFFFFu, e[j], 16);  // element d +- 64
+        o4[j] = lane < 16 ? e[j] * cs[j].x - other * cs[j].y : e[j] * cs[j].x + other * cs[j].y;
+    }
+    return make_float4(o4[0], o4[1], o4[2], o4[3]);
+}
+
+// the split-K slices of one head's 128 q|k|v outputs for token t, added in slice order (lane: 4 dims)
+__device__ __forceinline__ float4 head_sum(const float* Y, int nparts, size_t ps, size_t off, int lane) {
+    float4 v = reinterpret_cast<const float4*>(Y + off)[lane];
+    for (int z = 1; z < nparts; z++) {
+        const float4 w = reinterpret_cast<const float4*>(Y + z * ps + off)[lane];
+        v.x += w.x;
+        v.y += w.y;
+        v.z += w.z;
+        v.w += w.w;
+    }
+    return v;
+}
+
 // Per token and head of the q|k|v outputs Y[t][QKVR] (the sum of nparts split-K slices, in order):
 // q heads get q_norm + RoPE into Q[t][NQ*128]; k heads k_norm + RoPE and v heads as they are go
 // into the cache (cpu_inference.rs:134-141, :196-215; the RoPE table is the decode path's). One
@@ -366,29 +394,13 @@ __global__ void qkv_post(const float* Y, int nparts, int n, int start, int NQ, i
     const size_t head_stride_l = (size_t)layer * NKV * max_seq * 128;
     const int QKVR = per_tok * 128;
     const size_t ps = (size_t)n * QKVR;
-    float4 v = reinterpret_cast<const float4*>(Y + (size_t)t * QKVR + (size_t)hh * 128)[lane];
-    for (int z = 1; z < nparts; z++) {
-        const float4 w = reinterpret_cast<const float4*>(Y + z * ps + (size_t)t * QKVR + (size_t)hh * 128)[lane];
-        v.x += w.x;
-        v.y += w.y;
-        v.z += w.z;
-        v.w += w.w;
-    }
+    const float4 v = head_sum(Y, nparts, ps, (size_t)t * QKVR + (size_t)hh * 128, lane);
     if (hh >= NQ + NKV) {  // v head: straight into the cache
         const int g = hh - NQ - NKV;
         reinterpret_cast<float4*>(Vc + head_stride_l + ((size_t)g * max_seq + pos) * 128)[lane] = v;
         return;
     }
-    float ss = v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
-    const float s = rsqrtf(ss / 128.0f + eps);
-    float e[4] = {v.x, v.y, v.z, v.w}, o4[4];
-    for (int j = 0; j < 4; j++) e[j] = e[j] * s * gv[j];
-    for (int j = 0; j < 4; j++) {
-        const float other = __shfl_xor_sync(0xFFFFFFFFu, e[j], 16);  // element d +- 64
-        o4[j] = lane < 16 ? e[j] * cs[j].x - other * cs[j].y : e[j] * cs[j].x + other * cs[j].y;
-    }
-    const float4 out = make_float4(o4[0], o4[1], o4[2], o4[3]);
+    const float4 out = head_norm_rope(v, gv, cs, eps, lane);
     if (hh < NQ) reinterpret_cast<float4*>(Q + (size_t)t * NQ * 128 + (size_t)hh * 128)[lane] = out;
     else reinterpret_cast<float4*>(Kc + head_stride_l + ((size_t)(hh - NQ) * max_seq + pos) * 128)[lane] = out;
 }
@@ -1035,12 +1047,22 @@ constexpr int RA_PER_WARP = ROW_SPLIT / RA_WARPS;
 // combines them in split order and writes the o_proj GEMM's input halves for the G heads. Same
 // math as cpu_inference.rs:143-161 (scores scaled by 1/sqrt(128), softmax, sum of p . v), with the
 // softmax done online.
-template <int G>
+//
+// FUSED (rows in distinct caches, so no row reads another row's K/V of this step): the CTA also
+// does qkv_post's work for itself. Warps 0 .. G-1 sum the split-K slices of Y for the G query heads
+// and apply q_norm + RoPE into shared memory (every split of the row recomputes them); in the
+// split holding the row's position, warps G and G+1 form that position's k (k_norm + RoPE) and v
+// and write them into the cache before the CTA's K/V loads. Same helpers, so the same values as
+// the qkv_post pass.
+template <int G, bool FUSED>
 __global__ void __launch_bounds__(RA_THREADS) row_attention(const float* Q, const RowView* rows, int NQ, int NKV, int layer,
                                                             float scale, float* part, int splits, unsigned* tickets,
-                                                            uint16_t* ahi, uint16_t* alo) {
+                                                            uint16_t* ahi, uint16_t* alo, const float* Y, int nparts,
+                                                            const uint16_t* qn, const uint16_t* kn, float eps) {
+    static_assert(!FUSED || G + 2 <= RA_WARPS, "fused q|k|v epilogue needs G + 2 warps");
     __shared__ float sm_o[RA_WARPS][G][128];
     __shared__ float sm_m[RA_WARPS][G], sm_l[RA_WARPS][G];
+    __shared__ __align__(16) float sm_q[FUSED ? G : 1][128];
     const int b = blockIdx.x, g = blockIdx.y, z = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // the row views were last written by the previous step's argmax, which every kernel since
@@ -1050,8 +1072,8 @@ __global__ void __launch_bounds__(RA_THREADS) row_attention(const float* Q, cons
     if (p_begin > rv.pos) return;  // past this row's positions (the merge reads only live splits)
     const int p_end = min(p_begin + ROW_SPLIT, rv.pos + 1);
     const size_t head_off = ((size_t)layer * NKV + g) * rv.max_seq * 128;
-    const float* kb = rv.k + head_off;
-    const float* vb = rv.v + head_off;
+    float* kb = rv.k + head_off;
+    float* vb = rv.v + head_off;
     // warm L2 with the split's K/V rows while the previous kernel finishes; the loads themselves
     // come after the wait (qkv_post writes this step's rows, and in a multi-position pass other
     // rows' positions too)
@@ -1059,13 +1081,42 @@ __global__ void __launch_bounds__(RA_THREADS) row_attention(const float* Q, cons
         bulk_prefetch_l2(kb + (size_t)p_begin * 128, (uint32_t)(p_end - p_begin) * 512u);
         bulk_prefetch_l2(vb + (size_t)p_begin * 128, (uint32_t)(p_end - p_begin) * 512u);
     }
+    // fused: this warp's head (q heads g G .. g G + G - 1, then k and v of head g in the split that
+    // holds the row's position), its gains and RoPE row, fetched before the wait
+    const bool cur = p_end == rv.pos + 1;
+    const int hw = FUSED ? (warp < G ? g * G + warp : warp == G && cur ? NQ + g : warp == G + 1 && cur ? NQ + NKV + g : -1) : -1;
+    float gv[4] = {0.f, 0.f, 0.f, 0.f};
+    float2 cs[4] = {};
+    if (FUSED && hw >= 0 && hw < NQ + NKV) {
+        const uint16_t* gw = hw < NQ ? qn : kn;
+        const float2* rr = rv.rope + (size_t)rv.pos * 64;
+        for (int j = 0; j < 4; j++) {
+            gv[j] = bf16f(gw[lane * 4 + j]);
+            cs[j] = rr[(lane * 4 + j) & 63];
+        }
+    }
     pdl_wait();
     pdl_trigger();
+    if constexpr (FUSED) {
+        if (hw >= 0) {
+            const int QKVR = (NQ + 2 * NKV) * 128;
+            const float4 v = head_sum(Y, nparts, (size_t)gridDim.x * QKVR, (size_t)b * QKVR + (size_t)hw * 128, lane);
+            if (hw >= NQ + NKV) {
+                reinterpret_cast<float4*>(vb + (size_t)rv.pos * 128)[lane] = v;
+            } else {
+                const float4 e = head_norm_rope(v, gv, cs, eps, lane);
+                if (hw < NQ) reinterpret_cast<float4*>(sm_q[warp])[lane] = e;
+                else reinterpret_cast<float4*>(kb + (size_t)rv.pos * 128)[lane] = e;
+            }
+        }
+        __syncthreads();  // q in shared memory; this position's k and v in the cache (CTA-visible)
+    }
     float4 q[G], o[G];
     float m[G], l[G];
 #pragma unroll
     for (int h = 0; h < G; h++) {
-        q[h] = reinterpret_cast<const float4*>(Q + (size_t)b * NQ * 128 + (size_t)(g * G + h) * 128)[lane];
+        if constexpr (FUSED) q[h] = reinterpret_cast<const float4*>(sm_q[h])[lane];
+        else q[h] = reinterpret_cast<const float4*>(Q + (size_t)b * NQ * 128 + (size_t)(g * G + h) * 128)[lane];
         o[h] = make_float4(0.f, 0.f, 0.f, 0.f);
         m[h] = -INFINITY;
         l[h] = 0.f;
@@ -1280,8 +1331,9 @@ int argmax_rows(const float* d_logits, int V, int B, RowView* d_rows, uint32_t* 
 typedef void (*NormSplitFn)(float*, int, const uint16_t*, float, uint16_t*, uint16_t*, const float*, int, size_t);
 inline NormSplitFn norm_kernel(int nparts) { return nparts > 4 ? norm_split<true> : norm_split<false>; }
 
-static int forward_pass(const Weights& w, const CacheView& c, const RowView* rows, int splits, const uint32_t* d_ids, int n,
-                        int start, float* d_logits, Scratch& sc, int* err_word, cudaStream_t s, std::string& err) {
+static int forward_pass(const Weights& w, const CacheView& c, const RowView* rows, int splits, bool fused,
+                        const uint32_t* d_ids, int n, int start, float* d_logits, Scratch& sc, int* err_word,
+                        cudaStream_t s, std::string& err) {
     const int H = w.H, I = w.I, NQ = w.NQ, NKV = w.NKV, QD = NQ * 128, KVD = NKV * 128, QKVR = QD + 2 * KVD;
     const size_t nH = (size_t)n * H;
     if (sc.ycap < y_floats(n, H, I, NQ, NKV)) {
@@ -1293,33 +1345,36 @@ static int forward_pass(const Weights& w, const CacheView& c, const RowView* row
     const float scale = 1.0f / sqrtf(128.0f);
     const int ks_qkv = ksplit_for(n, QKVR, H), ks_o = ksplit_for(n, H, QD), ks_gu = ksplit_for(n, 2 * I, H),
               ks_d = ksplit_for(n, H, I);
+    // residual add of the previous projection's nparts slices + RMSNorm + bf16 split, one CTA per row
+    auto norm = [&](int nparts, const uint16_t* gain) {
+        launch(norm_kernel(nparts), dim3(n), dim3(ROW_THREADS), 0, s, sc.X, H, gain, w.eps, sc.ahi, sc.alo, sc.Y, nparts, nH);
+    };
     for (int l = 0; l < w.L; l++) {
         const uint16_t* W = w.layer_w + (size_t)l * w.layer_stride;
         const uint16_t* nrm = w.layer_n + (size_t)l * w.norm_stride;
         int rc;
         // A: (the previous layer's down_proj slices into X) rmsnorm -> q|k|v
-        launch(norm_kernel(l == 0 ? 0 : ks_d), dim3(n), dim3(ROW_THREADS), 0, s, sc.X, H, nrm, w.eps, sc.ahi, sc.alo, sc.Y,
-               l == 0 ? 0 : ks_d, nH);
+        norm(l == 0 ? 0 : ks_d, nrm);
         if ((rc = tc::gemm(sc.ahi, sc.alo, H, W, H, sc.Y, QKVR, n, QKVR, H, err_word, s, err, ks_qkv))) return rc;
         // B: q/k norm + RoPE, K/V into the cache, attention -> o_proj input halves
         const int items = n * (NQ + 2 * NKV);
-        launch(qkv_post, dim3((items + 7) / 8), dim3(256), 0, s, sc.Y, ks_qkv, n, start, NQ, NKV, nrm + 2 * H,
-               nrm + 2 * H + 128, w.eps, c, rows, l, sc.Q);
+        if (!(rows && fused))
+            launch(qkv_post, dim3((items + 7) / 8), dim3(256), 0, s, sc.Y, ks_qkv, n, start, NQ, NKV, nrm + 2 * H,
+                   nrm + 2 * H + 128, w.eps, c, rows, l, sc.Q);
         if (rows) {
             if (row_partial_floats(n, NQ, splits) > sc.attp_cap) {
                 err = "row attention partial buffer too small";
                 return QW_ERR_ARG;
             }
             const dim3 ag(n, NKV, splits);
-            if (G == 1)
-                launch(row_attention<1>, dim3(ag), dim3(RA_THREADS), 0, s, sc.Q, rows, NQ, NKV, l, scale, sc.attp, splits,
-                       sc.att_tickets, sc.ahi, sc.alo);
-            else if (G == 2)
-                launch(row_attention<2>, dim3(ag), dim3(RA_THREADS), 0, s, sc.Q, rows, NQ, NKV, l, scale, sc.attp, splits,
-                       sc.att_tickets, sc.ahi, sc.alo);
-            else
-                launch(row_attention<3>, dim3(ag), dim3(RA_THREADS), 0, s, sc.Q, rows, NQ, NKV, l, scale, sc.attp, splits,
-                       sc.att_tickets, sc.ahi, sc.alo);
+            const uint16_t *qn = nrm + 2 * H, *kn = nrm + 2 * H + 128;
+#define QW_ROW_ATT(GQ, F)                                                                                             \
+    launch(row_attention<GQ, F>, dim3(ag), dim3(RA_THREADS), 0, s, sc.Q, rows, NQ, NKV, l, scale, sc.attp, splits,    \
+           sc.att_tickets, sc.ahi, sc.alo, (const float*)sc.Y, ks_qkv, qn, kn, w.eps)
+            if (G == 1) fused ? QW_ROW_ATT(1, true) : QW_ROW_ATT(1, false);
+            else if (G == 2) fused ? QW_ROW_ATT(2, true) : QW_ROW_ATT(2, false);
+            else fused ? QW_ROW_ATT(3, true) : QW_ROW_ATT(3, false);
+#undef QW_ROW_ATT
         } else {
             const size_t hsl = (size_t)l * NKV * c.max_seq * 128;
             rc = G == 1 ? launch_attention_tc<1>(sc.Q, sc.att, c.k, c.v, n, start, NQ, NKV, hsl, c.max_seq, scale, sc.attp,
@@ -1340,7 +1395,7 @@ static int forward_pass(const Weights& w, const CacheView& c, const RowView* row
         // C: o_proj (its slices go into X in the next norm)
         if ((rc = tc::gemm(sc.ahi, sc.alo, QD, W + (size_t)QKVR * H, QD, sc.Y, H, n, H, QD, err_word, s, err, ks_o))) return rc;
         // D: residual + rmsnorm -> gate|up -> silu(gate) * up
-        launch(norm_kernel(ks_o), dim3(n), dim3(ROW_THREADS), 0, s, sc.X, H, nrm + H, w.eps, sc.ahi, sc.alo, sc.Y, ks_o, nH);
+        norm(ks_o, nrm + H);
         const uint16_t* Wgu = W + (size_t)QKVR * H + (size_t)H * QD;
         const uint16_t* Wd = Wgu + (size_t)2 * I * H;
         if (ks_gu == 1 && n > tc::SK_NB && (size_t)I * 2 <= (size_t)QD * 4) {
@@ -1361,7 +1416,7 @@ static int forward_pass(const Weights& w, const CacheView& c, const RowView* row
     }
     // the last down_proj's slices go into X with the final norm; without logits, add them alone
     if (d_logits) {
-        launch(norm_kernel(ks_d), dim3(n), dim3(ROW_THREADS), 0, s, sc.X, H, w.final_norm, w.eps, sc.ahi, sc.alo, sc.Y, ks_d, nH);
+        norm(ks_d, w.final_norm);
         int rc;
         if ((rc = tc::gemm(sc.ahi, sc.alo, H, w.lm_head, H, d_logits, w.V, n, w.V, H, err_word, s, err, 1))) return rc;
     } else {
@@ -1377,16 +1432,16 @@ static int forward_pass(const Weights& w, const CacheView& c, const RowView* row
 
 int run(const Weights& w, const CacheView& c, const uint32_t* d_ids, int n, int start, float* d_logits, Scratch& sc,
         int* err_word, cudaStream_t s, std::string& err) {
-    return forward_pass(w, c, nullptr, 0, d_ids, n, start, d_logits, sc, err_word, s, err);
+    return forward_pass(w, c, nullptr, 0, false, d_ids, n, start, d_logits, sc, err_word, s, err);
 }
 
-int run_rows(const Weights& w, const RowView* d_rows, int B, int splits, const uint32_t* d_tok, float* d_logits,
-             Scratch& sc, int* err_word, cudaStream_t s, std::string& err) {
+int run_rows(const Weights& w, const RowView* d_rows, int B, int splits, bool distinct_caches, const uint32_t* d_tok,
+             float* d_logits, Scratch& sc, int* err_word, cudaStream_t s, std::string& err) {
     if (B < 1 || B > ROWS_MAX || splits < 1) {
         err = "row step: 1 <= rows <= 16 and splits >= 1";
         return QW_ERR_ARG;
     }
-    return forward_pass(w, CacheView{}, d_rows, splits, d_tok, B, 0, d_logits, sc, err_word, s, err);
+    return forward_pass(w, CacheView{}, d_rows, splits, distinct_caches, d_tok, B, 0, d_logits, sc, err_word, s, err);
 }
 
 }  // namespace pf

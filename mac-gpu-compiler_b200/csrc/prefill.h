@@ -86,9 +86,12 @@ size_t row_partial_floats(int B, int NQ, int splits);
 
 // One row-mode step over B rows (B <= ROWS_MAX): row b feeds d_tok[b] at d_rows[b].pos into its
 // own cache and, with d_logits ([B][V]), gets its logits. `splits` position splits of ROW_SPLIT
-// cover every row's positions (pos < splits * ROW_SPLIT). Stream-ordered; capturable.
-int run_rows(const Weights& w, const RowView* d_rows, int B, int splits, const uint32_t* d_tok, float* d_logits,
-             Scratch& sc, int* err_word, cudaStream_t s, std::string& err);
+// cover every row's positions (pos < splits * ROW_SPLIT). distinct_caches: no two rows share a
+// cache, so each attention CTA may form its own row's q, k and v (no separate qkv_post pass); rows
+// that share a cache (a lookup verify pass) need every row's K/V written before any attention.
+// Stream-ordered; capturable.
+int run_rows(const Weights& w, const RowView* d_rows, int B, int splits, bool distinct_caches, const uint32_t* d_tok,
+             float* d_logits, Scratch& sc, int* err_word, cudaStream_t s, std::string& err);
 
 // device scratch of the row argmax: per row, the best (value, index) of each of its AR_PARTS
 // blocks and an arrival ticket (zero between launches)
