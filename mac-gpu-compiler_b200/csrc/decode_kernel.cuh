@@ -55,7 +55,7 @@ constexpr int HD = 128;                       // head_dim (the reference's atten
 constexpr int ATT_P = SLOT_BYTES / (2 * HD * 4);  // cached positions per attention ring slot (24)
 constexpr int MAX_G = 3;                      // query heads per KV head
 constexpr int MAX_S = 18;                     // attention chunks per KV head
-constexpr int MIN_CHUNK = 32;                 // default fewest positions per attention chunk (DecodeParams::min_chunk)
+constexpr int MIN_CHUNK = 48;                 // default fewest positions per attention chunk (DecodeParams::min_chunk)
 constexpr uint32_t LM_PREFETCH_BYTES = 256u * 1024;  // lm_head bytes per CTA warmed into L2 ahead of use
 constexpr int APART_STRIDE = HD + 4;          // words per attention partial: acc[128], m, l, pad
 constexpr int ATT_WST = HD + 4;               // floats per (warp, head) softmax state staged in part: acc[128], m, l, pad
