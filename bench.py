@@ -40,6 +40,7 @@ import os
 import statistics
 import subprocess
 import sys
+import threading
 import time
 from pathlib import Path
 
@@ -550,24 +551,46 @@ class ClockSampler:
         self.proc = None
 
     def __enter__(self):
+        # a reader thread collects samples; entering waits (up to 3 s) for the first one, so a short
+        # timed region still falls inside the sampling window
+        self.lines = []
+        self._thread = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
+            return self
+        first = threading.Event()
+
+        def read():
+            for l in self.proc.stdout:
+                if l.strip():
+                    self.lines.append(l.strip())
+                    first.set()
+            first.set()
+
+        self._thread = threading.Thread(target=read, daemon=True)
+        self._thread.start()
+        first.wait(timeout=3.0)
+        self._start = len(self.lines)
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
         if self.proc is not None:
+            n = len(self.lines)
+            deadline = time.time() + 0.5
+            while len(self.lines) <= n and time.time() < deadline:  # one sample at the end of the region
+                time.sleep(0.02)
             self.proc.terminate()
             try:
-                out, _ = self.proc.communicate(timeout=5)
+                self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+                self.proc.wait()
+            if self._thread is not None:
+                self._thread.join(timeout=5)
         return False
 
     def summary(self) -> dict:
