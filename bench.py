@@ -103,11 +103,11 @@ def workload_config(name: str, world: int, rows: int = 0) -> dict:
 # (metal_infrence_engine/README.md:22)
 PUBLISHED_TPS = 46.37
 # DRAM traffic of the decode kernel relative to its algorithmic bytes, from one ncu capture of
-# mac-gpu-compiler_b200/profile_case.py's decode launch: a 4-token launch at positions 8..11 read
-# 4,777,855,000 B and wrote 5,338,112 B against 4,778,041,344 algorithmic bytes. The bench launch
+# `bench.py --profile-case decode`'s decode launch: a 4-token launch at positions 8..11 read
+# 4,777,358,000 B and wrote 4,609,280 B against 4,778,041,344 algorithmic bytes. The bench launch
 # (128 tokens, ~158 GB) is too large to capture, and its traffic grows with the same weight + K/V
 # bytes per token, so roofline.traffic is that ratio times the launch's algorithmic bytes.
-NCU_TRAFFIC_RATIO = (4_777_855_000 + 5_338_112) / 4_778_041_344
+NCU_TRAFFIC_RATIO = (4_777_358_000 + 4_609_280) / 4_778_041_344
 
 
 def kv_bytes_at(cfg, pos: int) -> int:
