@@ -1036,7 +1036,7 @@ int grid_for(size_t total) { return (int)std::min<size_t>((total + 255) / 256, 1
 // cache. Attention is per (row, KV head, split of ROW_SPLIT positions) — flash-decoding — and the
 // last split CTA of each (row, KV head) combines the splits into the o_proj input halves.
 
-constexpr int RA_WARPS = 8;            // warp w takes positions p0 + w + 8 j, j < ROW_SPLIT / 8
+constexpr int RA_WARPS = 16;           // warp w takes positions p0 + w + 16 j, j < ROW_SPLIT / 16
 constexpr int RA_THREADS = RA_WARPS * 32;
 constexpr int RA_PER_WARP = ROW_SPLIT / RA_WARPS;
 
