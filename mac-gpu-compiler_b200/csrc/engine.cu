@@ -661,6 +661,7 @@ void qw_free(qw_model* m) {
     cudaFree(m->pf.alo);
     cudaFree(m->pf.attp);
     cudaFree(m->pf.att_tickets);
+    cudaFree(m->pf.row_ssq);
     for (auto& g : m->graphs) cudaGraphExecDestroy(g.second);
     cudaFree(m->d_rows);
     cudaFree(m->d_btok);
@@ -799,6 +800,7 @@ int ensure_prefill(qw_model* m, size_t n, size_t start, bool logits, size_t row_
         sc.attp = m->pf.attp;
         sc.attp_cap = m->pf.attp_cap;
         sc.att_tickets = m->pf.att_tickets;
+        sc.row_ssq = m->pf.row_ssq;
         m->pf = sc;
         m->d_pf_ids = ids;
     }
@@ -916,6 +918,7 @@ int ensure_batch(qw_model* m, size_t B, int splits, size_t out_entries) {
         QW_CUDA(cudaMalloc(&m->pf.att_tickets, nb));
         QW_CUDA(cudaMemset(m->pf.att_tickets, 0, nb));
     }
+    if (!m->pf.row_ssq) QW_CUDA(cudaMalloc(&m->pf.row_ssq, 2 * (size_t)qw::pf::ROWS_MAX * qw::pf::NORM_BLOCKS_MAX * 4));
     if (out_entries > m->bout_cap) {
         uint32_t* d = nullptr;
         const size_t cap = std::max(out_entries, 2 * m->bout_cap);

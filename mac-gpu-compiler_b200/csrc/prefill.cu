@@ -210,6 +210,14 @@ __device__ __forceinline__ float add_slices(float v, const float* p, int n, size
     return v;
 }
 
+// 1 / sqrt(mean(x^2) + eps) of a row whose norm_part blocks left nblk sums of squares at ssq (added
+// in block order, so every consumer of the row gets the same scale)
+__device__ __forceinline__ float row_scale(const float* ssq, int nblk, int H, float eps) {
+    float t = 0.f;
+    for (int k = 0; k < nblk; k++) t += ssq[k];
+    return rsqrtf(t / (float)H + eps);
+}
+
 // X[t] = f32(embed[ids[t]]) (cpu_inference.rs:109-111)
 // X[t] = embed[ids[t]] (cpu_inference.rs:109-111). An id >= V (device memory the host did not
 // check: qw_prefill_device, or a device first token of a batch decode) is never read through: the
@@ -288,6 +296,37 @@ __global__ void __launch_bounds__(ROW_THREADS) norm_split(float* X, int H, const
     }
 }
 
+// Row mode's residual add + RMSNorm input over many CTAs: CTA (b, t) takes columns
+// [128 b, 128 b + 128) of row t. X[t] += the nparts slices (in slice order); A_hi/A_lo = split(X[t]
+// * gain) WITHOUT the RMSNorm scale; ssq[t][b] = the block's sum of squares (warps in order). The
+// consumers of the next projection's outputs apply the scale (row_scale): the projection is linear,
+// so W (x * gain * s) = s * W (x * gain). Rows no longer wait on one CTA's 16-slice loads and
+// block-wide reduction; the scale costs each consumer a few loads.
+constexpr int NP_THREADS = 128;
+__global__ void __launch_bounds__(NP_THREADS) norm_part(float* X, int H, const uint16_t* gain, uint16_t* hi, uint16_t* lo,
+                                                        const float* parts, int nparts, size_t part_stride, float* ssq) {
+    __shared__ float red[NP_THREADS / 32];
+    const int t = blockIdx.y, i = blockIdx.x * NP_THREADS + threadIdx.x;
+    const float g = i < H ? bf16f(gain[i]) : 0.f;  // the gains do not depend on earlier kernels
+    pdl_wait();
+    pdl_trigger();
+    float v = 0.f;
+    if (i < H) {
+        v = add_slices<KSPLIT_MAX>(X[(size_t)t * H + i], parts + (size_t)t * H + i, nparts, part_stride);
+        if (nparts) X[(size_t)t * H + i] = v;
+        split_store(v * g, hi, lo, (size_t)t * H + i);
+    }
+    float ss = v * v;
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float c = 0.f;
+        for (int w = 0; w < NP_THREADS / 32; w++) c += red[w];
+        ssq[t * NORM_BLOCKS_MAX + blockIdx.x] = c;
+    }
+}
+
 // A_hi/A_lo = split(src) over n rows of K
 __global__ void split_rows(const float* src, size_t total, uint16_t* hi, uint16_t* lo) {
     pdl_wait();
@@ -309,7 +348,10 @@ __global__ void residual_add(float* X, const float* Y, size_t total, int nparts)
 
 // h[t][i] = silu(gate) * up from the interleaved gate/up outputs Y[t][2i], Y[t][2i+1] (the sum of
 // nparts split-K slices, in order), split for the down GEMM (cpu_inference.rs:166-170, :187)
-__global__ void silu_split(const float* Y, size_t n_inter, uint16_t* hi, uint16_t* lo, int nparts) {
+// (with ssq: the gate|up inputs were left unscaled by norm_part, and row i / I's RMSNorm scale is
+// applied here, to the summed gate and up values, before the SiLU)
+__global__ void silu_split(const float* Y, size_t n_inter, uint16_t* hi, uint16_t* lo, int nparts, const float* ssq,
+                           int nblk, int I, int H, float eps) {
     pdl_wait();
     pdl_trigger();
     const size_t ps = 2 * n_inter;
@@ -318,6 +360,11 @@ __global__ void silu_split(const float* Y, size_t n_inter, uint16_t* hi, uint16_
         for (int z = 1; z < nparts; z++) {
             g += Y[z * ps + 2 * i];
             u += Y[z * ps + 2 * i + 1];
+        }
+        if (ssq) {
+            const float sc = row_scale(ssq + (i / I) * NORM_BLOCKS_MAX, nblk, H, eps);
+            g *= sc;
+            u *= sc;
         }
         split_store(g / (1.0f + __expf(-g)) * u, hi, lo, i);
     }
@@ -1052,13 +1099,15 @@ constexpr int RA_PER_WARP = ROW_SPLIT / RA_WARPS;
 // does qkv_post's work for itself. Warps 0 .. G-1 sum the split-K slices of Y for the G query heads
 // and apply q_norm + RoPE into shared memory (every split of the row recomputes them); in the
 // split holding the row's position, warps G and G+1 form that position's k (k_norm + RoPE) and v
-// and write them into the cache before the CTA's K/V loads. Same helpers, so the same values as
-// the qkv_post pass.
+// and write them into the cache before the CTA's K/V loads. Same helpers as the qkv_post pass.
+// With ssq, the q|k|v outputs come from unscaled norm_part inputs and the row's RMSNorm scale is
+// applied to the summed head values first.
 template <int G, bool FUSED>
 __global__ void __launch_bounds__(RA_THREADS) row_attention(const float* Q, const RowView* rows, int NQ, int NKV, int layer,
                                                             float scale, float* part, int splits, unsigned* tickets,
                                                             uint16_t* ahi, uint16_t* alo, const float* Y, int nparts,
-                                                            const uint16_t* qn, const uint16_t* kn, float eps) {
+                                                            const uint16_t* qn, const uint16_t* kn, float eps,
+                                                            const float* ssq, int nblk, int H) {
     static_assert(!FUSED || G + 2 <= RA_WARPS, "fused q|k|v epilogue needs G + 2 warps");
     __shared__ float sm_o[RA_WARPS][G][128];
     __shared__ float sm_m[RA_WARPS][G], sm_l[RA_WARPS][G];
@@ -1100,7 +1149,11 @@ __global__ void __launch_bounds__(RA_THREADS) row_attention(const float* Q, cons
     if constexpr (FUSED) {
         if (hw >= 0) {
             const int QKVR = (NQ + 2 * NKV) * 128;
-            const float4 v = head_sum(Y, nparts, (size_t)gridDim.x * QKVR, (size_t)b * QKVR + (size_t)hw * 128, lane);
+            float4 v = head_sum(Y, nparts, (size_t)gridDim.x * QKVR, (size_t)b * QKVR + (size_t)hw * 128, lane);
+            if (ssq) {  // the input RMSNorm's scale, left out by norm_part
+                const float sc = row_scale(ssq + b * NORM_BLOCKS_MAX, nblk, H, eps);
+                v = make_float4(v.x * sc, v.y * sc, v.z * sc, v.w * sc);
+            }
             if (hw >= NQ + NKV) {
                 reinterpret_cast<float4*>(vb + (size_t)rv.pos * 128)[lane] = v;
             } else {
@@ -1345,16 +1398,27 @@ static int forward_pass(const Weights& w, const CacheView& c, const RowView* row
     const float scale = 1.0f / sqrtf(128.0f);
     const int ks_qkv = ksplit_for(n, QKVR, H), ks_o = ksplit_for(n, H, QD), ks_gu = ksplit_for(n, 2 * I, H),
               ks_d = ksplit_for(n, H, I);
-    // residual add of the previous projection's nparts slices + RMSNorm + bf16 split, one CTA per row
+    // residual add of the previous projection's nparts slices + RMSNorm + bf16 split, one CTA per row;
+    // in a fused row step (distinct caches) the layers' two norms run as norm_part over 128-column
+    // blocks and leave the scale to the consumers (row attention for q|k|v, silu_split for gate|up)
+    const int nblk = (H + NP_THREADS - 1) / NP_THREADS;
+    const bool deferred = rows && fused && nblk <= NORM_BLOCKS_MAX && sc.row_ssq;
+    float* const ssq_a = sc.row_ssq;
+    float* const ssq_d = sc.row_ssq ? sc.row_ssq + ROWS_MAX * NORM_BLOCKS_MAX : nullptr;
     auto norm = [&](int nparts, const uint16_t* gain) {
         launch(norm_kernel(nparts), dim3(n), dim3(ROW_THREADS), 0, s, sc.X, H, gain, w.eps, sc.ahi, sc.alo, sc.Y, nparts, nH);
+    };
+    auto norm_deferred = [&](int nparts, const uint16_t* gain, float* ssq) {
+        launch(norm_part, dim3(nblk, n), dim3(NP_THREADS), 0, s, sc.X, H, gain, sc.ahi, sc.alo, (const float*)sc.Y, nparts,
+               nH, ssq);
     };
     for (int l = 0; l < w.L; l++) {
         const uint16_t* W = w.layer_w + (size_t)l * w.layer_stride;
         const uint16_t* nrm = w.layer_n + (size_t)l * w.norm_stride;
         int rc;
         // A: (the previous layer's down_proj slices into X) rmsnorm -> q|k|v
-        norm(l == 0 ? 0 : ks_d, nrm);
+        if (deferred) norm_deferred(l == 0 ? 0 : ks_d, nrm, ssq_a);
+        else norm(l == 0 ? 0 : ks_d, nrm);
         if ((rc = tc::gemm(sc.ahi, sc.alo, H, W, H, sc.Y, QKVR, n, QKVR, H, err_word, s, err, ks_qkv))) return rc;
         // B: q/k norm + RoPE, K/V into the cache, attention -> o_proj input halves
         const int items = n * (NQ + 2 * NKV);
@@ -1370,7 +1434,8 @@ static int forward_pass(const Weights& w, const CacheView& c, const RowView* row
             const uint16_t *qn = nrm + 2 * H, *kn = nrm + 2 * H + 128;
 #define QW_ROW_ATT(GQ, F)                                                                                             \
     launch(row_attention<GQ, F>, dim3(ag), dim3(RA_THREADS), 0, s, sc.Q, rows, NQ, NKV, l, scale, sc.attp, splits,    \
-           sc.att_tickets, sc.ahi, sc.alo, (const float*)sc.Y, ks_qkv, qn, kn, w.eps)
+           sc.att_tickets, sc.ahi, sc.alo, (const float*)sc.Y, ks_qkv, qn, kn, w.eps,                       \
+           deferred ? (const float*)ssq_a : (const float*)nullptr, nblk, H)
             if (G == 1) fused ? QW_ROW_ATT(1, true) : QW_ROW_ATT(1, false);
             else if (G == 2) fused ? QW_ROW_ATT(2, true) : QW_ROW_ATT(2, false);
             else fused ? QW_ROW_ATT(3, true) : QW_ROW_ATT(3, false);
@@ -1395,7 +1460,8 @@ static int forward_pass(const Weights& w, const CacheView& c, const RowView* row
         // C: o_proj (its slices go into X in the next norm)
         if ((rc = tc::gemm(sc.ahi, sc.alo, QD, W + (size_t)QKVR * H, QD, sc.Y, H, n, H, QD, err_word, s, err, ks_o))) return rc;
         // D: residual + rmsnorm -> gate|up -> silu(gate) * up
-        norm(ks_o, nrm + H);
+        if (deferred) norm_deferred(ks_o, nrm + H, ssq_d);
+        else norm(ks_o, nrm + H);
         const uint16_t* Wgu = W + (size_t)QKVR * H + (size_t)H * QD;
         const uint16_t* Wd = Wgu + (size_t)2 * I * H;
         if (ks_gu == 1 && n > tc::SK_NB && (size_t)I * 2 <= (size_t)QD * 4) {
@@ -1409,7 +1475,8 @@ static int forward_pass(const Weights& w, const CacheView& c, const RowView* row
             if ((rc = tc::gemm(hh, hl, I, Wd, I, sc.Y, H, n, H, I, err_word, s, err, ks_d))) return rc;
         } else {
             if ((rc = tc::gemm(sc.ahi, sc.alo, H, Wgu, H, sc.Y, 2 * I, n, 2 * I, H, err_word, s, err, ks_gu))) return rc;
-            launch(silu_split, dim3(grid_for((size_t)n * I)), dim3(256), 0, s, sc.Y, (size_t)n * I, sc.ahi, sc.alo, ks_gu);
+            launch(silu_split, dim3(grid_for((size_t)n * I)), dim3(256), 0, s, sc.Y, (size_t)n * I, sc.ahi, sc.alo, ks_gu,
+                   deferred ? (const float*)ssq_d : (const float*)nullptr, nblk, I, H, w.eps);
             // E: down (its slices go into X in the next layer's norm)
             if ((rc = tc::gemm(sc.ahi, sc.alo, I, Wd, I, sc.Y, H, n, H, I, err_word, s, err, ks_d))) return rc;
         }

@@ -65,7 +65,11 @@ struct Scratch {
     size_t attp_cap = 0;       // floats attp holds
     size_t ycap = 0;           // floats Y holds
     unsigned* att_tickets = nullptr;  // row mode: [ROWS_MAX][NKV] split arrivals, zero between launches
+    float* row_ssq = nullptr;  // row mode: [2][ROWS_MAX][NORM_BLOCKS_MAX] per-block sums of squares of the norms
 };
+
+// row mode: the most 128-column blocks a hidden row splits into for the block-parallel norm
+constexpr int NORM_BLOCKS_MAX = 64;
 
 // floats of Scratch::Y a pass over n rows needs (largest ksplit x n x N over the four GEMMs)
 size_t y_floats(int n, int H, int I, int NQ, int NKV);
