@@ -128,6 +128,23 @@ def test_decode_is_deterministic(mid_model_path):
     assert runs[0][1] == runs[1][1]
 
 
+def test_traced_and_untraced_kernel_instances_agree(mid_model_path):
+    """Tracing launches the kernel instance with the timeline stamps compiled in; the stamps are its
+    only difference, so its logits and tokens are bit-identical to the untraced instance's."""
+    gpu = ci.CudaModel.load_model(mid_model_path)
+    ids = randmodel.prompt_ids(24, gpu.config.vocab_size, seed=9)
+    runs = []
+    for traced in (False, True):
+        gpu.set_trace(traced)
+        cache = ci.CudaKVCache(gpu, 64)
+        lg = [gpu.forward(t, p, cache) for p, t in enumerate(ids)]
+        toks = gpu.decode(co.argmax(lg[-1]), len(ids), 12, cache)
+        runs.append((np.stack(lg), toks))
+    gpu.set_trace(False)
+    assert np.array_equal(runs[0][0], runs[1][0])
+    assert runs[0][1] == runs[1][1]
+
+
 def test_long_context_split_attention(mid_model_path):
     # config 2's shape of work: a 2048-token prompt fed token by token, then decode; the
     # attention splits each KV head's 2048+ positions over 18 CTAs and several ring slots each
