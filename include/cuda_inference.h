@@ -176,6 +176,17 @@ int qw_num_ctas(const qw_model* model);
 #define QW_DECODER_CLUSTER 1
 int qw_decoder_kind(const qw_model* model);
 
+/* How qw_decode_batch runs batches of at most 8 rows (no reference counterpart: the reference
+ * decodes one sequence per engine, metal_inference.rs:286-387). QW_BATCH_ROWS, the default: a
+ * captured graph of row-mode kernels per step (skinny tensor-core GEMMs, row attention).
+ * QW_BATCH_PERSISTENT, when the environment sets QW_BATCH_DECODER=persistent at load and the
+ * model's shapes fit: one persistent launch for all steps, streaming the weights once per step
+ * for every row (batch_kernel.cuh). Batches of 9 to 16 rows always run in row mode. -1 for a null
+ * model. */
+#define QW_BATCH_ROWS 0
+#define QW_BATCH_PERSISTENT 1
+int qw_batch_decoder_kind(qw_model* model);
+
 /* The model's own cudaStream_t (what qw_forward/qw_decode run on), e.g. to bracket them with
  * events. */
 void* qw_model_stream(const qw_model* model);

@@ -22,6 +22,7 @@
 #include "../../include/cuda_inference.h"
 #include "cluster_decode.cuh"
 #include "decode_kernel.cuh"
+#include "batch_kernel.cuh"
 #include "model_file.h"
 #include "prefill.h"
 
@@ -139,6 +140,18 @@ struct qw_model {
     int nctas = 0;    // grid of the decode kernel in use
     int kind = 0;     // QW_DECODER_GRID (decode_kernel.cuh) or QW_DECODER_CLUSTER (cluster_decode.cuh)
     bool generic = true;  // grid kernel: the shapes need the generic GEMV routine (full_segment_shapes)
+    // persistent batch kernel (batch_kernel.cuh): 0 unchecked, 1 usable, -1 not for this model;
+    // bk_use: qw_decode_batch runs it for batches of at most 8 rows (QW_BATCH_DECODER)
+    int bk_state = 0;
+    bool bk_use = false;
+    uint8_t* d_bk = nullptr;     // its scratch: tagged x, q|k|v, h, att, partials, then argmax partials and flags
+    u64 *bk_x = nullptr, *bk_qkv = nullptr, *bk_h = nullptr, *bk_att = nullptr, *bk_apart = nullptr, *bk_flags = nullptr;
+    float* bk_am_val = nullptr;
+    unsigned* bk_am_idx = nullptr;
+    int* bk_nan0 = nullptr;
+    size_t bk_tagged_bytes = 0;
+    unsigned bk_epoch = 0;
+    int bk_S = 1;
     bool cl_coop = true;          // cluster launches also ask for co-residency (cooperative) until refused
     uint16_t* d_clw = nullptr;    // cluster kernel: o_proj and down_proj repacked per (layer, cluster, rank)
     u64 *d_po = nullptr, *d_pd = nullptr;  // cluster kernel: [8][hidden] partial residual updates (tagged words)
@@ -552,6 +565,8 @@ int qw_load(const char* path, int device, qw_model** out) {
     {
         const bool shape = H == (uint64_t)cl::H && I == (uint64_t)cl::I && c.heads == (uint64_t)cl::NQ &&
                            c.kv_heads == (uint64_t)cl::NKV && c.head_dim == (uint64_t)cl::HD;
+        const char* bd = std::getenv("QW_BATCH_DECODER");
+        m->bk_use = bd && std::strcmp(bd, "persistent") == 0;
         const char* dec = std::getenv("QW_DECODER");
         if (dec && std::strcmp(dec, "cluster") == 0) {
             if (!shape || std::getenv("QW_CTAS"))
@@ -650,6 +665,7 @@ void qw_free(qw_model* m) {
     if (m->stream) cudaStreamSynchronize(m->stream);
     cudaFree(m->d_weights);
     cudaFree(m->d_clw);
+    cudaFree(m->d_bk);
     cudaFree(m->d_scratch);
     cudaFree(m->d_tok);
     cudaFree(m->d_trace);
@@ -688,6 +704,17 @@ uint64_t qw_weight_bytes_per_token(const qw_model* m) { return m ? m->wbytes : 0
 int qw_num_ctas(const qw_model* m) { return m ? m->nctas : 0; }
 
 int qw_decoder_kind(const qw_model* m) { return m ? m->kind : -1; }
+
+namespace {
+int bk_setup(qw_model* m);  // below, with the batch decode host code
+}
+
+int qw_batch_decoder_kind(qw_model* m) {
+    if (!m) return -1;
+    if (!m->bk_use) return QW_BATCH_ROWS;
+    if (cudaSetDevice(m->device) != cudaSuccess || bk_setup(m) != QW_OK) return -1;
+    return m->bk_state == 1 ? QW_BATCH_PERSISTENT : QW_BATCH_ROWS;
+}
 
 void* qw_model_stream(const qw_model* m) { return m ? static_cast<void*>(m->stream) : nullptr; }
 
@@ -974,6 +1001,115 @@ int row_graph(qw_model* m, int kind, int B, int splits, uint32_t* out, int* ew, 
     return QW_OK;
 }
 
+// The persistent batch kernel (batch_kernel.cuh), set up on first use: the shapes it covers, its
+// shared-memory plan on this GPU, and its scratch. bk_state ends 1 (usable) or -1.
+int bk_setup(qw_model* m) {
+    if (m->bk_state != 0) return QW_OK;
+    m->bk_state = -1;
+    const ModelConfig& c = m->cfg;
+    const uint64_t H = c.hidden, I = c.inter, QD = c.heads * c.head_dim, KVD = c.kv_heads * c.head_dim;
+    const uint64_t QKVR = QD + 2 * KVD;
+    const int nctas = m->nctas;
+    if (m->kind != QW_DECODER_GRID || c.head_dim != 128 || H != (uint64_t)bk::KBLK || QD % bk::KBLK || I % bk::KBLK ||
+        c.heads % c.kv_heads || c.heads / c.kv_heads > (uint64_t)bk::MAX_G)
+        return QW_OK;
+    auto ceil_div = [](uint64_t a, uint64_t b) { return (a + b - 1) / b; };
+    auto max_rows = [&](uint64_t rows, uint64_t unit) { return unit * ceil_div(rows / unit, nctas); };
+    const uint64_t uq = QKVR % 8 == 0 && QKVR / 8 >= (uint64_t)nctas ? 8 : 1;
+    auto fits = [&](uint64_t rows, uint64_t K) {
+        const uint64_t rpp = bk::SLOT_BYTES / (2 * K);
+        return rows <= (uint64_t)bk::MAX_ROWS && rpp >= 1 && ceil_div(rows, rpp) <= (uint64_t)bk::NSLOT;
+    };
+    if (!fits(max_rows(QKVR, uq), H) || !fits(max_rows(H, 8), QD) || !fits(2 * max_rows(I, 8), H) || !fits(max_rows(H, 8), I))
+        return QW_OK;
+    if (cudaFuncSetAttribute(bk::batch_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bk::DYN_BYTES) !=
+        cudaSuccess) {
+        (void)cudaGetLastError();
+        return QW_OK;
+    }
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, bk::batch_decode_kernel, bk::NTHREADS, bk::DYN_BYTES) !=
+            cudaSuccess || per_sm < 1) {
+        (void)cudaGetLastError();
+        return QW_OK;
+    }
+    const size_t G = c.heads / c.kv_heads;
+    const size_t nb = bk::NB;
+    const size_t tagged = (nb * H + nb * QKVR + nb * I + nb * QD + nb * c.kv_heads * bk::MAX_S * G * bk::APART) * 8;
+    const size_t rest = (size_t)nctas * nb * 8 + 64 + (size_t)nctas * 8;
+    if (cudaMalloc(&m->d_bk, tagged + rest) != cudaSuccess) return set_err(QW_ERR_NOMEM, "batch kernel scratch allocation failed");
+    QW_CUDA(cudaMemset(m->d_bk, 0, tagged + rest));
+    u64* t = reinterpret_cast<u64*>(m->d_bk);
+    m->bk_x = t;
+    m->bk_qkv = m->bk_x + nb * H;
+    m->bk_h = m->bk_qkv + nb * QKVR;
+    m->bk_att = m->bk_h + nb * I;
+    m->bk_apart = m->bk_att + nb * QD;
+    m->bk_tagged_bytes = tagged;
+    uint8_t* r = m->d_bk + tagged;
+    m->bk_am_val = reinterpret_cast<float*>(r);
+    m->bk_am_idx = reinterpret_cast<unsigned*>(r + (size_t)nctas * nb * 4);
+    m->bk_nan0 = reinterpret_cast<int*>(r + (size_t)nctas * nb * 8);
+    m->bk_flags = reinterpret_cast<u64*>(r + (size_t)nctas * nb * 8 + 64);
+    m->bk_state = 1;
+    return QW_OK;
+}
+
+// one launch of the persistent batch kernel over `rows` (validated by batch_rows), first tokens in
+// m->d_btok, tokens recorded into m->d_bout [steps][B]
+int bk_launch(qw_model* m, qw_cache* const* caches, size_t B, const size_t* start_pos, size_t steps, cudaStream_t s) {
+    const ModelConfig& g = m->cfg;
+    bk::BParams p{};
+    p.layer_w = m->d_layer_w;
+    p.layer_n = m->d_layer_n;
+    p.final_norm = m->d_final_norm;
+    p.embed = m->d_embed;
+    p.lm_head = m->d_lm_head;
+    for (size_t b = 0; b < B; b++) {
+        p.kc[b] = caches[b]->d_k;
+        p.vc[b] = caches[b]->d_v;
+        p.rope[b] = caches[b]->d_rope;
+        p.max_seq[b] = (int)caches[b]->max_seq;
+        p.pos0[b] = (int)start_pos[b];
+    }
+    p.x = m->bk_x;
+    p.qkv = m->bk_qkv;
+    p.hbuf = m->bk_h;
+    p.att = m->bk_att;
+    p.apart = m->bk_apart;
+    p.am_val = m->bk_am_val;
+    p.am_idx = m->bk_am_idx;
+    p.nan0 = m->bk_nan0;
+    p.flags = m->bk_flags;
+    p.err = m->d_err;
+    p.tok_in = m->d_btok;
+    p.tok_out = m->d_bout;
+    p.layer_stride = m->layer_stride;
+    p.norm_stride = m->norm_stride;
+    p.H = (int)g.hidden;
+    p.I = (int)g.inter;
+    p.L = (int)g.layers;
+    p.NQ = (int)g.heads;
+    p.NKV = (int)g.kv_heads;
+    p.V = (int)g.vocab;
+    p.nb = (int)B;
+    p.steps = (int)steps;
+    const unsigned e = ++m->bk_epoch;
+    if ((e & 0xFFFu) == 0) QW_CUDA(cudaMemsetAsync(m->d_bk, 0, m->bk_tagged_bytes, s));  // tags would repeat
+    p.epoch = e;
+    p.eps = g.eps;
+    p.scale = 1.0f / sqrtf((float)g.head_dim);  // cpu_inference.rs:144
+    p.S = std::max(1, std::min(bk::MAX_S, m->nctas / (int)(B * g.kv_heads)));
+    p.min_chunk = m->min_chunk;
+    p.timeout_ns = m->timeout_ns;
+    p.trace = m->d_trace;  // the decode kernel's timeline buffer and layout, when tracing is on
+    void* args[] = {&p};
+    const cudaError_t ce = cudaLaunchCooperativeKernel((const void*)bk::batch_decode_kernel, dim3(m->nctas), dim3(bk::NTHREADS),
+                                                       args, bk::DYN_BYTES, s);
+    if (ce != cudaSuccess) return cuda_err(ce, "batch decode kernel launch");
+    return QW_OK;
+}
+
 // stream-ordered batch decode: rows from host positions, first tokens already in m->d_btok; the
 // step graph records tokens into m->d_bout ([steps][B]), so one capture serves every batch of the
 // same shape
@@ -983,6 +1119,10 @@ int batch_decode_launch(qw_model* m, qw_cache* const* caches, size_t B, const si
     int splits = 0;
     if (int e = batch_rows(m, caches, B, start_pos, steps, rows, splits)) return e;
     if (int e = ensure_batch(m, B, splits, steps * B)) return e;
+    if (m->bk_use && B <= (size_t)bk::NB) {
+        if (int e = bk_setup(m)) return e;
+        if (m->bk_state == 1) return bk_launch(m, caches, B, start_pos, steps, s);
+    }
     int* ew = qw::device_err_word_for(m->device);
     if (!ew) return set_err(QW_ERR_NOMEM, "error word allocation failed");
     cudaGraphExec_t g = nullptr;
@@ -1041,6 +1181,7 @@ int qw_decode_batch(qw_model* m, qw_cache* const* caches, size_t B, const uint32
     QW_CUDA(cudaMemcpyAsync(&h, ew, sizeof(int), cudaMemcpyDeviceToHost, s));
     QW_CUDA(cudaStreamSynchronize(s));
     if (h) return set_err(QW_ERR_DEVICE_TIMEOUT, "decode_batch: a GEMM pipeline wait expired on the device");
+    if (int e = check_device_err(m)) return e;  // the persistent batch kernel's error word
     for (size_t b = 0; b < B; b++)
         for (size_t i = 0; i < steps; i++) tokens_out[b * steps + i] = rec[i * B + b];
     return QW_OK;

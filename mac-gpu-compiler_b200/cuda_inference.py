@@ -103,6 +103,7 @@ def lib() -> ctypes.CDLL:
             "qw_cache_read": (i32, [vp, sz, sz, vp, vp]),
             "qw_num_ctas": (i32, [vp]),
             "qw_decoder_kind": (i32, [vp]),
+            "qw_batch_decoder_kind": (i32, [vp]),
             "qw_model_stream": (vp, [vp]),
             "qw_trace_stride": (sz, [vp]),
             "qw_set_trace": (i32, [vp, i32]),
@@ -163,6 +164,12 @@ class CudaModel:
     def decoder_kind(self) -> str:
         """'grid' (one CTA per SM, the default) or 'cluster' (8 clusters of 8 CTAs, QW_DECODER=cluster)."""
         return {0: "grid", 1: "cluster"}.get(int(lib().qw_decoder_kind(self._h)), "?")
+
+    @property
+    def batch_decoder_kind(self) -> str:
+        """'rows' (captured row-mode step graphs, the default) or 'persistent' (one persistent launch
+        for batches of at most 8 rows: QW_BATCH_DECODER=persistent at load, where the shapes fit)."""
+        return {0: "rows", 1: "persistent"}.get(int(lib().qw_batch_decoder_kind(self._h)), "?")
 
     @property
     def stream(self) -> int:
