@@ -20,6 +20,11 @@
 //   * attention: one CTA per (row, KV head, chunk) item, each row over its own cache;
 //   * lm_head: per weight-row piece, each warp group combines its 4 warps' sums through a
 //     double-buffered shared-memory stage and keeps a running argmax per row.
+//
+// Measured on B200 (Qwen3-0.6B geometry, 8 rows): 1.7 ms per step against 0.99 ms for the row-mode
+// graph, so qw_decode_batch runs it only when asked (QW_BATCH_DECODER=persistent). Its GEMV
+// phases take as long for one row as for eight: each weight row costs about 100 instructions per
+// warp (the 64 FMAs per lane and the 9-shuffle reduction), which bounds the phase, not its bytes.
 #pragma once
 #include <cstddef>
 #include <cstdint>
