@@ -62,3 +62,20 @@ def test_workload_config_is_engine_free():
         c = bench.workload_config(name, 4)
         assert c["workload"].startswith("configs[")
         assert "engine" not in c and "impl" not in c
+
+
+def test_clock_summary_flags_throttle_reasons():
+    """The clock record the bench line carries: median SM clock under load, the max clock, and every
+    throttle reason seen active in any sample (nvidia-smi csv rows, as the sampler collects them)."""
+    cs = bench.ClockSampler(0)
+    cs.lines = [
+        "0, 1965, 1965, 700.1, 0x0000000000000000, Not Active, Not Active, Not Active, Not Active",
+        "0, 1950, 1965, 980.2, 0x0000000000000004, Not Active, Not Active, Not Active, Active",
+        "0, 1965, 1965, 990.0, 0x0000000000000000, Not Active, Not Active, Not Active, Not Active",
+        "garbage line",
+    ]
+    got = cs.summary()
+    assert got["sm_mhz"] == 1965.0 and got["sm_max_mhz"] == 1965.0 and got["samples"] == 3
+    assert got["reasons"] == ["sw_power_cap"]
+    cs.lines = []
+    assert cs.summary()["sm_mhz"] is None
