@@ -98,6 +98,8 @@ struct BParams {
     int S, min_chunk;
     long long timeout_ns;
     u64* trace;                  // [grid][14 L + 4] globaltimer stamps of step 0 (the decode kernel's layout), or null
+    int stall_cta;               // test hook (-1: off): this CTA never raises its first end-of-step flag,
+                                 // so every CTA's bounded barrier wait runs out and the launch reports it
 };
 
 struct BLoop {
@@ -560,7 +562,7 @@ public:
         const BParams& p = bk_sm.prm;
         named_bar_sync(1, NCT);
         const u64 target = ((u64)p.epoch << 32) | done;
-        if (tid() == 0) {
+        if (tid() == 0 && !(cta() == p.stall_cta && done == 1)) {
             fence_acq_rel_gpu();
             st_relaxed_u64(p.flags + cta(), target);
         }

@@ -1103,6 +1103,8 @@ int bk_launch(qw_model* m, qw_cache* const* caches, size_t B, const size_t* star
     p.min_chunk = m->min_chunk;
     p.timeout_ns = m->timeout_ns;
     p.trace = m->d_trace;  // the decode kernel's timeline buffer and layout, when tracing is on
+    p.stall_cta = m->stall_cta;
+    m->stall_cta = -1;
     void* args[] = {&p};
     const cudaError_t ce = cudaLaunchCooperativeKernel((const void*)bk::batch_decode_kernel, dim3(m->nctas), dim3(bk::NTHREADS),
                                                        args, bk::DYN_BYTES, s);

@@ -137,3 +137,24 @@ def test_persistent_batch_bad_first_token(tiny_model_path, monkeypatch):
     with pytest.raises(ci.QwError) as e:
         gm.decode_batch([4, gm.config.vocab_size], [3, 3], 2, cs)
     assert e.value.code == ci.QW_ERR_ARG
+
+
+def test_persistent_batch_expired_wait_is_reported_and_recovers(mid_model_path, monkeypatch):
+    """The batch kernel's bounded waits, as for the decode kernels: with QW_TEST_STALL_CTA one CTA
+    never raises its first end-of-step flag, every CTA's barrier wait expires (QW_WAIT_TIMEOUT_MS
+    at its 50 ms floor), and the launch ends on its own with QW_ERR_DEVICE_TIMEOUT. The next
+    batch decode on the same handle gives the same tokens as a model that never stalled."""
+    monkeypatch.setenv("QW_BATCH_DECODER", "persistent")
+    ref = ci.CudaModel.load_model(mid_model_path)
+    monkeypatch.setenv("QW_TEST_STALL_CTA", "7")
+    monkeypatch.setenv("QW_WAIT_TIMEOUT_MS", "50")
+    gm = ci.CudaModel.load_model(mid_model_path)
+    assert gm.batch_decoder_kind == "persistent"
+    lens = [9, 17]
+    gcs, _, _ = _prefilled(gm, None, lens, 12)
+    with pytest.raises(ci.QwError) as e:
+        gm.decode_batch([3, 4], lens, 4, gcs)
+    assert e.value.code == ci.QW_ERR_DEVICE_TIMEOUT
+    gcs, _, _ = _prefilled(gm, None, lens, 12)
+    rcs, _, _ = _prefilled(ref, None, lens, 12)
+    assert (gm.decode_batch([3, 4], lens, 6, gcs) == ref.decode_batch([3, 4], lens, 6, rcs)).all()
