@@ -12,6 +12,9 @@ Fixtures written next to this script (float32 logits from transformers):
   hf_mid.npz    Qwen3-0.6B per-layer shapes with 3 layers, 4 positions, full logits
   hf_full.npz   the full Qwen3-0.6B geometry, 3 positions: top-16 ids/values and 512 logits at
                 fixed seeded indices (full rows would be 1.8 MB)
+  hf_*_long.npz longer prompts in the same sampled form (top-16 and 256 sampled logits per
+                position, plus the top-2 margin): tiny 128, mid 48 and full 24 positions, so the
+                RoPE table and the attention softmax are pinned over longer contexts
 
 Run from the repo root:  python tests/golden/make_golden.py
 This script needs ``transformers`` (importable in the build container); the tests that read the
@@ -73,5 +76,27 @@ def main() -> None:
             print(geometry, "->", HERE / name)
 
 
+LONG_SPECS = {"tiny": 128, "mid": 48, "qwen3-0.6b": 24}
+N_SAMPLE_LONG = 256
+
+
+def main_long() -> None:
+    torch.set_num_threads(8)
+    for geometry, n in LONG_SPECS.items():
+        vocab = randmodel.GEOMETRIES[geometry]["vocab_size"]
+        ids = randmodel.prompt_ids(n, vocab, seed=2)
+        logits = hf_logits(geometry, ids)
+        rng = np.random.Generator(np.random.PCG64(11))
+        idx = np.sort(rng.choice(vocab, min(N_SAMPLE_LONG, vocab), replace=False)).astype(np.int64)
+        top_ids = np.argsort(-logits, axis=1, kind="stable")[:, :TOPK].astype(np.int64)
+        top = np.take_along_axis(logits, top_ids, 1).astype(np.float32)
+        name = "hf_" + ("full" if geometry == "qwen3-0.6b" else geometry) + "_long.npz"
+        np.savez(HERE / name, ids=np.array(ids, np.int64), sample_idx=idx, sample_logits=logits[:, idx].astype(np.float32),
+                 top_ids=top_ids, top_logits=top, argmax=logits.argmax(1).astype(np.int64),
+                 margin=(top[:, 0] - top[:, 1]).astype(np.float32))
+        print(geometry, "->", HERE / name)
+
+
 if __name__ == "__main__":
     main()
+    main_long()

@@ -41,6 +41,24 @@ def test_oracle_matches_transformers_full_geometry(full_model_path):
         assert co.argmax(lg) == int(d["argmax"][pos])
 
 
+@pytest.mark.parametrize("geometry,fixture", [("tiny", "hf_tiny_long.npz"), ("mid", "hf_mid_long.npz"),
+                                              ("full", "hf_full_long.npz")])
+def test_oracle_matches_transformers_longer_prompts(geometry, fixture, request):
+    """Longer prompts (128, 48 and 24 positions): the oracle's per-position logits against
+    transformers' at 256 sampled vocabulary ids and the top 16, and the same argmax wherever
+    transformers' top-2 margin leaves room for the tolerance."""
+    path = request.getfixturevalue(f"{geometry}_model_path")
+    d = np.load(GOLDEN / fixture)
+    m = co.Model.load_model(path)
+    cache = co.KVCache(m)
+    for pos, tok in enumerate(d["ids"]):
+        lg = m.forward(int(tok), pos, cache)
+        assert np.abs(lg[d["sample_idx"]] - d["sample_logits"][pos]).max() < HF_TOL, pos
+        assert np.abs(lg[d["top_ids"][pos]] - d["top_logits"][pos]).max() < HF_TOL, pos
+        if d["margin"][pos] > 2 * HF_TOL:
+            assert co.argmax(lg) == int(d["argmax"][pos]), pos
+
+
 def test_weight_bytes_rule_matches_reference(full_model_path):
     # tests/mbu.rs:19-30 on the Qwen3-0.6B geometry gives the reference's published
     # 1,192,101,888 B/token (mlx_baseline/results/engine_metal_m1_ai.json:140)
