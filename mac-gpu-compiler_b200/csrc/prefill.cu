@@ -837,6 +837,28 @@ attention_tc(const float* Q, float* att, const float* Kc, const float* Vc, int n
     const int t0 = tile * QT, ntok = min(QT, n - t0);
     const int last = min(start + t0 + ntok - 1, c_end * PC - 1);
 
+    const float* kb = Kc + head_stride_l + (size_t)g * max_seq * 128;
+    const float* vb = Vc + head_stride_l + (size_t)g * max_seq * 128;
+    // K and V rows of a chunk: warp w takes positions 8 w + (lane & 7), lane group lane >> 3 dims
+    // 4 (lane >> 3) + 16 u, u < 8 (8 rows x 64 contiguous bytes per load). The next chunk's rows are
+    // loaded into registers while this chunk's S MMA and softmax run, so their global-load latency
+    // is off the chunk's critical path. The first chunk's loads go out before the Q tile's.
+    const int kv_p = 8 * warp + (lane & 7), dg = lane >> 3;
+    float4 kv[8], vv[8];
+    auto load_kv = [&](int p0n) {
+        const int npn = min(PC, last + 1 - p0n);
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            kv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            vv[u] = kv[u];
+            if (kv_p < npn) {
+                kv[u] = __ldcg(reinterpret_cast<const float4*>(kb + (size_t)(p0n + kv_p) * 128) + dg + 4 * u);
+                vv[u] = __ldcg(reinterpret_cast<const float4*>(vb + (size_t)(p0n + kv_p) * 128) + dg + 4 * u);
+            }
+        }
+    };
+    if (c_begin * PC <= last) load_kv(c_begin * PC);
+
     if (tid == 0) {
         mbar_init(&bar_s, 1);
         mbar_init(&bar_o, 1);
@@ -875,8 +897,6 @@ attention_tc(const float* Q, float* att, const float* Kc, const float* Vc, int n
     const int row = 32 * (warp & 3) + lane, half = warp >> 2;
     const uint32_t lane_base = (uint32_t)(32 * (warp & 3)) << 16;
     const uint32_t idesc_s = tc::idesc_bf16_f32(128, 64), idesc_o = tc::idesc_bf16_f32(128, 128);
-    const float* kb = Kc + head_stride_l + (size_t)g * max_seq * 128;
-    const float* vb = Vc + head_stride_l + (size_t)g * max_seq * 128;
     const int pos_r = start + t0 + row / G;
     float m_run = -INFINITY, l_run = 0.f;
     int chunk = 0;
@@ -890,20 +910,8 @@ attention_tc(const float* Q, float* att, const float* Kc, const float* Vc, int n
             break;
         }
         {
-            // K and V rows of the chunk: warp w takes positions 8 w + (lane & 7), lane group lane >> 3
-            // dims 4 (lane >> 3) + 16 u, u < 8 (8 rows x 64 contiguous bytes per load). K goes out as
-            // 8-byte row pieces, V^T as single elements (dims x positions).
-            const int p = 8 * warp + (lane & 7), dg = lane >> 3;
-            float4 kv[8], vv[8];
-#pragma unroll
-            for (int u = 0; u < 8; u++) {
-                kv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-                vv[u] = kv[u];
-                if (p < np) {
-                    kv[u] = __ldcg(reinterpret_cast<const float4*>(kb + (size_t)(p0 + p) * 128) + dg + 4 * u);
-                    vv[u] = __ldcg(reinterpret_cast<const float4*>(vb + (size_t)(p0 + p) * 128) + dg + 4 * u);
-                }
-            }
+            // K goes out as 8-byte row pieces, V^T as single elements (dims x positions)
+            const int p = kv_p;
 #pragma unroll
             for (int u = 0; u < 8; u++) {
                 const int d0 = 4 * (dg + 4 * u);
@@ -931,8 +939,9 @@ attention_tc(const float* Q, float* att, const float* Kc, const float* Vc, int n
                 tc::mma_bf16(tS, ql, kh, idesc_s, 1u);
             }
             tc::mma_commit(&bar_s);
-            ok = tc::bounded_wait(&bar_s, chunk & 1, &abort_flag);
         }
+        if (p0 + PC <= last) load_kv(p0 + PC);
+        if (tid == 0) ok = tc::bounded_wait(&bar_s, chunk & 1, &abort_flag);
         if (!__syncthreads_and(ok && !abort_flag)) {
             ok = false;
             break;
