@@ -160,7 +160,11 @@ gemm_bf16x2_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_con
     // 1024-byte aligned ring (the 128-byte swizzle atom spans 8 rows x 128 bytes)
     uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    // tiles in launch order with the M tile fastest (gridDim.y M tiles, gridDim.x N tiles): the CTAs
+    // that share a weight tile start together, so a weight matrix larger than L2 (the lm_head's
+    // 311 MB) is read from HBM once instead of once per M tile
+    const int lin = (int)(blockIdx.x + blockIdx.y * gridDim.x);
+    const int m0 = (lin % (int)gridDim.y) * BM, n0 = (lin / (int)gridDim.y) * BN;
     // split-K: CTA z of gridDim.z covers K blocks [kb0, kb0 + nkb) and writes its own output slice
     const int nkb_all = args.K / BK;
     const int kb0 = (int)((long long)nkb_all * blockIdx.z / gridDim.z);
