@@ -192,11 +192,25 @@ class CudaModel:
         _check(lib().qw_forward(self._h, cache._h, token, pos, out.ctypes.data))
         return out
 
-    def prefill(self, ids, start_pos: int, cache: "CudaKVCache", logits: bool = True) -> np.ndarray | None:
+    def prefill(self, ids, start_pos: int, cache: "CudaKVCache", logits: bool = True,
+                out: np.ndarray | None = None) -> np.ndarray | None:
         """One batched pass over the prompt ids at positions start_pos.. (qw_prefill): fills the KV
-        cache like len(ids) forward calls; returns the [len(ids), vocab] logits when asked."""
+        cache like len(ids) forward calls; returns the [len(ids), vocab] logits when asked.
+
+        `out`, if given, is a C-contiguous float32 [len(ids), vocab] array that receives the logits
+        (and is returned) instead of a new array. A caller that decodes many prompts can keep one,
+        for instance the numpy view of a page-locked torch tensor, which the copy then reaches by
+        one DMA; a new or pageable array goes through the library's pinned stages."""
         a = np.ascontiguousarray(np.asarray(ids, dtype=np.uint32))
-        out = np.empty((a.size, self.config.vocab_size), np.float32) if logits else None
+        if out is not None:
+            if not logits:
+                raise ValueError("out given with logits=False")
+            if (out.dtype != np.float32 or out.shape != (a.size, self.config.vocab_size)
+                    or not out.flags.c_contiguous or not out.flags.writeable):
+                raise ValueError(f"out must be a writeable C-contiguous float32 array of shape "
+                                 f"({a.size}, {self.config.vocab_size})")
+        elif logits:
+            out = np.empty((a.size, self.config.vocab_size), np.float32)
         _check(lib().qw_prefill(self._h, cache._h, a.ctypes.data, a.size, start_pos,
                                 out.ctypes.data if out is not None else None))
         return out

@@ -107,3 +107,31 @@ def test_prefill_device_bad_id_is_reported(tiny_model_path):
     ids = [3, 1, 5, 2]
     lg = m.prefill(ids, 0, ci.CudaKVCache(m, 16))
     assert np.isfinite(lg).all()
+
+
+def test_prefill_logits_copy_paths_agree(full_model_path):
+    """qw_prefill hands the logits to host memory in three ways: one DMA into a page-locked
+    buffer, and, for pageable memory, two pinned stages that host threads copy out (into a new
+    array, whose pages those threads touch first, or into an array written before). Each gives
+    exactly the bytes that the device-side call leaves in device memory."""
+    m = ci.CudaModel.load_model(full_model_path)
+    V = m.config.vocab_size
+    n = 200  # 121.5 MB of logits: seven full 16 MB stages and a partial one
+    ids = randmodel.prompt_ids(n, V, seed=9)
+    fresh = m.prefill(ids, 0, ci.CudaKVCache(m, n))
+    reused = np.full((n, V), np.nan, np.float32)
+    assert m.prefill(ids, 0, ci.CudaKVCache(m, n), out=reused) is reused
+    pinned = torch.empty((n, V), dtype=torch.float32).pin_memory().numpy()
+    pinned.fill(np.nan)
+    assert m.prefill(ids, 0, ci.CudaKVCache(m, n), out=pinned) is pinned
+    d_ids = torch.tensor(ids, dtype=torch.int32, device="cuda:0")
+    d_lg = torch.empty((n, V), dtype=torch.float32, device="cuda:0")
+    m.prefill_device(ci.CudaKVCache(m, n), d_ids.data_ptr(), n, 0, d_lg.data_ptr())
+    m.sync()
+    want = d_lg.cpu().numpy()
+    for got in (fresh, reused, pinned):
+        assert np.array_equal(got, want)
+    with pytest.raises(ValueError):
+        m.prefill(ids, 0, ci.CudaKVCache(m, n), out=np.empty((n, V), np.float64))
+    with pytest.raises(ValueError):
+        m.prefill(ids, 0, ci.CudaKVCache(m, n), out=np.empty((n - 1, V), np.float32))
