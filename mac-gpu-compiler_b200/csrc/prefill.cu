@@ -839,11 +839,14 @@ attention_tc(const float* Q, float* att, const float* Kc, const float* Vc, int n
 
     const float* kb = Kc + head_stride_l + (size_t)g * max_seq * 128;
     const float* vb = Vc + head_stride_l + (size_t)g * max_seq * 128;
-    // K and V rows of a chunk: warp w takes positions 8 w + (lane & 7), lane group lane >> 3 dims
-    // 4 (lane >> 3) + 16 u, u < 8 (8 rows x 64 contiguous bytes per load). The next chunk's rows are
-    // loaded into registers while this chunk's S MMA and softmax run, so their global-load latency
-    // is off the chunk's critical path. The first chunk's loads go out before the Q tile's.
+    // K and V rows of a chunk, 8 rows x 64 contiguous bytes per warp load. K: warp w takes position
+    // 8 w + (lane & 7), lane group lane >> 3 dims 4 (lane >> 3) + 16 u, u < 8. V: thread t takes
+    // positions 8 (t & 7) .. + 7 of dims 4 (t >> 3) .. + 3, so that each dim's 8 positions leave as
+    // one 16-byte chunk of the transposed tile. The next chunk's rows are loaded into registers
+    // while this chunk's S MMA and softmax run, so their global-load latency is off the chunk's
+    // critical path. The first chunk's loads go out before the Q tile's.
     const int kv_p = 8 * warp + (lane & 7), dg = lane >> 3;
+    const int v_p = 8 * (tid & 7), v_d = 4 * (tid >> 3);
     float4 kv[8], vv[8];
     auto load_kv = [&](int p0n) {
         const int npn = min(PC, last + 1 - p0n);
@@ -851,10 +854,8 @@ attention_tc(const float* Q, float* att, const float* Kc, const float* Vc, int n
         for (int u = 0; u < 8; u++) {
             kv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
             vv[u] = kv[u];
-            if (kv_p < npn) {
-                kv[u] = __ldcg(reinterpret_cast<const float4*>(kb + (size_t)(p0n + kv_p) * 128) + dg + 4 * u);
-                vv[u] = __ldcg(reinterpret_cast<const float4*>(vb + (size_t)(p0n + kv_p) * 128) + dg + 4 * u);
-            }
+            if (kv_p < npn) kv[u] = __ldcg(reinterpret_cast<const float4*>(kb + (size_t)(p0n + kv_p) * 128) + dg + 4 * u);
+            if (v_p + u < npn) vv[u] = __ldcg(reinterpret_cast<const float4*>(vb + (size_t)(p0n + v_p + u) * 128 + v_d));
         }
     };
     if (c_begin * PC <= last) load_kv(c_begin * PC);
@@ -910,16 +911,26 @@ attention_tc(const float* Q, float* att, const float* Kc, const float* Vc, int n
             break;
         }
         {
-            // K goes out as 8-byte row pieces, V^T as single elements (dims x positions)
-            const int p = kv_p;
+            // K goes out as 8-byte row pieces; V^T (dims x positions) as one 16-byte chunk per dim
 #pragma unroll
             for (int u = 0; u < 8; u++) {
                 const int d0 = 4 * (dg + 4 * u);
-                ta_split4(sm + TA_K + (d0 >> 6) * 8192, sm + TA_KLO + (d0 >> 6) * 8192, ta_sw128(p, d0 & 63), kv[u]);
-                ta_split(sm + TA_V, sm + TA_VLO, ta_sw128(d0, p), vv[u].x);
-                ta_split(sm + TA_V, sm + TA_VLO, ta_sw128(d0 + 1, p), vv[u].y);
-                ta_split(sm + TA_V, sm + TA_VLO, ta_sw128(d0 + 2, p), vv[u].z);
-                ta_split(sm + TA_V, sm + TA_VLO, ta_sw128(d0 + 3, p), vv[u].w);
+                ta_split4(sm + TA_K + (d0 >> 6) * 8192, sm + TA_KLO + (d0 >> 6) * 8192, ta_sw128(kv_p, d0 & 63), kv[u]);
+            }
+            {
+                float e[8];
+#pragma unroll
+                for (int u = 0; u < 8; u++) e[u] = vv[u].x;
+                ta_split8(sm + TA_V, sm + TA_VLO, ta_sw128(v_d, v_p), e);
+#pragma unroll
+                for (int u = 0; u < 8; u++) e[u] = vv[u].y;
+                ta_split8(sm + TA_V, sm + TA_VLO, ta_sw128(v_d + 1, v_p), e);
+#pragma unroll
+                for (int u = 0; u < 8; u++) e[u] = vv[u].z;
+                ta_split8(sm + TA_V, sm + TA_VLO, ta_sw128(v_d + 2, v_p), e);
+#pragma unroll
+                for (int u = 0; u < 8; u++) e[u] = vv[u].w;
+                ta_split8(sm + TA_V, sm + TA_VLO, ta_sw128(v_d + 3, v_p), e);
             }
         }
         fence_proxy_async_smem();
