@@ -87,7 +87,8 @@ int qw_forward(qw_model* model, qw_cache* cache, uint32_t token, size_t pos, flo
  * positions start_pos .. start_pos+n-1 whose projections run as tcgen05 tensor-core GEMMs over all
  * n tokens. Writes their K/V into the cache exactly where n forward calls would; with logits_out
  * (host, n * vocab_size floats, row t = position start_pos + t) also every position's logits.
- * Synchronous. A page-locked logits_out (cudaHostAlloc, cudaHostRegister, a pinned torch tensor) is
+ * Synchronous. logits_out must be host memory (a device pointer is refused with QW_ERR_ARG before
+ * any work). A page-locked logits_out (cudaHostAlloc, cudaHostRegister, a pinned torch tensor) is
  * filled by one DMA; pageable memory of 32 MB or more goes through two 16 MB pinned stages that the
  * model allocates on first use and up to 8 host threads copy out (311 MB for 512 positions: 8.6 ms
  * page-locked, 9.9 ms into pageable memory written before, 18 ms into a new array). */

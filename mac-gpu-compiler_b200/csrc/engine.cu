@@ -873,8 +873,8 @@ namespace {
 
 // Device -> caller host memory for large results (the prefill's per-position logits, 311 MB for
 // 512 positions of a 151,936-token vocabulary), enqueued on the model's stream after the work that
-// produces them; returns once the data is in `dst`. A page-locked destination takes one DMA.
-// A pageable one goes through two pinned stages of OUT_STAGE bytes: the DMA into one stage runs
+// produces them; returns once the data is in `dst`. A page-locked (or managed) destination takes
+// one DMA; device memory is refused (QW_ERR_ARG). A pageable one goes through two pinned stages of OUT_STAGE bytes: the DMA into one stage runs
 // while host threads copy the other out to the caller's pages, and those threads also take the
 // page faults of freshly allocated memory in parallel. (One pageable cudaMemcpy of 311 MB measured
 // 18 ms into memory touched before and 65 ms into fresh pages on the B200 hosts, against 6 ms for
@@ -885,8 +885,9 @@ int copy_to_host(qw_model* m, void* dst, const void* src, size_t bytes) {
     cudaPointerAttributes at{};
     const cudaError_t pe = cudaPointerGetAttributes(&at, dst);
     if (pe != cudaSuccess) cudaGetLastError();  // not known to CUDA: treated as pageable
-    const bool pinned = pe == cudaSuccess && at.type == cudaMemoryTypeHost;
-    if (pinned || bytes < 2 * OUT_STAGE) {
+    if (pe == cudaSuccess && at.type == cudaMemoryTypeDevice) return set_err(QW_ERR_ARG, "copy-out to device memory");
+    const bool direct = pe == cudaSuccess && (at.type == cudaMemoryTypeHost || at.type == cudaMemoryTypeManaged);
+    if (direct || bytes < 2 * OUT_STAGE) {
         QW_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, m->stream));
         QW_CUDA(cudaStreamSynchronize(m->stream));
         return QW_OK;
@@ -918,17 +919,25 @@ int copy_to_host(qw_model* m, void* dst, const void* src, size_t bytes) {
         std::memcpy(static_cast<uint8_t*>(dst) + k * OUT_STAGE + a, m->h_out_stage + (k & 1) * OUT_STAGE + a, b - a);
     };
     std::vector<std::thread> helpers;
-    for (int t = 1; t < nthr; t++)
-        helpers.emplace_back([&, t] {
-            for (size_t k = 0; k < nch; k++) {
-                while (ready.load(std::memory_order_acquire) < (long long)k) {
-                    if (quit.load(std::memory_order_relaxed)) return;
-                    std::this_thread::yield();
+    try {
+        for (int t = 1; t < nthr; t++)
+            helpers.emplace_back([&, t] {
+                for (size_t k = 0; k < nch; k++) {
+                    while (ready.load(std::memory_order_acquire) < (long long)k) {
+                        if (quit.load(std::memory_order_relaxed)) return;
+                        std::this_thread::yield();
+                    }
+                    copy_slice(k, t);
+                    finished.fetch_add(1, std::memory_order_acq_rel);
                 }
-                copy_slice(k, t);
-                finished.fetch_add(1, std::memory_order_acq_rel);
-            }
-        });
+            });
+    } catch (...) {  // no threads to be had: stop those started, then one pageable copy
+        quit.store(true);
+        for (auto& h : helpers) h.join();
+        QW_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, m->stream));
+        QW_CUDA(cudaStreamSynchronize(m->stream));
+        return QW_OK;
+    }
     int rc = QW_OK;
     for (size_t k = 0; k < std::min<size_t>(2, nch) && rc == QW_OK; k++) rc = enqueue(k);
     for (size_t k = 0; k < nch && rc == QW_OK; k++) {
@@ -956,6 +965,13 @@ int qw_prefill(qw_model* m, qw_cache* c, const uint32_t* ids, size_t n, size_t s
     for (size_t i = 0; i < n; i++)
         if (ids[i] >= m->cfg.vocab) return set_err(QW_ERR_ARG, "token id >= vocab_size");
     QW_CUDA(cudaSetDevice(m->device));
+    if (logits_out) {  // host memory only (the _device call takes device buffers); refused before any work
+        cudaPointerAttributes at{};
+        const cudaError_t pe = cudaPointerGetAttributes(&at, logits_out);
+        if (pe != cudaSuccess) cudaGetLastError();
+        else if (at.type == cudaMemoryTypeDevice)
+            return set_err(QW_ERR_ARG, "logits_out is device memory: qw_prefill writes host memory (qw_prefill_device takes device buffers)");
+    }
     if (int e = ensure_prefill(m, n, start_pos, logits_out != nullptr)) return e;
     int* ew = qw::device_err_word_for(m->device);
     if (!ew) return set_err(QW_ERR_NOMEM, "error word allocation failed");

@@ -88,6 +88,10 @@ def test_prefill_argument_errors(tiny_model_path):
     with pytest.raises(ci.QwError) as e:
         m.prefill([1, m.config.vocab_size], 0, cache)   # token id out of range
     assert e.value.code == ci.QW_ERR_ARG
+    # a device buffer as qw_prefill's host logits: refused before any work (qw_prefill_device takes those)
+    ids = np.array([1, 2, 3], np.uint32)
+    d_lg = torch.empty((3, m.config.vocab_size), dtype=torch.float32, device="cuda:0")
+    assert ci.lib().qw_prefill(m._h, cache._h, ids.ctypes.data, 3, 0, d_lg.data_ptr()) == ci.QW_ERR_ARG
 
 
 def test_prefill_device_bad_id_is_reported(tiny_model_path):
