@@ -897,8 +897,9 @@ int copy_to_host(qw_model* m, void* dst, const void* src, size_t bytes) {
             m->h_out_stage = nullptr;
             return set_err(QW_ERR_NOMEM, "pinned staging allocation failed");
         }
-        for (cudaEvent_t& e : m->out_ev) QW_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     }
+    for (cudaEvent_t& e : m->out_ev)
+        if (!e) QW_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     const size_t nch = (bytes + OUT_STAGE - 1) / OUT_STAGE;
     auto chunk_len = [&](size_t k) { return std::min(OUT_STAGE, bytes - k * OUT_STAGE); };
     auto enqueue = [&](size_t k) -> int {
